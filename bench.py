@@ -1,0 +1,509 @@
+"""Benchmark of the B200 paged-KV decode path (tiny-vLLM Llama-3.2-1B geometry).
+
+Workload (per GPU; weak scaling, requests sharded across GPUs, no collective on
+the data path): decode_sweep — 256 rows with attended lengths L ~ U[512, 8192]
+(seed 4), 16 layers, 32 Q / 8 KV heads, head_dim 64, BF16 N(0, 1) K/V in
+16-token pages scattered over a pool sized to fit.  One step = one decode step
+of the hot path over all 16 layers: the plan, then per layer the fused
+RoPE(q, k) + paged append of the new token and the fused GQA decode attention.
+
+Metric: paged-decode KV GB/s = K+V bytes attended (sum_L * 2 KiB per layer) per
+second, whole job; also decode tok/s and the fraction of measured HBM peak.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`--impl reference` times the reference algorithm's CPU restatement (the
+reference has no CPU implementation of this path) on all host cores, on a
+bounded sample of the same workload, and prints the same JSON line shape.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT), str(ROOT / "tests")]
+
+import workloads as W  # noqa: E402
+
+METRIC = "paged-decode KV GB/s"
+UNIT = "GB/s"
+PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_HBM_GBS = 6650.0
+TRAFFIC_FILE = ROOT / "profiles" / "paged_decode_kernel.decode_sweep.json"
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def hbm_peak():
+    try:
+        peaks = json.loads(PEAKS_FILE.read_text())
+        return float(peaks["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def algorithmic_bytes(lens: np.ndarray) -> dict:
+    """Bytes one decode-attention launch must move (one layer)."""
+    lens = lens.astype(np.int64)
+    kv = int(lens.sum()) * W.KV_DIM * 2 * 2          # K and V, 1 KiB each per token
+    qo = int(lens.size) * W.Q_DIM * 2 * 2             # q in, out
+    tables = int(((lens + 15) // 16).sum()) * 4
+    return {"kv": kv, "q_out": qo, "tables": tables, "total": kv + qo + tables}
+
+
+def config_block(world, batch):
+    return {
+        "workload": "decode_sweep",
+        "rows_per_gpu": batch,
+        "global_rows": batch * world,
+        "seq_len": "L ~ U[512, 8192] (seed 4)",
+        "layers": 16,
+        "q_heads": 32,
+        "kv_heads": 8,
+        "head_dim": 64,
+        "page_tokens": 16,
+        "parallelism": f"request-sharded x{world} (no collective)",
+        "l2": "inputs larger than L2 (>=2.2 GB of K+V per layer launch)",
+    }
+
+
+# --------------------------------------------------------------- CPU legs ---
+def cpu_sample_case(rows: int, seed: int = 4):
+    lens = W.sweep_lengths(seed)[:rows]
+    return W.decode_random(seed + 7, lens, slack_pages=0)
+
+
+def time_cpu(rows: int, budget_s: float, threads: int = 0):
+    """Times the oracle (reference semantics, OpenMP) on the first `rows` rows
+    of the workload, one layer, repeated until `budget_s` elapsed."""
+    import oracle
+    case = cpu_sample_case(rows)
+    cores = threads if threads > 0 else oracle.max_threads()
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        oracle.decode_attention(case.q, case.k_pool, case.v_pool, 0, case.tables, case.lens,
+                                threads=cores)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    kv = algorithmic_bytes(case.lens)["kv"]
+    gbs = kv * reps / el / 1e9
+    return {"value": round(gbs, 3), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": (f"{rows} rows of decode_sweep (sum L = {int(case.lens.sum())}), 1 layer, "
+                       f"{reps} repetitions in {el:.1f} s; oracle/tvp_oracle.c (reference "
+                       "rounding points, FP32), OpenMP")}, el
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    rows = 32
+    samples = []
+    for _ in range(args.warmup):
+        time_cpu(rows, 0.5)
+    for _ in range(args.steps):
+        cb, el = time_cpu(rows, args.cpu_seconds / max(args.steps, 1))
+        samples.append(cb["value"])
+    value = statistics.median(samples)
+    cb["value"] = round(value, 3)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": config_block(world, 256), "cpu_baseline": cb,
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- clocks ---
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "200"], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags)
+                          if f.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows),
+                "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ------------------------------------------------------------- our arm ---
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from vllm_b200 import _native as N
+    from vllm_b200 import ops
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    case = W.decode_sweep(seed=4, batch=args.rows)
+    B, P, layers = case.batch, case.num_pages, case.num_layers
+    lens = case.lens
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    shape = (layers, P, 16, W.KV_DIM)
+    k_pool = torch.empty(shape, dtype=torch.bfloat16, device=dev)
+    v_pool = torch.empty(shape, dtype=torch.bfloat16, device=dev)
+    for l in range(layers):
+        k_pool[l].normal_(generator=gen)
+        v_pool[l].normal_(generator=gen)
+    tables = torch.from_numpy(case.tables).to(dev)
+    seq_lens = torch.from_numpy(lens).to(dev)
+    positions = seq_lens - 1
+    q_all = torch.randn((layers, B, W.Q_DIM), generator=gen, device=dev).to(torch.bfloat16)
+    k_new = torch.randn((layers, B, W.KV_DIM), generator=gen, device=dev).to(torch.bfloat16)
+    v_new = torch.randn((layers, B, W.KV_DIM), generator=gen, device=dev).to(torch.bfloat16)
+    out = torch.empty((layers, B, W.Q_DIM), dtype=torch.bfloat16, device=dev)
+    err = ops.new_error_word(dev)
+    ws = ops.DecodeWorkspace(B, dev)
+    stream = torch.cuda.current_stream(dev)
+    stride = case.tables.shape[1]
+
+    def step(events=None):
+        ops.decode_plan(seq_lens, stride, ws, error=err, stream=stream)
+        for l in range(layers):
+            ops.rope_append(k_pool, v_pool, l, tables, positions, k_new[l], v_new[l], q=q_all[l],
+                            writeback_k=False, error=err, stream=stream)
+            if events is not None:
+                events[l][0].record(stream)
+            ops.paged_decode_attention(q_all[l], k_pool, v_pool, l, tables, seq_lens, ws,
+                                       out=out[l], error=err, stream=stream)
+            if events is not None:
+                events[l][1].record(stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    assert int(err.item()) == 0, f"device error bits {int(err.item())}"
+
+    # ---- device-resident timing ----
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(layers)]
+          for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local_rank)
+    barrier()
+    torch.cuda.synchronize(dev)
+    clocks.start()
+    t0.record(stream)
+    for s in range(args.steps):
+        step(ev[s])
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clock_info = clocks.stop()
+    ms_total = max_over_ranks(t0.elapsed_time(t1))
+    launch_ms = [e[0].elapsed_time(e[1]) for s in ev for e in s]
+    attn_ms = statistics.mean(launch_ms)
+    ms_per_step = ms_total / args.steps
+    nbytes = algorithmic_bytes(lens)
+    kv_step = nbytes["kv"] * layers
+    value = kv_step * world / (ms_per_step / 1e3) / 1e9
+    tok_s = B * world / (ms_per_step / 1e3)
+
+    # ---- end to end through the C-ABI with host buffers ----
+    q_h = q_all.cpu().pin_memory()
+    k_h = k_new.cpu().pin_memory()
+    v_h = v_new.cpu().pin_memory()
+    out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    q_d, k_d, v_d = torch.empty_like(q_all), torch.empty_like(k_new), torch.empty_like(v_new)
+
+    def e2e_step():
+        q_d.copy_(q_h, non_blocking=True)
+        k_d.copy_(k_h, non_blocking=True)
+        v_d.copy_(v_h, non_blocking=True)
+        ops.decode_plan(seq_lens, stride, ws, error=err, stream=stream)
+        for l in range(layers):
+            ops.rope_append(k_pool, v_pool, l, tables, positions, k_d[l], v_d[l], q=q_d[l],
+                            writeback_k=False, error=err, stream=stream)
+            ops.paged_decode_attention(q_d[l], k_pool, v_pool, l, tables, seq_lens, ws,
+                                       out=out[l], error=err, stream=stream)
+        out_h.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    h2d = (q_h.numel() + k_h.numel() + v_h.numel()) * 2
+    d2h = out_h.numel() * 2
+    e2e_value = kv_step * world / (e2e_ms / 1e3) / 1e9
+    assert int(err.item()) == 0, f"device error bits {int(err.item())}"
+
+    if rank != 0:
+        return
+    peak, peak_kind = hbm_peak()
+    achieved = nbytes["total"] / (attn_ms / 1e3) / 1e9
+    traffic = None
+    try:
+        prof = json.loads(TRAFFIC_FILE.read_text())
+        traffic = int(prof["dram_bytes_per_kv_byte"] * nbytes["kv"])
+    except Exception:
+        traffic = None
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) BF16 K/V/q, seeded lengths and page scatter)",
+        "config": config_block(world, B),
+        "decode_tok_s": round(tok_s, 1),
+        "hbm_peak_frac": round(value / world / peak, 4),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "kernel": "tvp::paged_decode_kernel<6,2>",
+                     "algorithmic_bytes_per_launch": nbytes["total"],
+                     "avg_launch_ms": round(attn_ms, 4), "peak_source": f"{peak_kind} hbm_gbs"},
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": args.steps * (1 + 2 * layers),
+        "clocks": clock_info,
+    }
+    if world == 1 and not args.no_extras:
+        line.update(extras(args, dev, case, k_pool, v_pool, q_all, out, tables, seq_lens, ws))
+    if world == 1 and not args.no_cpu_baseline:
+        cb, _ = time_cpu(32, args.cpu_seconds)
+        line["cpu_baseline"] = cb
+    print(json.dumps(line), flush=True)
+
+
+def extras(args, dev, case, k_pool, v_pool, q_all, out, tables, seq_lens, ws):
+    """Spot parity at full size, the long-context workload and the reference's
+    gather+cuBLAS path on decode_small (when its build is present)."""
+    import torch
+    import oracle
+    from vllm_b200 import ops
+    res = {}
+    # parity spot check: 3 rows of layer 5 against exact attention
+    rows = [0, int(np.argmax(case.lens)), int(np.argmin(case.lens))]
+    layer = 5
+    torch.cuda.synchronize(dev)
+    ops.decode_plan(seq_lens, case.tables.shape[1], ws)
+    ops.paged_decode_attention(q_all[layer], k_pool, v_pool, layer, tables, seq_lens, ws,
+                               out=out[layer])
+    torch.cuda.synchronize(dev)
+    worst = 0.0
+    for r in rows:
+        L = int(case.lens[r])
+        pages = case.tables[r, :(L + 15) // 16]
+        kp = k_pool[layer][torch.from_numpy(pages).to(dev).long()]
+        vpp = v_pool[layer][torch.from_numpy(pages).to(dev).long()]
+        h = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+        kp_h, vp_h = h(kp)[None], h(vpp)[None]
+        tab = np.arange(pages.size, dtype=np.int32)[None]
+        exact = oracle.decode_attention_f64(h(q_all[layer][r:r + 1]), kp_h, vp_h, 0, tab,
+                                            np.array([L], np.int32))
+        got = W.bf16_to_f32(h(out[layer][r:r + 1])).astype(np.float64)
+        worst = max(worst, float(np.abs(got - exact).max()))
+    res["parity_spot_check"] = {"rows": rows, "layer": layer, "max_abs_err_vs_exact": worst,
+                                "tolerance": "1e-2 abs + 2e-2 rel"}
+    res["long_context"] = bench_long_context(dev)
+    res["decode_small"] = bench_decode_small(dev)
+    return res
+
+
+def bench_long_context(dev, iters=20):
+    import torch
+    from vllm_b200 import ops
+    case = W.long_context(seed=5, batch=16, L=32768, num_layers=1)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(99)
+    shape = (1, case.num_pages, 16, W.KV_DIM)
+    kp = torch.empty(shape, dtype=torch.bfloat16, device=dev).normal_(generator=gen)
+    vp = torch.empty(shape, dtype=torch.bfloat16, device=dev).normal_(generator=gen)
+    q = torch.randn((16, W.Q_DIM), generator=gen, device=dev).to(torch.bfloat16)
+    tables = torch.from_numpy(case.tables).to(dev)
+    lens = torch.from_numpy(case.lens).to(dev)
+    ws = ops.DecodeWorkspace(16, dev)
+    ops.decode_plan(lens, case.tables.shape[1], ws)
+    out = torch.empty_like(q)
+    for _ in range(3):
+        ops.paged_decode_attention(q, kp, vp, 0, tables, lens, ws, out=out)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(iters)]
+    torch.cuda.synchronize(dev)
+    for a, b in ev:
+        a.record()
+        ops.paged_decode_attention(q, kp, vp, 0, tables, lens, ws, out=out)
+        b.record()
+    torch.cuda.synchronize(dev)
+    ms = statistics.median(a.elapsed_time(b) for a, b in ev)
+    nb = algorithmic_bytes(case.lens)
+    peak, kind = hbm_peak()
+    gbs = nb["total"] / (ms / 1e3) / 1e9
+    del kp, vp
+    torch.cuda.empty_cache()
+    return {"workload": "long_context 16 x 32768, 1 layer, split-K", "us_per_launch": round(ms * 1e3, 2),
+            "GBps": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4), "peak_source": kind,
+            "inputs": "larger than L2 (1.07 GB per launch)"}
+
+
+def bench_decode_small(dev, iters=50):
+    """decode_small (4 rows, L = 17..256): our fused launch vs the reference's
+    gather + cuBLAS + softmax sequence, both with L2 flushed between launches."""
+    import ctypes
+    import torch
+    import oracle
+    from vllm_b200 import ops
+    case = W.decode_small()
+    to = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).to(dev).view(torch.bfloat16)
+    k, v, q = to(case.k_pool), to(case.v_pool), to(case.q)
+    tables = torch.from_numpy(case.tables).to(dev)
+    lens = torch.from_numpy(case.lens).to(dev)
+    ws = ops.DecodeWorkspace(4, dev)
+    out = torch.empty_like(q)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    times = []
+    for i in range(iters + 3):
+        flush.fill_(i & 0xFF)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        ops.decode_plan(lens, case.tables.shape[1], ws)
+        ops.paged_decode_attention(q, k, v, 0, tables, lens, ws, out=out)
+        b.record()
+        torch.cuda.synchronize(dev)
+        if i >= 3:
+            times.append(a.elapsed_time(b))
+    ours_us = statistics.median(times) * 1e3
+    res = {"workload": "decode_small 4 rows L={17,64,129,256}, 1 layer, L2 flushed",
+           "ours_us_plan_plus_attention": round(ours_us, 2)}
+    ref = oracle.load_reference()
+    if ref is None:
+        res["reference_gather_cublas_us"] = None
+        res["note"] = "reference build (oracle/_ref) not present"
+        return res
+    ref_out = torch.empty_like(q)
+    tab = np.ascontiguousarray(case.tables, np.int32)
+    ln = np.ascontiguousarray(case.lens, np.int32)
+    ms = ctypes.c_float(0.0)
+    rc = ref.ref_paged_decode(ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(k.data_ptr()),
+                              ctypes.c_void_p(v.data_ptr()), case.num_pages, 0,
+                              tab.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), tab.shape[1],
+                              ln.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), 4,
+                              ctypes.c_void_p(ref_out.data_ptr()), iters, 256 << 20,
+                              ctypes.byref(ms))
+    if rc != 0:
+        res["reference_gather_cublas_us"] = None
+        res["note"] = f"reference path returned {rc}"
+        return res
+    ref_us = ms.value * 1e3
+    res["reference_gather_cublas_us"] = round(ref_us, 2)
+    res["speedup_vs_reference"] = round(ref_us / ours_us, 2)
+    kv = algorithmic_bytes(case.lens)["kv"]
+    res["reference_kv_GBps"] = round(kv / (ref_us / 1e6) / 1e9, 3)
+    res["ours_kv_GBps"] = round(kv / (ours_us / 1e6) / 1e9, 3)
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--rows", type=int, default=256)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local_rank = env_int("LOCAL_RANK", 0)
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,215 @@
+/*
+ * tvp_paged.h — C-ABI of the B200 paged-KV hot path for the tiny-vLLM
+ * Llama-3.2-1B engine (arpitsri28/vllm).
+ *
+ * Plain pointers and sizes only: no C++ types, no torch types.  Every entry
+ * point returns 0 (TVP_OK) on success and a negative TVP_ERR_* code on
+ * failure; nothing throws across this boundary.  The C++ host layer
+ * (tvp_paged.hpp, namespace tvp) maps the codes back onto the reference's
+ * exception types: TVP_ERR_INVALID_ARGUMENT -> std::invalid_argument,
+ * everything else -> std::runtime_error.
+ *
+ * Geometry is the reference's hard-coded one (src/model/paged_kvcache.cu:10-11,
+ * src/model/paged_attention.cu:10-12, src/model/RoPe.cu:7):
+ *   head_dim 64, 16-token pages, 4 query heads per KV head (GQA),
+ *   8 KV heads x 64 = 512 channels per cached token, 32 query heads.
+ *
+ * Pool layout (identical to the reference, src/model/paged_kvcache.cu:160):
+ *   element (layer, page, slot, kv_head, d) of the K (or V) pool lives at
+ *   ((layer * num_pages + page) * 16 + slot) * (kv_heads * 64) + kv_head * 64 + d
+ * so a page of one layer is kv_heads * 2 KiB of contiguous BF16 per pool.
+ *
+ * "Device pointer" arguments (prefixed d_ or documented as such) must be CUDA
+ * device memory of the current device.  "stream" is a cudaStream_t (NULL =
+ * legacy default stream, as in the reference).  Kernels that detect a bad page
+ * id, length or a stalled pipeline do not trap: they OR a TVP_DEVERR_* bit into
+ * *d_error (optional, may be NULL) and skip the offending access.
+ */
+#ifndef TVP_PAGED_H
+#define TVP_PAGED_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef uint16_t tvp_bf16;   /* raw IEEE bfloat16 bits */
+typedef void* tvp_stream_t;  /* cudaStream_t */
+
+/* ---- return codes ----------------------------------------------------- */
+#define TVP_OK 0
+#define TVP_ERR_INVALID_ARGUMENT (-1) /* reference: std::invalid_argument          */
+#define TVP_ERR_RUNTIME (-2)          /* reference: std::runtime_error (CUDA error)  */
+#define TVP_ERR_NO_FREE_BLOCKS (-3)   /* reference: runtime_error, pool exhausted    */
+#define TVP_ERR_UNSUPPORTED (-4)      /* geometry/mode this build does not provide   */
+#define TVP_ERR_WORKSPACE (-5)        /* workspace missing or too small             */
+
+/* ---- device error bits (written into *d_error by kernels) -------------- */
+#define TVP_DEVERR_BAD_PAGE 1u     /* block-table entry outside [0, num_pages)   */
+#define TVP_DEVERR_BAD_LENGTH 2u   /* sequence length < 0 or beyond its table    */
+#define TVP_DEVERR_TIMEOUT 4u      /* a pipeline wait ran out its bound          */
+#define TVP_DEVERR_BAD_PLAN 8u     /* workspace planned for another batch/grid   */
+#define TVP_DEVERR_BAD_TOKEN 16u   /* append: token's sequence row or position invalid */
+
+/* ---- fixed geometry ---------------------------------------------------- */
+#define TVP_HEAD_DIM 64
+#define TVP_PAGE_TOKENS 16
+#define TVP_GQA_GROUP 4
+#define TVP_KV_HEADS 8
+#define TVP_Q_HEADS 32
+
+/* ---- decode attention numerics ----------------------------------------- */
+/* FAST: one pass, FP32 online softmax (base-2 exponent), BF16 probabilities
+ * into the P.V product, FP32 accumulation, BF16 output. */
+#define TVP_MODE_FAST 0
+/* COMPAT: the reference's rounding points (src/model/attention.cu:53-142,
+ * src/model/softmax.cu:6-45): BF16 scores, exact max, expf, pairwise-tree sum,
+ * BF16 probabilities, FP32 P.V, BF16 output.  Lengths up to 4096. */
+#define TVP_MODE_COMPAT 1
+
+/* ---- flags of tvp_rope_append ------------------------------------------ */
+#define TVP_APPEND_ROPE_K 1     /* apply llama3 RoPE to K before it is stored      */
+#define TVP_APPEND_ROPE_Q 2     /* apply llama3 RoPE to q in place                  */
+#define TVP_APPEND_WRITEBACK_K 4 /* also write the (RoPE'd) K back into k          */
+
+const char* tvp_strerror(int code);
+int tvp_version(void);
+
+/* Number of SMs of the current device (the default decode grid size). */
+int tvp_device_sm_count(int* out_sms);
+
+/*
+ * K1 — fused llama3 RoPE + paged KV append.
+ *
+ * Replaces, in one launch:
+ *   rope(k)/ropeBatch(k)                 src/model/RoPe.cu:31-62 (K, in place)
+ *   rope(q)/ropeBatch(q)                 src/model/RoPe.cu:31-62 (q, in place; optional)
+ *   storePagedKV                         src/model/paged_kvcache.cu:147-166 (prefill)
+ *   storePagedKVBatch / ...Kernel        src/model/paged_attention.cu:89-99,123-131 (decode)
+ *
+ * Token i (0 <= i < num_tokens) belongs to block-table row
+ *   seq = d_token_seq ? d_token_seq[i] : i
+ * and absolute position pos = d_token_pos[i]; it is written to slot pos % 16
+ * of physical page d_block_tables[seq * table_stride + pos / 16].
+ * k, v: [num_tokens][kv_heads * 64] BF16 (device).  q: [num_tokens][q_heads * 64]
+ * (device, only with TVP_APPEND_ROPE_Q).  RoPE arithmetic is the reference
+ * ropeKernel's, bit for bit.  Does not advance any sequence length.
+ */
+int tvp_rope_append(tvp_bf16* k_pool, tvp_bf16* v_pool, int num_pages, int num_layers,
+                    int layer, int kv_heads, const int32_t* d_block_tables, int table_stride,
+                    int num_seqs, const int32_t* d_token_seq, const int32_t* d_token_pos,
+                    int num_tokens, tvp_bf16* k, const tvp_bf16* v, tvp_bf16* q, int q_heads,
+                    int flags, int32_t* d_error, tvp_stream_t stream);
+
+/*
+ * Workspace of the decode path: plan header, per-sequence page prefix sums,
+ * last-arriver counters and split-K partials for `num_ctas` CTAs (0 = one per SM).
+ */
+size_t tvp_decode_workspace_bytes(int batch, int kv_heads, int num_ctas);
+
+/*
+ * Per-step plan (the device side of preparePagedBatch,
+ * src/model/paged_attention.cu:30-87): page prefix sums over d_seq_lens and a
+ * reset of the split-K counters.  One plan serves every layer of a decode step.
+ * d_seq_lens[b] = attended length L (= current_seq_len + 1 after the append).
+ */
+int tvp_decode_plan(const int32_t* d_seq_lens, int batch, int table_stride, int kv_heads,
+                    int num_ctas, void* d_workspace, size_t workspace_bytes, int32_t* d_error,
+                    tvp_stream_t stream);
+
+/*
+ * K2 — fused GQA paged decode attention (+ split-K combine).
+ *
+ * Replaces src/model/paged_transformer.cu:85-94:
+ *   computePagedAttentionScores (gather + 32*B cuBLAS GEMVs)  src/model/paged_attention.cu:133-146
+ *   softmaxRows per (row, head)                               src/model/softmax.cu:47-72
+ *   pagedAttentionScoresTimesV (gather + 32*B cuBLAS GEMVs)   src/model/paged_attention.cu:148-161
+ * q:   [batch][q_heads * 64] BF16, already RoPE'd.
+ * out: [batch][q_heads * 64] BF16, head-major (head h at h*64), as the reference.
+ * out[b, h] = softmax(scale * q[b,h] . K[b, kv(h)]^T) . V[b, kv(h)] over the
+ * first d_seq_lens[b] tokens of row b's pages, kv(h) = h / 4.
+ * Pages are read in place.  The workspace must hold a plan made by
+ * tvp_decode_plan with the same d_seq_lens contents, batch and num_ctas.
+ */
+int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const tvp_bf16* v_pool,
+                               int num_pages, int num_layers, int layer, int kv_heads, int q_heads,
+                               const int32_t* d_block_tables, int table_stride,
+                               const int32_t* d_seq_lens, int batch, float scale, int mode,
+                               int num_ctas, void* d_workspace, size_t workspace_bytes,
+                               tvp_bf16* out, int32_t* d_error, tvp_stream_t stream);
+
+/* ======================================================================= *
+ * Host API mirror: PagedKVCache / SequenceKVState / PagedBatchMetadata.
+ * Same allocator semantics as src/model/paged_kvcache.cu:65-145 (LIFO free
+ * list seeded descending, lazy ceil(L/16) pages, exhaustion checked before
+ * mutation, O(n) double-free rejection), with the 1024-token context cap
+ * made a per-cache parameter (max_seq_len, 1024 reproduces the reference).
+ * ======================================================================= */
+typedef struct tvp_cache tvp_cache; /* PagedKVCache  (include/paged_kvcache.cuh:8-14) */
+typedef struct tvp_seq tvp_seq;     /* SequenceKVState (include/paged_kvcache.cuh:16-19) */
+typedef struct tvp_batch tvp_batch; /* PagedBatchMetadata (include/paged_attention.cuh:6-15) */
+
+/* allocatePagedKVCache (src/model/paged_kvcache.cu:65-90).  device_storage=0
+ * builds the allocator only (no pools), for host-side tests. */
+int tvp_cache_create(int num_blocks, int num_layers, int kv_heads, int max_seq_len,
+                     int device_storage, tvp_cache** out);
+/* freePagedKVCache (src/model/paged_kvcache.cu:92-98). */
+void tvp_cache_destroy(tvp_cache* cache);
+int tvp_cache_pools(const tvp_cache* cache, tvp_bf16** k_pool, tvp_bf16** v_pool,
+                    int* num_blocks);
+int tvp_cache_free_count(const tvp_cache* cache);
+/* Copies the free list (bottom..top of the LIFO stack); returns its length. */
+int tvp_cache_free_list(const tvp_cache* cache, int32_t* out, int capacity);
+/* Overwrites the free list (bottom..top); for seeded shuffled pools. */
+int tvp_cache_set_free_list(tvp_cache* cache, const int32_t* blocks, int count);
+/* allocatePhysicalBlock (src/model/paged_kvcache.cu:100-108). */
+int tvp_allocate_physical_block(tvp_cache* cache, int* out_block);
+/* freePhysicalBlock (src/model/paged_kvcache.cu:110-117). */
+int tvp_free_physical_block(tvp_cache* cache, int block);
+
+int tvp_seq_create(tvp_seq** out);
+void tvp_seq_destroy(tvp_seq* seq);
+int tvp_seq_length(const tvp_seq* seq);
+int tvp_seq_set_length(tvp_seq* seq, int current_seq_len);
+/* Copies the block table; returns its length. */
+int tvp_seq_block_table(const tvp_seq* seq, int32_t* out, int capacity);
+/* reserveSequenceBlocks (src/model/paged_kvcache.cu:128-145). */
+int tvp_reserve_sequence_blocks(tvp_cache* cache, tvp_seq* seq, int total_seq_len);
+/* freeSequenceBlocks (src/model/paged_kvcache.cu:119-126). */
+int tvp_free_sequence_blocks(tvp_cache* cache, tvp_seq* seq);
+
+/* storePagedKV (src/model/paged_kvcache.cu:147-166): reserve + append
+ * num_tokens rows of k, v (device) at current_seq_len.. through K1; with
+ * rope_q non-NULL the fused form also applies RoPE to k (in place) and q,
+ * replacing rope(q), rope(k), storePagedKV of src/model/paged_transformer.cu:34-36. */
+int tvp_store_paged_kv(tvp_cache* cache, tvp_seq* seq, int layer, tvp_bf16* k,
+                       const tvp_bf16* v, int num_tokens, int apply_rope, tvp_bf16* rope_q,
+                       tvp_stream_t stream);
+
+/* PagedBatchMetadata with persistent device tables (no per-step malloc). */
+int tvp_batch_create(int max_batch, int max_pages_per_seq, tvp_batch** out);
+void tvp_batch_destroy(tvp_batch* batch);
+/* preparePagedBatch (src/model/paged_attention.cu:30-87): validates the rows,
+ * reserves the page of the new token, uploads tables / positions / lengths and
+ * plans the decode grid. */
+int tvp_prepare_paged_batch(tvp_cache* cache, tvp_seq* const* seqs, int count, tvp_batch* batch,
+                            tvp_stream_t stream);
+int tvp_batch_positions(const tvp_batch* batch, const int32_t** d_positions,
+                        const int32_t** d_lengths, const int32_t** d_tables, int* table_stride);
+/* ropeBatch(q) + ropeBatch(k) + storePagedKVBatch (src/model/paged_transformer.cu:80-84). */
+int tvp_store_paged_kv_batch(tvp_cache* cache, const tvp_batch* batch, int layer, tvp_bf16* q,
+                             tvp_bf16* k, const tvp_bf16* v, tvp_stream_t stream);
+/* computePagedAttentionScores + softmaxRows + pagedAttentionScoresTimesV
+ * (src/model/paged_transformer.cu:85-94) as one fused launch. */
+int tvp_paged_attention(const tvp_cache* cache, tvp_batch* batch, int layer, const tvp_bf16* q,
+                        tvp_bf16* out, int mode, tvp_stream_t stream);
+/* Device error word of the batch's launches (synchronises the stream). */
+int tvp_batch_error(tvp_batch* batch, tvp_stream_t stream, int32_t* out_bits);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TVP_PAGED_H */

@@ -1,0 +1,171 @@
+// ref_shim.cu — TEST INFRASTRUCTURE ONLY (the checker, never the product).
+//
+// A C entry layer over the reference's OWN hot-path functions, compiled
+// together with the reference sources where they lie (see oracle/Makefile;
+// nothing of the reference is copied here).  It lets the tests and the bench
+// run the unmodified reference path on a B200 as an oracle and as the
+// gather+cuBLAS baseline:
+//   ref_rope / ref_rope_batch   -> rope / ropeBatch         (src/model/RoPe.cu:31-62)
+//   ref_store_paged_kv          -> storePagedKV             (src/model/paged_kvcache.cu:147-166)
+//   ref_paged_decode            -> preparePagedBatch, computePagedAttentionScores,
+//                                  softmaxRows per (row, head), pagedAttentionScoresTimesV,
+//                                  freePagedBatch, in the order of
+//                                  src/model/paged_transformer.cu:65,85-94,135
+// Pools are caller-owned device buffers in the reference layout; the shim
+// wraps them in the reference's PagedKVCache without taking ownership.
+#include <cublas_v2.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <exception>
+#include <stdexcept>
+#include <vector>
+
+#include "attention.cuh"
+#include "paged_attention.cuh"
+#include "paged_kvcache.cuh"
+#include "rope.cuh"
+#include "softmax.cuh"
+
+namespace {
+
+cublasHandle_t cublas() {
+  static cublasHandle_t h = nullptr;
+  if (!h && cublasCreate(&h) != CUBLAS_STATUS_SUCCESS) throw std::runtime_error("cublasCreate");
+  return h;
+}
+
+// A PagedKVCache view of caller-owned pools; every block not named in `used`
+// is on the free list (descending, as allocatePagedKVCache seeds it).
+PagedKVCache wrap_pools(uint16_t* k_pool, uint16_t* v_pool, int num_blocks,
+                        const std::vector<char>& used) {
+  PagedKVCache cache{};
+  cache.k_blocks = reinterpret_cast<__nv_bfloat16*>(k_pool);
+  cache.v_blocks = reinterpret_cast<__nv_bfloat16*>(v_pool);
+  cache.num_blocks = num_blocks;
+  for (int b = num_blocks - 1; b >= 0; --b)
+    if (!used[b]) cache.free_blocks.push_back(b);
+  return cache;
+}
+
+int finish() { return cudaDeviceSynchronize() == cudaSuccess ? 0 : -2; }
+
+}  // namespace
+
+extern "C" {
+
+int ref_rope(uint16_t* x, int tokens, int proj_dim, int position_offset) {
+  rope(reinterpret_cast<__nv_bfloat16*>(x), tokens, proj_dim, position_offset);
+  return finish();
+}
+
+int ref_rope_batch(uint16_t* x, int batch, int proj_dim, const int* d_positions) {
+  try {
+    ropeBatch(reinterpret_cast<__nv_bfloat16*>(x), batch, proj_dim, d_positions);
+  } catch (const std::invalid_argument&) {
+    return -1;
+  } catch (const std::exception&) {
+    return -2;
+  }
+  return finish();
+}
+
+int ref_store_paged_kv(uint16_t* k_pool, uint16_t* v_pool, int num_blocks, int layer,
+                       const int* table, int table_len, int start, const uint16_t* d_k,
+                       const uint16_t* d_v, int num_tokens) {
+  try {
+    std::vector<char> used(num_blocks, 0);
+    for (int i = 0; i < table_len; ++i) {
+      if (table[i] < 0 || table[i] >= num_blocks) return -1;
+      used[table[i]] = 1;
+    }
+    PagedKVCache cache = wrap_pools(k_pool, v_pool, num_blocks, used);
+    SequenceKVState seq{};
+    seq.block_table.assign(table, table + table_len);
+    seq.current_seq_len = start;
+    storePagedKV(cache, seq, layer, reinterpret_cast<const __nv_bfloat16*>(d_k),
+                 reinterpret_cast<const __nv_bfloat16*>(d_v), num_tokens);
+  } catch (const std::invalid_argument&) {
+    return -1;
+  } catch (const std::exception&) {
+    return -2;
+  }
+  return finish();
+}
+
+// tables: host [batch][table_stride]; lens: host attended lengths (L = current_seq_len + 1).
+// When iters > 0, *ms_out receives the mean time of the three-call decode
+// attention sequence per launch set, with `flush_bytes` of a scratch buffer
+// rewritten between iterations (outside the timed interval).
+int ref_paged_decode(const uint16_t* d_q, uint16_t* k_pool, uint16_t* v_pool, int num_blocks,
+                     int layer, const int* tables, int table_stride, const int* lens, int batch,
+                     uint16_t* d_out, int iters, size_t flush_bytes, float* ms_out) {
+  PagedBatchMetadata md{};
+  __nv_bfloat16* scores = nullptr;
+  void* flush = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  int rc = 0;
+  try {
+    std::vector<char> used(num_blocks, 0);
+    std::vector<SequenceKVState> states(batch);
+    std::vector<SequenceKVState*> rows;
+    for (int b = 0; b < batch; ++b) {
+      const int pages = (lens[b] + BLOCK_SIZE - 1) / BLOCK_SIZE;
+      for (int j = 0; j < pages; ++j) {
+        const int blk = tables[b * table_stride + j];
+        if (blk < 0 || blk >= num_blocks || used[blk]) return -1;
+        used[blk] = 1;
+        states[b].block_table.push_back(blk);
+      }
+      states[b].current_seq_len = lens[b] - 1;
+      rows.push_back(&states[b]);
+    }
+    PagedKVCache cache = wrap_pools(k_pool, v_pool, num_blocks, used);
+    preparePagedBatch(cache, rows, md);
+    if (cudaMalloc(&scores, sizeof(__nv_bfloat16) * batch * 32 * md.score_stride) != cudaSuccess)
+      throw std::runtime_error("cudaMalloc scores");
+    cublasHandle_t h = cublas();
+    auto step = [&]() {
+      computePagedAttentionScores(h, reinterpret_cast<const __nv_bfloat16*>(d_q), cache, md, layer,
+                                  scores);
+      for (int row = 0; row < batch; ++row)
+        for (int head = 0; head < 32; ++head)
+          softmaxRows(scores + (row * 32 + head) * md.score_stride, 1, md.lengths[row]);
+      pagedAttentionScoresTimesV(h, scores, cache, md, layer,
+                                 reinterpret_cast<__nv_bfloat16*>(d_out));
+    };
+    step();
+    if (cudaDeviceSynchronize() != cudaSuccess) throw std::runtime_error("decode failed");
+    if (iters > 0 && ms_out) {
+      if (flush_bytes && cudaMalloc(&flush, flush_bytes) != cudaSuccess)
+        throw std::runtime_error("cudaMalloc flush");
+      cudaEventCreate(&e0);
+      cudaEventCreate(&e1);
+      double total = 0.0;
+      for (int i = 0; i < iters; ++i) {
+        if (flush) cudaMemsetAsync(flush, i & 0xff, flush_bytes);
+        cudaEventRecord(e0);
+        step();
+        cudaEventRecord(e1);
+        cudaEventSynchronize(e1);
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        total += ms;
+      }
+      *ms_out = static_cast<float>(total / iters);
+    }
+  } catch (const std::invalid_argument&) {
+    rc = -1;
+  } catch (const std::exception&) {
+    rc = -2;
+  }
+  freePagedBatch(md);
+  cudaFree(scores);
+  cudaFree(flush);
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  if (rc == 0) rc = finish();
+  return rc;
+}
+
+}  // extern "C"

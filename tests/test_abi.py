@@ -1,0 +1,114 @@
+"""The C-ABI library: loads, exports every declared symbol, rejects bad
+arguments on the host before touching the device (no GPU needed)."""
+import ctypes
+
+import pytest
+
+from vllm_b200 import _native as N
+
+
+def test_library_exports_every_declared_symbol(native):
+    declared = N.declared_symbols()
+    assert len(declared) >= 30
+    missing = [name for name in declared if not hasattr(native, name)]
+    assert not missing, f"declared in include/tvp_paged.h but not exported: {missing}"
+
+
+def test_every_declared_symbol_has_a_binding():
+    assert set(N.declared_symbols()) == set(N._SIGNATURES)
+
+
+def test_strerror_and_version(native):
+    assert native.tvp_version() == 1
+    assert native.tvp_strerror(N.TVP_OK) == b"ok"
+    assert b"invalid" in native.tvp_strerror(N.TVP_ERR_INVALID_ARGUMENT)
+    assert b"free blocks" in native.tvp_strerror(N.TVP_ERR_NO_FREE_BLOCKS)
+
+
+def test_rope_append_rejects_bad_arguments_on_host(native):
+    # Null pools / tables: refused before any CUDA call.
+    rc = native.tvp_rope_append(None, None, 8, 16, 0, 8, None, 4, 1, None, None, 1, None, None,
+                                None, 32, 0, None, None)
+    assert rc == N.TVP_ERR_INVALID_ARGUMENT
+    fake = ctypes.c_void_p(0x10000)
+    # layer out of range
+    rc = native.tvp_rope_append(fake, fake, 8, 16, 16, 8, fake, 4, 1, None, fake, 1, fake, fake,
+                                None, 32, 0, None, None)
+    assert rc == N.TVP_ERR_INVALID_ARGUMENT
+    # unknown flag bit
+    rc = native.tvp_rope_append(fake, fake, 8, 16, 0, 8, fake, 4, 1, None, fake, 1, fake, fake,
+                                None, 32, 64, None, None)
+    assert rc == N.TVP_ERR_INVALID_ARGUMENT
+    # q rope requested without q
+    rc = native.tvp_rope_append(fake, fake, 8, 16, 0, 8, fake, 4, 1, None, fake, 1, fake, fake,
+                                None, 32, N.TVP_APPEND_ROPE_Q, None, None)
+    assert rc == N.TVP_ERR_INVALID_ARGUMENT
+    # misaligned v
+    rc = native.tvp_rope_append(fake, fake, 8, 16, 0, 8, fake, 4, 1, None, fake, 1, fake,
+                                ctypes.c_void_p(0x10002), None, 32, 0, None, None)
+    assert rc == N.TVP_ERR_INVALID_ARGUMENT
+    # zero tokens is a no-op
+    rc = native.tvp_rope_append(fake, fake, 8, 16, 0, 8, fake, 4, 1, None, fake, 0, fake, fake,
+                                None, 32, 0, None, None)
+    assert rc == N.TVP_OK
+
+
+def test_decode_rejects_bad_arguments_on_host(native):
+    fake = ctypes.c_void_p(0x10000)
+    args = dict(q=fake, k=fake, v=fake, pages=8, layers=16, layer=0, kvh=8, qh=32, tables=fake,
+                stride=4, lens=fake, batch=2, scale=0.125, mode=0, ctas=148, ws=fake, wsb=1 << 30,
+                out=fake, err=None, stream=None)
+
+    def call(**over):
+        a = dict(args, **over)
+        return native.tvp_paged_decode_attention(a["q"], a["k"], a["v"], a["pages"], a["layers"],
+                                                 a["layer"], a["kvh"], a["qh"], a["tables"],
+                                                 a["stride"], a["lens"], a["batch"], a["scale"],
+                                                 a["mode"], a["ctas"], a["ws"], a["wsb"], a["out"],
+                                                 a["err"], a["stream"])
+
+    assert call(q=None) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(layer=16) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(batch=0) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(scale=float("nan")) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(kvh=4) == N.TVP_ERR_UNSUPPORTED
+    assert call(qh=16) == N.TVP_ERR_UNSUPPORTED
+    assert call(mode=7) == N.TVP_ERR_UNSUPPORTED
+    assert call(ws=None) == N.TVP_ERR_WORKSPACE
+    assert call(wsb=16) == N.TVP_ERR_WORKSPACE
+    assert call(out=ctypes.c_void_p(0x10008)) == N.TVP_ERR_INVALID_ARGUMENT
+
+
+def test_workspace_size_grows_with_batch_and_grid(native):
+    a = native.tvp_decode_workspace_bytes(4, 8, 148)
+    b = native.tvp_decode_workspace_bytes(256, 8, 148)
+    c = native.tvp_decode_workspace_bytes(256, 8, 296)
+    assert 0 < a < b < c
+    assert a % 256 == 0
+    assert native.tvp_decode_workspace_bytes(0, 8, 148) == 0
+    assert native.tvp_decode_workspace_bytes(4, 4, 148) == 0
+    # partials: 2 slots x 8 KV heads x (4 + 4 + 256) floats per CTA
+    assert c - b >= 148 * 2 * 8 * 264 * 4
+
+
+def test_python_layer_maps_codes_to_reference_exceptions():
+    with pytest.raises(ValueError):
+        N.check(N.TVP_ERR_INVALID_ARGUMENT)
+    with pytest.raises(N.TvpNoFreeBlocks):
+        N.check(N.TVP_ERR_NO_FREE_BLOCKS)
+    with pytest.raises(N.TvpError):
+        N.check(N.TVP_ERR_RUNTIME)
+    assert N.check(3) == 3
+
+
+def test_cxx_header_compiles_against_c_header(tmp_path):
+    """include/tvp_paged.h is plain C (no C++ or torch types)."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not available")
+    src = tmp_path / "t.c"
+    src.write_text("#include \"tvp_paged.h\"\nint main(void){return tvp_version() == 0;}\n")
+    subprocess.run([gcc, "-std=c99", "-Wall", "-Werror", "-I", str(N.HEADER_PATH.parent), "-c",
+                    str(src), "-o", str(tmp_path / "t.o")], check=True)

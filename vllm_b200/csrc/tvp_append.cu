@@ -1,0 +1,98 @@
+// K1 — fused llama3 RoPE + paged KV append (prefill and decode forms).
+//
+// One CTA per token row.  The CTA rotates the row's q heads in place (optional),
+// rotates its K heads, and writes K and V straight into the token's physical
+// page slot.  Replaces rope/ropeBatch (src/model/RoPe.cu:31-62) followed by
+// storePagedKV (src/model/paged_kvcache.cu:147-166, a host loop of synchronous
+// D2D copies) or storePagedKVBatchKernel (src/model/paged_attention.cu:89-99).
+#include "tvp_params.cuh"
+
+namespace tvp {
+
+// llama3-scaled inverse frequency of rotate-half pair `pair` (0..31):
+// theta_0 = 500000, factor 32, low/high frequency factors 1/4, original
+// context 8192.  Same calls (powf) and the same expression order as the
+// reference ropeKernel (src/model/RoPe.cu:15-22), so the FP32 value is the
+// reference's bit for bit under the same compiler flags (no fast-math,
+// default FMA contraction).
+__device__ __forceinline__ float llama3_theta(int pair) {
+  float theta = 1.0f / powf(500000.0f, (2.0f * pair) / kHeadDim);
+  float wavelength = 6.283185307179586f / theta;
+  if (wavelength > 8192.0f) {
+    theta /= 32.0f;
+  } else if (wavelength >= 2048.0f) {
+    float smooth = (8192.0f / wavelength - 1.0f) / 3.0f;
+    theta = (1.0f - smooth) * theta / 32.0f + smooth * theta;
+  }
+  return theta;
+}
+
+// Rotation of one (x, y) = (d, d + 32) pair, as src/model/RoPe.cu:23-27.
+__device__ __forceinline__ void rope_rotate(__nv_bfloat16 x_i, __nv_bfloat16 y_i, int position,
+                                            float theta, __nv_bfloat16& x_o,
+                                            __nv_bfloat16& y_o) {
+  float angle = position * theta;
+  x_o = (__nv_bfloat16)((float)x_i * cosf(angle) - (float)y_i * sinf(angle));
+  y_o = (__nv_bfloat16)((float)x_i * sinf(angle) + (float)y_i * cosf(angle));
+}
+
+
+__global__ void __launch_bounds__(256) rope_append_kernel(AppendParams p) {
+  const int t = blockIdx.x;
+  const int pos = p.token_pos[t];
+  const int seq = p.token_seq ? p.token_seq[t] : t;
+  const int kv_dim = p.kv_heads * kHeadDim;
+
+  if (p.flags & TVP_APPEND_ROPE_Q) {
+    __nv_bfloat16* qrow = p.q + (size_t)t * p.q_heads * kHeadDim;
+    const int pairs = p.q_heads * (kHeadDim / 2);
+    for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
+      const int pair = i % (kHeadDim / 2);
+      const int x_index = (i / (kHeadDim / 2)) * kHeadDim + pair;
+      const int y_index = x_index + kHeadDim / 2;
+      __nv_bfloat16 xo, yo;
+      rope_rotate(qrow[x_index], qrow[y_index], pos, llama3_theta(pair), xo, yo);
+      qrow[x_index] = xo;
+      qrow[y_index] = yo;
+    }
+  }
+
+  const bool row_ok = seq >= 0 && seq < p.num_seqs && pos >= 0 && (pos / kPage) < p.table_stride;
+  if (!row_ok) {
+    if (threadIdx.x == 0) record_error(p.err, TVP_DEVERR_BAD_TOKEN);
+    return;
+  }
+  const int phys = p.tables[(size_t)seq * p.table_stride + pos / kPage];
+  if (phys < 0 || phys >= p.num_pages) {
+    if (threadIdx.x == 0) record_error(p.err, TVP_DEVERR_BAD_PAGE);
+    return;
+  }
+  const size_t dst = (size_t)(p.layer_row_base + (long long)phys * kPage + pos % kPage) * kv_dim;
+  __nv_bfloat16* krow = p.k + (size_t)t * kv_dim;
+
+  const int kpairs = p.kv_heads * (kHeadDim / 2);
+  for (int i = threadIdx.x; i < kpairs; i += blockDim.x) {
+    const int pair = i % (kHeadDim / 2);
+    const int x_index = (i / (kHeadDim / 2)) * kHeadDim + pair;
+    const int y_index = x_index + kHeadDim / 2;
+    __nv_bfloat16 xo = krow[x_index], yo = krow[y_index];
+    if (p.flags & TVP_APPEND_ROPE_K) rope_rotate(xo, yo, pos, llama3_theta(pair), xo, yo);
+    p.k_pool[dst + x_index] = xo;
+    p.k_pool[dst + y_index] = yo;
+    if (p.flags & TVP_APPEND_WRITEBACK_K) {
+      krow[x_index] = xo;
+      krow[y_index] = yo;
+    }
+  }
+
+  const uint4* vsrc = reinterpret_cast<const uint4*>(p.v + (size_t)t * kv_dim);
+  uint4* vdst = reinterpret_cast<uint4*>(p.v_pool + dst);
+  for (int i = threadIdx.x; i < kv_dim / 8; i += blockDim.x) vdst[i] = vsrc[i];
+}
+
+cudaError_t launch_rope_append(const AppendParams& p, int num_tokens, cudaStream_t stream) {
+  rope_append_kernel<<<num_tokens, 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace tvp

@@ -1,0 +1,157 @@
+// K2c — decode attention with the reference's rounding points (COMPAT mode).
+//
+// The reference rounds three times on the decode path: the cuBLAS score GEMV
+// writes BF16 scores (alpha = scale applied to the FP32 dot product,
+// src/model/attention.cu:53-93), softmaxKernel turns them into BF16
+// probabilities with an exact max, expf and a pairwise-tree sum over the row
+// (src/model/softmax.cu:6-45), and the P.V GEMV accumulates in FP32 and writes
+// BF16 (src/model/attention.cu:95-142).  This kernel keeps every one of those
+// rounding points and the tree order of the sum; only the FP32 order inside the
+// two dot products is its own (sequential FMA), which cuBLAS does not specify.
+// One CTA per (sequence, KV head); pages are read in place.  Used where greedy
+// token identity with the reference matters more than bandwidth.
+#include "tvp_params.cuh"
+
+namespace tvp {
+
+constexpr int kCompatMaxLen = 4096;
+constexpr int kCompatThreads = 256;
+
+
+__device__ __forceinline__ float round_bf16(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+__global__ void __launch_bounds__(kCompatThreads) compat_decode_kernel(const CompatParams p) {
+  extern __shared__ float sm[];
+  float* qs = sm;                             // [4][64]
+  float* sc = qs + kGroup * kHeadDim;         // [4][kCompatMaxLen] scores, then probabilities
+  float* tree = sc + kGroup * kCompatMaxLen;  // [4][kCompatMaxLen] pairwise-sum buffer
+  __shared__ float red[kGroup][kCompatThreads / 32];
+  __shared__ float row_max[kGroup], row_sum[kGroup];
+
+  const int s = blockIdx.x, g = blockIdx.y, tid = threadIdx.x;
+  constexpr int kOutRow = kMaxKvHeads * kGroup * kHeadDim;
+  const int L = p.seq_lens[s];
+  __nv_bfloat16* out = p.out + (size_t)s * kOutRow + g * kGroup * kHeadDim;
+  if (L <= 0 || L > kCompatMaxLen || L > p.table_stride * kPage) {
+    if (L != 0 && tid == 0) record_error(p.err, TVP_DEVERR_BAD_LENGTH);
+    out[tid] = __float2bfloat16_rn(0.f);
+    return;
+  }
+  qs[tid] = __bfloat162float(p.q[(size_t)s * kOutRow + g * kGroup * kHeadDim + tid]);
+  __syncthreads();
+
+  // Scores: s = bf16(scale * (q . k)), FP32 accumulation.
+  for (int t = tid; t < L; t += kCompatThreads) {
+    const int phys = p.tables[(size_t)s * p.table_stride + t / kPage];
+    if (phys < 0 || phys >= p.num_pages) {
+      record_error(p.err, TVP_DEVERR_BAD_PAGE);
+      for (int h = 0; h < kGroup; ++h) sc[h * kCompatMaxLen + t] = -INFINITY;
+      continue;
+    }
+    const uint4* krow = reinterpret_cast<const uint4*>(
+        p.k_pool + (size_t)(p.layer_row_base + (long long)phys * kPage + t % kPage) *
+                       (kMaxKvHeads * kHeadDim) +
+        g * kHeadDim);
+    float k[kHeadDim];
+#pragma unroll
+    for (int i = 0; i < kHeadDim / 8; ++i) {
+      const uint4 u = __ldg(krow + i);
+      k[8 * i + 0] = bf16lo_to_f32(u.x); k[8 * i + 1] = bf16hi_to_f32(u.x);
+      k[8 * i + 2] = bf16lo_to_f32(u.y); k[8 * i + 3] = bf16hi_to_f32(u.y);
+      k[8 * i + 4] = bf16lo_to_f32(u.z); k[8 * i + 5] = bf16hi_to_f32(u.z);
+      k[8 * i + 6] = bf16lo_to_f32(u.w); k[8 * i + 7] = bf16hi_to_f32(u.w);
+    }
+#pragma unroll
+    for (int h = 0; h < kGroup; ++h) {
+      float acc = 0.f;
+#pragma unroll
+      for (int d = 0; d < kHeadDim; ++d) acc = fmaf(qs[h * kHeadDim + d], k[d], acc);
+      sc[h * kCompatMaxLen + t] = round_bf16(p.scale * acc);
+    }
+  }
+  __syncthreads();
+
+  // Exact row maximum (order-free).
+  float mx[kGroup];
+#pragma unroll
+  for (int h = 0; h < kGroup; ++h) mx[h] = -INFINITY;
+  for (int t = tid; t < L; t += kCompatThreads)
+#pragma unroll
+    for (int h = 0; h < kGroup; ++h) mx[h] = fmaxf(mx[h], sc[h * kCompatMaxLen + t]);
+#pragma unroll
+  for (int h = 0; h < kGroup; ++h) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], o));
+    if ((tid & 31) == 0) red[h][tid >> 5] = mx[h];
+  }
+  __syncthreads();
+  if (tid < kGroup) {
+    float m = red[tid][0];
+    for (int w = 1; w < kCompatThreads / 32; ++w) m = fmaxf(m, red[tid][w]);
+    row_max[tid] = m;
+  }
+  __syncthreads();
+
+  // e_t = expf(s_t - max), summed by the reference's pairwise tree:
+  // for i = 1, 2, 4, ...: e[t] += e[t + i] for t % 2i == 0 and t + i < L.
+  for (int t = tid; t < L; t += kCompatThreads)
+#pragma unroll
+    for (int h = 0; h < kGroup; ++h)
+      tree[h * kCompatMaxLen + t] = expf(sc[h * kCompatMaxLen + t] - row_max[h]);
+  __syncthreads();
+  for (int i = 1; i < L; i *= 2) {
+    for (int t = tid * 2 * i; t < L; t += kCompatThreads * 2 * i) {
+      if (t + i < L) {
+#pragma unroll
+        for (int h = 0; h < kGroup; ++h)
+          tree[h * kCompatMaxLen + t] = tree[h * kCompatMaxLen + t] + tree[h * kCompatMaxLen + t + i];
+      }
+    }
+    __syncthreads();
+  }
+  if (tid < kGroup) row_sum[tid] = tree[tid * kCompatMaxLen];
+  __syncthreads();
+  for (int t = tid; t < L; t += kCompatThreads)
+#pragma unroll
+    for (int h = 0; h < kGroup; ++h)
+      sc[h * kCompatMaxLen + t] =
+          round_bf16(expf(sc[h * kCompatMaxLen + t] - row_max[h]) / row_sum[h]);
+  __syncthreads();
+
+  // o[h][d] = bf16(sum_t p[h][t] * v[t][d]), FP32 accumulation.
+  const int h = tid / kHeadDim, d = tid % kHeadDim;
+  float acc = 0.f;
+  for (int t = 0; t < L; ++t) {
+    const int phys = __ldg(p.tables + (size_t)s * p.table_stride + t / kPage);
+    if (phys < 0 || phys >= p.num_pages) continue;
+    const float v = __bfloat162float(
+        p.v_pool[(size_t)(p.layer_row_base + (long long)phys * kPage + t % kPage) *
+                     (kMaxKvHeads * kHeadDim) +
+                 g * kHeadDim + d]);
+    acc = fmaf(sc[h * kCompatMaxLen + t], v, acc);
+  }
+  out[h * kHeadDim + d] = __float2bfloat16_rn(acc);
+}
+
+size_t compat_smem_bytes() {
+  return (size_t)(kGroup * kHeadDim + 2 * kGroup * kCompatMaxLen) * sizeof(float);
+}
+
+cudaError_t launch_compat_decode(const CompatParams& p, int batch, cudaStream_t stream) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    e = cudaFuncSetAttribute(compat_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)compat_smem_bytes());
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  compat_decode_kernel<<<dim3(batch, kMaxKvHeads), kCompatThreads, compat_smem_bytes(), stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace tvp

@@ -1,0 +1,478 @@
+// K2 — fused GQA paged decode attention with a split-K (flash-decoding)
+// combine, and the per-step plan kernel.
+//
+// Replaces the reference's decode attention (src/model/paged_transformer.cu:85-94):
+// gatherPagedKernel copies every page of K into a contiguous view, 32 cuBLAS
+// GEMVs per row compute BF16 scores, 32 softmax launches per row normalise
+// them, a second gather copies V and 32 more GEMVs form the output
+// (src/model/paged_attention.cu:102-161, src/model/attention.cu:53-142,
+// src/model/softmax.cu:6-72).  Here one persistent launch reads every page
+// once, in place.
+//
+// Work split.  The plan kernel turns the attended lengths into page prefix
+// sums cu[0..B].  The T = cu[B] pages of the step, laid end to end, are cut
+// into gridDim.x contiguous ranges of floor/ceil(T / C) pages, one per CTA, so
+// every CTA streams the same number of pages whatever the length mix.  A range
+// covers whole sequences ("complete pieces", finalised in place) and at most
+// two sequence fragments at its ends ("partial pieces"); partials go to the
+// workspace and the last CTA to finish a sequence merges them (a counter per
+// (sequence, KV head), no waiting).
+//
+// CTA layout: one producer warp and SETS x 8 consumer warps.  The producer
+// streams one page (all 8 KV heads, 16 rows x 1 KiB of K and of V) per stage
+// into shared memory with bulk copies (cp.async.bulk, one per 1 KiB row, so each
+// row can land at a 1040-byte pitch that keeps ldmatrix conflict-free).
+// Consumer warp g of set s owns KV head g on the pages k with k % SETS == s.
+// Per page it forms S^T = K_g Q_g^T (16 tokens x 8 query columns, 4 real) and
+// O^T += V_g^T P^T with mma.m16n8k16 (BF16 in, FP32 accumulate), running an
+// online softmax in base 2 on the accumulator fragments; P^T is turned from
+// accumulator layout into operand layout with movmatrix.
+#include "tvp_params.cuh"
+
+namespace tvp {
+
+constexpr int kPlanMagic = 0x54565031;  // "TVP1"
+constexpr int kRowBytes = kMaxKvHeads * kHeadDim * 2;      // 1024: one token of one pool
+constexpr int kPitch = kRowBytes + 16;                      // shared-memory row pitch
+constexpr int kStageBytes = 2 * kPage * kPitch;             // K rows then V rows
+constexpr int kMergeFields = 20;                            // m0 m1 l0 l1 acc[16]
+
+
+// ---------------------------------------------------------------------------
+// Plan: cu[b] = sum_{i<b} ceil(L_i / 16), header, counters = 0.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024)
+    decode_plan_kernel(const int32_t* __restrict__ lens, int batch, int table_stride,
+                       int num_ctas, int groups, int32_t* header, int32_t* cu,
+                       int32_t* counters, int32_t* err) {
+  __shared__ int warp_sums[32];
+  __shared__ int carry;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < batch; base += 1024) {
+    const int i = base + tid;
+    int L = i < batch ? lens[i] : 0;
+    if (i < batch && (L < 0 || L > table_stride * kPage)) {
+      record_error(err, TVP_DEVERR_BAD_LENGTH);
+      L = L < 0 ? 0 : table_stride * kPage;
+    }
+    const int pages = (L + kPage - 1) / kPage;
+    int x = pages;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int w = warp_sums[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      warp_sums[lane] = w;
+    }
+    __syncthreads();
+    if (i < batch) cu[i] = carry + (warp > 0 ? warp_sums[warp - 1] : 0) + x - pages;
+    __syncthreads();
+    if (tid == 0) carry += warp_sums[31];
+    __syncthreads();
+  }
+  if (tid == 0) {
+    cu[batch] = carry;
+    header[0] = kPlanMagic;
+    header[1] = batch;
+    header[2] = num_ctas;
+    header[3] = groups;
+  }
+  for (int i = tid; i < batch * groups; i += blockDim.x) counters[i] = 0;
+}
+
+// CTA whose page range holds flattened page p (ranges [floor(cT/C), floor((c+1)T/C))).
+__device__ __forceinline__ int cta_of_page(long long p, long long T, long long C) {
+  return (int)(((p + 1) * C - 1) / T);
+}
+__device__ __forceinline__ int range_begin(long long c, long long T, long long C) {
+  return (int)(c * T / C);
+}
+// Partial slot of sequence [first, end) inside CTA c: slot 0 when the
+// sequence started at or before the CTA's range, slot 1 otherwise.
+__device__ __forceinline__ int partial_slot(int c, int first, long long T, long long C) {
+  return c * 2 + (range_begin(c, T, C) < first ? 1 : 0);
+}
+
+// Merge of all partial pieces of one sequence for KV head g (32 lanes: lane
+// -> query head lane/8 of the group, channels (lane%8)*8 .. +7).
+__device__ void combine_sequence(const DecodeParams& p, int s, int first, int end, int g,
+                                 long long T, long long C, int lane) {
+  const int c0 = cta_of_page(first, T, C), c1 = cta_of_page(end - 1, T, C);
+  const int h = lane >> 3, d0 = (lane & 7) * 8;
+  float M = -INFINITY;
+  for (int c = c0; c <= c1; ++c) {
+    const int slot = (c == c0) ? partial_slot(c, first, T, C) : c * 2;
+    const float* part = p.partials + ((size_t)slot * kMaxKvHeads + g) * kPartialFloats;
+    M = fmaxf(M, __ldcg(part + h));
+  }
+  float o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = 0.f;
+  float lsum = 0.f;
+  for (int c = c0; c <= c1; ++c) {
+    const int slot = (c == c0) ? partial_slot(c, first, T, C) : c * 2;
+    const float* part = p.partials + ((size_t)slot * kMaxKvHeads + g) * kPartialFloats;
+    const float m = __ldcg(part + h);
+    const float w = (m == -INFINITY) ? 0.f : exp2f(m - M);
+    lsum += w * __ldcg(part + kGroup + h);
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(part + 2 * kGroup + h * kHeadDim + d0));
+    const float4 b =
+        __ldcg(reinterpret_cast<const float4*>(part + 2 * kGroup + h * kHeadDim + d0 + 4));
+    o[0] += w * a.x; o[1] += w * a.y; o[2] += w * a.z; o[3] += w * a.w;
+    o[4] += w * b.x; o[5] += w * b.y; o[6] += w * b.z; o[7] += w * b.w;
+  }
+  const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+  uint4 packed;
+  packed.x = pack_bf16x2(o[0] * inv, o[1] * inv);
+  packed.y = pack_bf16x2(o[2] * inv, o[3] * inv);
+  packed.z = pack_bf16x2(o[4] * inv, o[5] * inv);
+  packed.w = pack_bf16x2(o[6] * inv, o[7] * inv);
+  __nv_bfloat16* dst = p.out + (size_t)s * (kMaxKvHeads * kGroup * kHeadDim) +
+                       (g * kGroup + h) * kHeadDim + d0;
+  *reinterpret_cast<uint4*>(dst) = packed;
+}
+
+template <int STAGES, int SETS>
+__global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
+    paged_decode_kernel(const DecodeParams p) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  const int T_header_ok = (p.header[0] == kPlanMagic && p.header[1] == p.batch &&
+                           p.header[2] == (int)gridDim.x && p.header[3] == kMaxKvHeads);
+  if (!T_header_ok) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) record_error(p.err, TVP_DEVERR_BAD_PLAN);
+    return;
+  }
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
+  uint64_t* empty_bar = full_bar + STAGES;
+  int* stage_ok = reinterpret_cast<int*>(empty_bar + STAGES);
+  volatile int* abort_flag = stage_ok + STAGES;
+  float* merge = reinterpret_cast<float*>(smem + STAGES * kStageBytes + 2 * STAGES * 8 +
+                                          (STAGES + 4) * 4);
+  merge = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(merge) + 15) & ~uintptr_t(15));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_addr(&full_bar[s]), 1);
+      mbar_init(smem_addr(&empty_bar[s]), kMaxKvHeads);
+    }
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  const long long C = gridDim.x, c = blockIdx.x;
+  const long long T = p.cu[p.batch];
+  const int p_begin = (int)(c * T / C), p_end = (int)((c + 1) * T / C);
+  const uint32_t smem_base = smem_addr(smem);
+
+  // First sequence of the range: the s with cu[s] <= p_begin < cu[s + 1].
+  int s0 = 0;
+  if (p_begin < p_end) {
+    int lo = 0, hi = p.batch;  // invariant: cu[lo] <= p_begin < cu[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (__ldg(p.cu + mid) <= p_begin) lo = mid; else hi = mid;
+    }
+    s0 = lo;
+  }
+
+  if (warp == SETS * kMaxKvHeads) {
+    // ------------------------------ producer ------------------------------
+    int s = s0;
+    int kk = 0;
+    for (int pg = p_begin; pg < p_end; ++pg, ++kk) {
+      while (pg >= __ldg(p.cu + s + 1)) ++s;
+      const int j = pg - __ldg(p.cu + s);
+      const int stage = kk % STAGES;
+      int stop = 0;
+      if (lane == 0) {
+        if (kk >= STAGES && !*abort_flag &&
+            !mbar_wait_bounded(smem_addr(&empty_bar[stage]), ((kk / STAGES) - 1) & 1)) {
+          *abort_flag = 1;
+          record_error(p.err, TVP_DEVERR_TIMEOUT);
+        }
+        stop = *abort_flag;
+      }
+      if (__shfl_sync(0xffffffffu, stop, 0)) break;
+      const int phys = __ldg(p.tables + (size_t)s * p.table_stride + j);
+      const bool ok = phys >= 0 && phys < p.num_pages;
+      const uint32_t full = smem_addr(&full_bar[stage]);
+      if (lane == 0) {
+        stage_ok[stage] = ok ? 1 : 0;
+        if (!ok) record_error(p.err, TVP_DEVERR_BAD_PAGE);
+        mbar_arrive_expect_tx(full, ok ? 2u * kPage * kRowBytes : 0u);
+      }
+      __syncwarp();
+      if (ok) {
+        const int row = lane & (kPage - 1);
+        const __nv_bfloat16* pool = lane < kPage ? p.k_pool : p.v_pool;
+        const __nv_bfloat16* src =
+            pool + (size_t)(p.layer_row_base + (long long)phys * kPage + row) * (kRowBytes / 2);
+        const uint32_t dst = smem_base + stage * kStageBytes + (lane < kPage ? 0 : kPage * kPitch) +
+                             row * kPitch;
+        bulk_copy_g2s(dst, src, kRowBytes, full);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------ consumers -------------------------------
+  const int set = warp / kMaxKvHeads;
+  const int g = warp % kMaxKvHeads;
+  const int tr = lane >> 2;   // accumulator row (token) of this lane
+  const int hc = lane & 3;    // accumulator column pair (query heads 2hc, 2hc+1)
+  const int mat = lane >> 3, mrow = lane & 7;
+  // ldmatrix row addresses (bytes within a stage) for this lane.
+  const uint32_t k_lane = (mrow + (mat & 1) * 8) * kPitch + g * 128 + (mat >> 1) * 16;
+  const uint32_t v_lane = kPage * kPitch + (mrow + (mat >> 1) * 8) * kPitch + g * 128 + (mat & 1) * 16;
+  constexpr int kOutRow = kMaxKvHeads * kGroup * kHeadDim;  // 2048
+
+  // Rows of length 0 attend to nothing: their output is zero.
+  if (set == 0) {
+    for (int s = blockIdx.x; s < p.batch; s += gridDim.x) {
+      if (__ldg(p.cu + s) == __ldg(p.cu + s + 1)) {
+        uint4 z = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(p.out + (size_t)s * kOutRow + g * kGroup * kHeadDim + lane * 8) = z;
+      }
+    }
+  }
+
+  int s = s0;
+  int pg = p_begin;
+  int kbase = 0;
+  while (pg < p_end) {
+    while (pg >= __ldg(p.cu + s + 1)) ++s;
+    const int first = __ldg(p.cu + s), end = __ldg(p.cu + s + 1);
+    const int piece_end = min(p_end, end);
+    const int n = piece_end - pg;
+    const bool complete = (pg == first) && (piece_end == end);
+    const int L = __ldg(p.seq_lens + s);
+
+    // Q_g^T operand fragments: column n = tr holds query head 4g + tr (tr < 4).
+    uint32_t qb[4][2];
+    {
+      const __nv_bfloat16* qrow = p.q + (size_t)s * kOutRow + (g * kGroup + tr) * kHeadDim + 2 * hc;
+#pragma unroll
+      for (int k4 = 0; k4 < 4; ++k4) {
+        qb[k4][0] = tr < kGroup ? __ldg(reinterpret_cast<const uint32_t*>(qrow + k4 * 16)) : 0u;
+        qb[k4][1] = tr < kGroup ? __ldg(reinterpret_cast<const uint32_t*>(qrow + k4 * 16 + 8)) : 0u;
+      }
+    }
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+
+    for (int i = set; i < n; i += SETS) {
+      const int kk = kbase + i;
+      const int stage = kk % STAGES;
+      const uint32_t parity = (kk / STAGES) & 1;
+      bool ready = false;
+      if (!*abort_flag) ready = mbar_wait_bounded(smem_addr(&full_bar[stage]), parity);
+      ready = __all_sync(0xffffffffu, ready);
+      if (!ready && lane == 0 && !*abort_flag) {
+        *abort_flag = 1;
+        record_error(p.err, TVP_DEVERR_TIMEOUT);
+      }
+      bool zeroed = false;
+      if (ready && stage_ok[stage]) {
+        const int j = pg - first + i;
+        const int valid = min(kPage, L - j * kPage);
+        const uint32_t sb = smem_base + stage * kStageBytes;
+        if (valid < kPage) {
+          // Rows past the sequence end hold stale data: zero this head's V slice
+          // so that 0-probability rows cannot inject NaN/Inf into P.V.
+          unsigned char* vbase = smem + stage * kStageBytes + kPage * kPitch + g * 128;
+          for (int idx = lane; idx < (kPage - valid) * 8; idx += 32) {
+            const int r = valid + (idx >> 3);
+            *reinterpret_cast<uint4*>(vbase + r * kPitch + (idx & 7) * 16) = make_uint4(0, 0, 0, 0);
+          }
+          zeroed = true;
+          __syncwarp();
+        }
+        // S^T = K_g Q_g^T
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+        for (int k4 = 0; k4 < 4; ++k4) {
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4(sb + k_lane + k4 * 32, a0, a1, a2, a3);
+          mma_bf16_16816(s0, s1, s2, s3, a0, a1, a2, a3, qb[k4][0], qb[k4][1]);
+        }
+        float x0 = s0 * p.scale_log2, x1 = s1 * p.scale_log2;
+        float x2 = s2 * p.scale_log2, x3 = s3 * p.scale_log2;
+        if (valid < kPage) {
+          if (tr >= valid) x0 = x1 = -INFINITY;
+          if (tr + 8 >= valid) x2 = x3 = -INFINITY;
+        }
+        float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+        }
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
+        m0 = mn0;
+        m1 = mn1;
+        const uint32_t pa = pack_bf16x2(exp2f(x0 - mn0), exp2f(x1 - mn1));
+        const uint32_t pb = pack_bf16x2(exp2f(x2 - mn0), exp2f(x3 - mn1));
+        l0 = l0 * al0 + (bf16lo_to_f32(pa) + bf16lo_to_f32(pb));
+        l1 = l1 * al1 + (bf16hi_to_f32(pa) + bf16hi_to_f32(pb));
+        if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
+#pragma unroll
+          for (int d = 0; d < 4; ++d) {
+            acc[d][0] *= al0; acc[d][1] *= al1; acc[d][2] *= al0; acc[d][3] *= al1;
+          }
+        }
+        // O^T += V_g^T P^T
+        const uint32_t y0 = movmatrix_trans(pa), y1 = movmatrix_trans(pb);
+#pragma unroll
+        for (int d = 0; d < 4; ++d) {
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4_trans(sb + v_lane + d * 32, a0, a1, a2, a3);
+          mma_bf16_16816(acc[d][0], acc[d][1], acc[d][2], acc[d][3], a0, a1, a2, a3, y0, y1);
+        }
+      }
+      if (zeroed) fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&empty_bar[stage]));
+    }
+
+    if (SETS > 1) {
+      float* mg = merge + g * kMergeFields * 32;
+      if (set == 1) {
+        mg[0 * 32 + lane] = m0; mg[1 * 32 + lane] = m1;
+        mg[2 * 32 + lane] = l0; mg[3 * 32 + lane] = l1;
+#pragma unroll
+        for (int d = 0; d < 4; ++d)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) mg[(4 + d * 4 + e) * 32 + lane] = acc[d][e];
+      }
+      named_barrier_sync(1 + g, 64);
+      if (set == 0) {
+        const float mb0 = mg[0 * 32 + lane], mb1 = mg[1 * 32 + lane];
+        const float M0 = fmaxf(m0, mb0), M1 = fmaxf(m1, mb1);
+        const float wa0 = m0 == -INFINITY ? 0.f : exp2f(m0 - M0);
+        const float wa1 = m1 == -INFINITY ? 0.f : exp2f(m1 - M1);
+        const float wb0 = mb0 == -INFINITY ? 0.f : exp2f(mb0 - M0);
+        const float wb1 = mb1 == -INFINITY ? 0.f : exp2f(mb1 - M1);
+        l0 = l0 * wa0 + mg[2 * 32 + lane] * wb0;
+        l1 = l1 * wa1 + mg[3 * 32 + lane] * wb1;
+#pragma unroll
+        for (int d = 0; d < 4; ++d) {
+          acc[d][0] = acc[d][0] * wa0 + mg[(4 + d * 4 + 0) * 32 + lane] * wb0;
+          acc[d][1] = acc[d][1] * wa1 + mg[(4 + d * 4 + 1) * 32 + lane] * wb1;
+          acc[d][2] = acc[d][2] * wa0 + mg[(4 + d * 4 + 2) * 32 + lane] * wb0;
+          acc[d][3] = acc[d][3] * wa1 + mg[(4 + d * 4 + 3) * 32 + lane] * wb1;
+        }
+        m0 = M0;
+        m1 = M1;
+      }
+      named_barrier_sync(1 + g, 64);
+    }
+
+    if (set == 0) {
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+      }
+      const int h0 = 2 * hc, h1 = 2 * hc + 1;
+      if (complete) {
+        if (hc < 2) {
+          const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+          __nv_bfloat16* o = p.out + (size_t)s * kOutRow + g * kGroup * kHeadDim;
+#pragma unroll
+          for (int d = 0; d < 4; ++d) {
+            const int ch = 16 * d + tr;
+            o[h0 * kHeadDim + ch] = __float2bfloat16_rn(acc[d][0] * inv0);
+            o[h1 * kHeadDim + ch] = __float2bfloat16_rn(acc[d][1] * inv1);
+            o[h0 * kHeadDim + ch + 8] = __float2bfloat16_rn(acc[d][2] * inv0);
+            o[h1 * kHeadDim + ch + 8] = __float2bfloat16_rn(acc[d][3] * inv1);
+          }
+        }
+      } else {
+        const int slot = (int)c * 2 + (first <= p_begin ? 0 : 1);
+        float* part = p.partials + ((size_t)slot * kMaxKvHeads + g) * kPartialFloats;
+        if (hc < 2) {
+          if (tr == 0) {
+            part[h0] = m0; part[h1] = m1;
+            part[kGroup + h0] = l0; part[kGroup + h1] = l1;
+          }
+          float* po = part + 2 * kGroup;
+#pragma unroll
+          for (int d = 0; d < 4; ++d) {
+            const int ch = 16 * d + tr;
+            po[h0 * kHeadDim + ch] = acc[d][0];
+            po[h1 * kHeadDim + ch] = acc[d][1];
+            po[h0 * kHeadDim + ch + 8] = acc[d][2];
+            po[h1 * kHeadDim + ch + 8] = acc[d][3];
+          }
+        }
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+          const int pieces = cta_of_page(end - 1, T, C) - cta_of_page(first, T, C) + 1;
+          const int old = atomicAdd(p.counters + (size_t)s * kMaxKvHeads + g, 1);
+          last = (old == pieces - 1);
+          if (last) {
+            atomicExch(p.counters + (size_t)s * kMaxKvHeads + g, 0);
+            __threadfence();
+          }
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) combine_sequence(p, s, first, end, g, T, C, lane);
+      }
+    }
+    kbase += n;
+    pg = piece_end;
+  }
+}
+
+constexpr int kStages = 6;
+constexpr int kSets = 2;
+constexpr int kDecodeThreads = (kSets * kMaxKvHeads + 1) * 32;
+
+size_t decode_smem_bytes() {
+  return (size_t)kStages * kStageBytes + 2 * kStages * 8 + (kStages + 4) * 4 + 16 +
+         (size_t)kMaxKvHeads * kMergeFields * 32 * 4;
+}
+
+cudaError_t launch_decode_plan(const int32_t* lens, int batch, int table_stride, int num_ctas,
+                               int32_t* header, int32_t* cu, int32_t* counters, int32_t* err,
+                               cudaStream_t stream) {
+  decode_plan_kernel<<<1, 1024, 0, stream>>>(lens, batch, table_stride, num_ctas, kMaxKvHeads,
+                                             header, cu, counters, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_paged_decode(const DecodeParams& p, int num_ctas, cudaStream_t stream) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const size_t smem = decode_smem_bytes();
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    e = cudaFuncSetAttribute(paged_decode_kernel<kStages, kSets>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  paged_decode_kernel<kStages, kSets><<<num_ctas, kDecodeThreads, smem, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace tvp

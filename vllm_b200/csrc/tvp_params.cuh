@@ -1,0 +1,74 @@
+// Kernel parameter blocks of the paged-KV hot path and the launchers that
+// take them, shared by the kernel files and the C-ABI layer.
+#pragma once
+
+#include "tvp_common.cuh"
+
+namespace tvp {
+
+// K1 (tvp_append.cu)
+struct AppendParams {
+  __nv_bfloat16* k_pool;
+  __nv_bfloat16* v_pool;
+  long long layer_row_base;  // layer * num_pages * 16
+  int num_pages;
+  const int32_t* tables;
+  int table_stride;
+  int num_seqs;
+  const int32_t* token_seq;  // nullable: token i -> block-table row i
+  const int32_t* token_pos;
+  __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  __nv_bfloat16* q;
+  int kv_heads;
+  int q_heads;
+  int flags;
+  int32_t* err;
+};
+
+// K2 (tvp_decode.cu)
+struct DecodeParams {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k_pool;
+  const __nv_bfloat16* v_pool;
+  __nv_bfloat16* out;
+  const int32_t* tables;
+  const int32_t* seq_lens;
+  const int32_t* header;
+  const int32_t* cu;
+  int32_t* counters;
+  float* partials;
+  long long layer_row_base;  // layer * num_pages * 16
+  int num_pages;
+  int table_stride;
+  int batch;
+  float scale_log2;  // scale * log2(e)
+  int32_t* err;
+};
+
+// K2c (tvp_compat.cu)
+struct CompatParams {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k_pool;
+  const __nv_bfloat16* v_pool;
+  __nv_bfloat16* out;
+  const int32_t* tables;
+  const int32_t* seq_lens;
+  long long layer_row_base;
+  int num_pages;
+  int table_stride;
+  float scale;
+  int32_t* err;
+};
+
+// m[4], l[4], o[4][64] of one (split-K slot, KV head).
+constexpr int kPartialFloats = 2 * kGroup + kGroup * kHeadDim;
+
+cudaError_t launch_rope_append(const AppendParams& p, int num_tokens, cudaStream_t stream);
+cudaError_t launch_decode_plan(const int32_t* lens, int batch, int table_stride, int num_ctas,
+                               int32_t* header, int32_t* cu, int32_t* counters, int32_t* err,
+                               cudaStream_t stream);
+cudaError_t launch_paged_decode(const DecodeParams& p, int num_ctas, cudaStream_t stream);
+cudaError_t launch_compat_decode(const CompatParams& p, int batch, cudaStream_t stream);
+
+}  // namespace tvp

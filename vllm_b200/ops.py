@@ -1,0 +1,163 @@
+"""Operator layer over the C-ABI: the paged-KV kernels on torch CUDA tensors.
+
+torch is used only as plumbing (device memory and the current stream); every
+operation here is one call into ``libtvp_paged.so``.
+
+Shapes (reference geometry, src/model/paged_kvcache.cu:10-11):
+  k_pool, v_pool : bf16 [num_layers, num_pages, 16, kv_heads * 64]
+  block_tables   : int32 [batch, table_stride]   (-1 = no page)
+  seq_lens       : int32 [batch]                 attended length L per row
+  q, out         : bf16 [batch, 32 * 64]         head h at h * 64
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _native as N
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _need(t, name, dtype, device=None):
+    if t is None:
+        raise ValueError(f"{name} is required")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if device is not None and t.device != device:
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+
+
+def _pool_geometry(k_pool, v_pool):
+    _need(k_pool, "k_pool", torch.bfloat16)
+    _need(v_pool, "v_pool", torch.bfloat16, k_pool.device)
+    if k_pool.dim() != 4 or k_pool.shape != v_pool.shape or k_pool.shape[2] != N.PAGE_TOKENS \
+            or k_pool.shape[3] % N.HEAD_DIM:
+        raise ValueError("pools must be [num_layers, num_pages, 16, kv_heads*64] and equal")
+    num_layers, num_pages, _, kv_dim = k_pool.shape
+    return num_layers, num_pages, kv_dim // N.HEAD_DIM
+
+
+def new_error_word(device) -> torch.Tensor:
+    return torch.zeros(1, dtype=torch.int32, device=device)
+
+
+def rope_append(k_pool, v_pool, layer, block_tables, token_pos, k, v, q=None, token_seq=None,
+                rope_k=True, writeback_k=True, error=None, stream=None):
+    """K1: RoPE (q optional, k) + append of k, v rows into their page slots.
+
+    Token i goes to row ``token_seq[i]`` (default i) of ``block_tables`` at
+    position ``token_pos[i]``.  k is rotated in place when ``writeback_k``.
+    """
+    lib = N.load()
+    num_layers, num_pages, kv_heads = _pool_geometry(k_pool, v_pool)
+    dev = k_pool.device
+    _need(block_tables, "block_tables", torch.int32, dev)
+    _need(token_pos, "token_pos", torch.int32, dev)
+    _need(k, "k", torch.bfloat16, dev)
+    _need(v, "v", torch.bfloat16, dev)
+    n = token_pos.numel()
+    if k.shape != (n, kv_heads * N.HEAD_DIM) or v.shape != k.shape:
+        raise ValueError("k and v must be [num_tokens, kv_heads*64]")
+    flags = 0
+    if rope_k:
+        flags |= N.TVP_APPEND_ROPE_K
+    if writeback_k:
+        flags |= N.TVP_APPEND_WRITEBACK_K
+    q_heads = 0
+    if q is not None:
+        _need(q, "q", torch.bfloat16, dev)
+        if q.dim() != 2 or q.shape[0] != n or q.shape[1] % N.HEAD_DIM:
+            raise ValueError("q must be [num_tokens, q_heads*64]")
+        q_heads = q.shape[1] // N.HEAD_DIM
+        flags |= N.TVP_APPEND_ROPE_Q
+    if token_seq is not None:
+        _need(token_seq, "token_seq", torch.int32, dev)
+        if token_seq.numel() != n:
+            raise ValueError("token_seq must have one entry per token")
+    if block_tables.dim() != 2:
+        raise ValueError("block_tables must be [rows, table_stride]")
+    rc = lib.tvp_rope_append(_ptr(k_pool), _ptr(v_pool), num_pages, num_layers, layer, kv_heads,
+                             _ptr(block_tables), block_tables.shape[1], block_tables.shape[0],
+                             _ptr(token_seq), _ptr(token_pos), n, _ptr(k), _ptr(v), _ptr(q),
+                             q_heads, flags, _ptr(error), _stream(stream))
+    N.check(rc, "tvp_rope_append")
+
+
+class DecodeWorkspace:
+    """Device workspace of the decode path for up to ``max_batch`` rows and a
+    fixed grid (``num_ctas`` CTAs, 0 = one per SM)."""
+
+    def __init__(self, max_batch: int, device=None, num_ctas: int = 0):
+        lib = N.load()
+        device = torch.device(device if device is not None else "cuda")
+        with torch.cuda.device(device):
+            sms = ctypes.c_int(0)
+            N.check(lib.tvp_device_sm_count(ctypes.byref(sms)), "tvp_device_sm_count")
+            self.num_ctas = num_ctas if num_ctas > 0 else sms.value
+            self.nbytes = int(lib.tvp_decode_workspace_bytes(max_batch, N.KV_HEADS, self.num_ctas))
+        if self.nbytes == 0:
+            raise ValueError("invalid workspace request")
+        self.max_batch = max_batch
+        self.buffer = torch.empty(self.nbytes, dtype=torch.uint8, device=device)
+        self.batch = None
+
+
+def decode_plan(seq_lens, table_stride, workspace: DecodeWorkspace, error=None, stream=None):
+    """Plan of one decode step (page prefix sums, split-K counters)."""
+    lib = N.load()
+    _need(seq_lens, "seq_lens", torch.int32, workspace.buffer.device)
+    batch = seq_lens.numel()
+    if batch > workspace.max_batch:
+        raise ValueError("batch larger than the workspace was sized for")
+    workspace.nbytes_needed = int(lib.tvp_decode_workspace_bytes(batch, N.KV_HEADS, workspace.num_ctas))
+    rc = lib.tvp_decode_plan(_ptr(seq_lens), batch, table_stride, N.KV_HEADS, workspace.num_ctas,
+                             _ptr(workspace.buffer), workspace.nbytes, _ptr(error), _stream(stream))
+    N.check(rc, "tvp_decode_plan")
+    workspace.batch = batch
+
+
+def paged_decode_attention(q, k_pool, v_pool, layer, block_tables, seq_lens, workspace=None,
+                           out=None, scale=0.125, mode=N.TVP_MODE_FAST, error=None, stream=None):
+    """K2: out = softmax(scale q K^T) V over each row's pages, read in place.
+
+    FAST mode needs ``workspace`` planned by :func:`decode_plan` for these lengths.
+    """
+    lib = N.load()
+    num_layers, num_pages, kv_heads = _pool_geometry(k_pool, v_pool)
+    dev = k_pool.device
+    _need(q, "q", torch.bfloat16, dev)
+    _need(block_tables, "block_tables", torch.int32, dev)
+    _need(seq_lens, "seq_lens", torch.int32, dev)
+    batch = seq_lens.numel()
+    if q.shape != (batch, kv_heads * N.GQA_GROUP * N.HEAD_DIM):
+        raise ValueError("q must be [batch, 32*64]")
+    if block_tables.dim() != 2 or block_tables.shape[0] < batch:
+        raise ValueError("block_tables must be [>=batch, table_stride]")
+    if out is None:
+        out = torch.empty_like(q)
+    _need(out, "out", torch.bfloat16, dev)
+    ws_ptr, ws_bytes, ctas = None, 0, 0
+    if mode == N.TVP_MODE_FAST:
+        if workspace is None or workspace.batch != batch:
+            raise ValueError("FAST mode needs a workspace planned for this batch")
+        ws_ptr, ws_bytes, ctas = _ptr(workspace.buffer), workspace.nbytes, workspace.num_ctas
+    rc = lib.tvp_paged_decode_attention(_ptr(q), _ptr(k_pool), _ptr(v_pool), num_pages, num_layers,
+                                        layer, kv_heads, kv_heads * N.GQA_GROUP,
+                                        _ptr(block_tables), block_tables.shape[1], _ptr(seq_lens),
+                                        batch, float(scale), mode, ctas, ws_ptr, ws_bytes,
+                                        _ptr(out), _ptr(error), _stream(stream))
+    N.check(rc, "tvp_paged_decode_attention")
+    return out
