@@ -66,13 +66,13 @@ def algorithmic_bytes(lens: np.ndarray) -> dict:
     return {"kv": kv, "q_out": qo, "tables": tables, "total": kv + qo + tables}
 
 
-def config_block(world, batch):
+def config_block(world, batch, layers=16):
     return {
         "workload": "decode_sweep",
         "rows_per_gpu": batch,
         "global_rows": batch * world,
         "seq_len": "L ~ U[512, 8192] (seed 4)",
-        "layers": 16,
+        "layers": layers,
         "q_heads": 32,
         "kv_heads": 8,
         "head_dim": 64,
@@ -150,7 +150,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.gpu), "-lms", "200"], stdout=subprocess.PIPE,
+                 "-i", str(self.gpu), "-lms", "100"], stdout=subprocess.PIPE,
                 stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -198,6 +198,7 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     case = W.decode_sweep(seed=4, batch=args.rows)
+    case.num_layers = args.layers
     B, P, layers = case.batch, case.num_pages, case.num_layers
     lens = case.lens
     gen = torch.Generator(device=dev)
@@ -323,12 +324,12 @@ def run_ours(args, rank, world, local_rank):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) BF16 K/V/q, seeded lengths and page scatter)",
-        "config": config_block(world, B),
+        "config": config_block(world, B, layers),
         "decode_tok_s": round(tok_s, 1),
         "hbm_peak_frac": round(value / world / peak, 4),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": "tvp::paged_decode_kernel<6,2>",
+                     "kernel": "tvp::paged_decode_kernel<7,1,true>",
                      "algorithmic_bytes_per_launch": nbytes["total"],
                      "avg_launch_ms": round(attn_ms, 4), "peak_source": f"{peak_kind} hbm_gbs"},
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
@@ -475,10 +476,11 @@ def bench_decode_small(dev, iters=50):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--rows", type=int, default=256)
+    ap.add_argument("--rows", type=int, default=256, help="decode rows per GPU (256)")
+    ap.add_argument("--layers", type=int, default=16, help="layers per step (16)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true")

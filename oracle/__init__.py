@@ -179,3 +179,24 @@ def decode_attention_f64(q, k_pool, v_pool, layer, tables, lens, scale=0.125, th
 
 def max_threads() -> int:
     return int(load().orc_max_threads())
+
+
+def rope_close(got: np.ndarray, expect: np.ndarray, rope_input: np.ndarray,
+               max_mismatch_frac: float = 0.005) -> tuple[bool, dict]:
+    """Compares RoPE outputs (bf16 bits) of two implementations whose FP32
+    sin/cos/pow may differ in the last bit.  An element may differ by one BF16
+    ulp at the scale of its input pair, |x| + |y| (the rotation's magnitude),
+    which allows multi-ulp bit differences only for outputs near a zero
+    crossing; at most `max_mismatch_frac` of elements may differ at all."""
+    got = np.ascontiguousarray(got, np.uint16)
+    expect = np.ascontiguousarray(expect, np.uint16)
+    x = bf16_to_f32(rope_input).astype(np.float64)
+    cols = np.arange(x.shape[-1])
+    partner = (cols // 64) * 64 + (cols % 64 + 32) % 64
+    mag = np.abs(x) + np.abs(x[..., partner])
+    err = np.abs(bf16_to_f32(got).astype(np.float64) - bf16_to_f32(expect).astype(np.float64))
+    within = err <= mag * 2.0 ** -7 + 1e-6
+    frac = float((got != expect).mean())
+    ok = bool(within.all()) and frac <= max_mismatch_frac
+    return ok, {"max_abs_err": float(err.max()) if err.size else 0.0, "mismatch_frac": frac,
+                "outside": int((~within).sum())}

@@ -61,8 +61,6 @@ def test_prefill_append_bit_exact_vs_reference(ref_lib):
                                               i32p(table), table.size, 0, vp(rk), vp(v), T) == 0
             assert torch.equal(k.view(torch.int16), rk.view(torch.int16)), "RoPE(K) bits"
             assert torch.equal(q.view(torch.int16), rq.view(torch.int16)), "RoPE(q) bits"
-        for s in seqs:
-            pass
     torch.cuda.synchronize()
     assert torch.equal(k_pool.view(torch.int16), ref_k.view(torch.int16)), "K pages"
     assert torch.equal(v_pool.view(torch.int16), ref_v.view(torch.int16)), "V pages"
@@ -151,9 +149,8 @@ def test_append_against_cpu_oracle():
                     token_seq=torch.zeros(T, dtype=torch.int32, device="cuda"))
     ours = host_bf16(kd)
     cpu = oracle.rope(kn, positions=pos)
-    diff = np.abs(ours.astype(np.int32) - cpu.astype(np.int32))
-    assert diff.max() <= 1, "more than one BF16 ulp from the libm restatement"
-    assert (diff > 0).mean() < 0.01
+    ok, stats = oracle.rope_close(ours, cpu, kn)
+    assert ok, stats
 
 
 def _cache_values(layer, positions, is_v):

@@ -1,0 +1,79 @@
+"""Multi-process host logic of the multi-GPU decode path, on CPU (gloo,
+world size 2): request sharding covers every row exactly once and balances the
+attended tokens; the bench's max-over-ranks timing reduction."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import workloads as W
+from vllm_b200 import sharding
+
+
+def test_request_shards_partition_and_balance():
+    lens = W.sweep_lengths(4)
+    for world in (1, 2, 4, 8):
+        shards = sharding.shard_by_request(lens, world)
+        allrows = np.concatenate(shards)
+        assert sorted(allrows.tolist()) == list(range(lens.size))
+        assert sharding.imbalance(lens, shards) < 1.0 + lens.max() / (lens.sum() / world)
+        assert sharding.imbalance(lens, shards) < 1.01
+
+
+def test_kv_head_shards():
+    assert [list(r) for r in sharding.shard_by_kv_head(8)] == [[i] for i in range(8)]
+    assert [list(r) for r in sharding.shard_by_kv_head(2)] == [[0, 1, 2, 3], [4, 5, 6, 7]]
+    with pytest.raises(ValueError):
+        sharding.shard_by_kv_head(3)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import torch
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        lens = W.sweep_lengths(4)
+        mine = sharding.shard_by_request(lens, world)[rank]
+        # every rank derives the same partition on its own: gather and compare
+        gathered = [None] * world
+        dist.all_gather_object(gathered, mine.tolist())
+        # bench timing reduction: max over ranks
+        t = torch.tensor([10.0 + rank], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        results[rank] = (gathered, float(t.item()), int(lens[mine].sum()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gloo_partition_agreement_and_max_timing():
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    g0, t0, load0 = results[0]
+    g1, t1, load1 = results[1]
+    assert g0 == g1
+    rows = sorted(g0[0] + g0[1])
+    assert rows == list(range(256))
+    assert t0 == t1 == 11.0
+    assert abs(load0 - load1) <= 8192

@@ -153,6 +153,8 @@ int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const 
     return TVP_ERR_INVALID_ARGUMENT;
   if (kv_heads != kMaxKvHeads || q_heads != kMaxKvHeads * kGroup) return TVP_ERR_UNSUPPORTED;
   if (mode != TVP_MODE_FAST && mode != TVP_MODE_COMPAT) return TVP_ERR_UNSUPPORTED;
+  // TMA row coordinates are 32-bit: the pools may hold at most 2^31 - 1 token rows.
+  if ((long long)num_layers * num_pages * kPage > 0x7fffffffLL) return TVP_ERR_UNSUPPORTED;
   if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(q, 4) || !aligned(out, 16))
     return TVP_ERR_INVALID_ARGUMENT;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -195,7 +197,7 @@ int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const 
   p.batch = batch;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = d_error;
-  return map_cuda(launch_paged_decode(p, ctas, st));
+  return map_cuda(launch_paged_decode(p, (long long)num_layers * num_pages * kPage, ctas, st));
 }
 
 }  // extern "C"

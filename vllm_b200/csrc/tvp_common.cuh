@@ -2,6 +2,7 @@
 // bulk-copy (TMA) and warp-level tensor-core primitives for sm_100a.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -79,6 +80,22 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uin
           dst),
       "l"(src), "r"(bytes), "r"(bar)
       : "memory");
+}
+
+// ---- tiled TMA load of a 2-D box (tensor map, no multicast) ---------------
+// x is the innermost (element) coordinate; x * sizeof(element) must be a
+// multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensor_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
 // Orders this thread's generic-proxy shared-memory writes before later

@@ -11,30 +11,36 @@
 //
 // Work split.  The plan kernel turns the attended lengths into page prefix
 // sums cu[0..B].  The T = cu[B] pages of the step, laid end to end, are cut
-// into gridDim.x contiguous ranges of floor/ceil(T / C) pages, one per CTA, so
-// every CTA streams the same number of pages whatever the length mix.  A range
+// into C = min(gridDim.x, T) contiguous ranges of floor/ceil(T / C) pages, one
+// per CTA, so every CTA streams the same number of pages whatever the length
+// mix (CTAs past C have no pages).  A range
 // covers whole sequences ("complete pieces", finalised in place) and at most
 // two sequence fragments at its ends ("partial pieces"); partials go to the
 // workspace and the last CTA to finish a sequence merges them (a counter per
 // (sequence, KV head), no waiting).
 //
 // CTA layout: one producer warp and SETS x 8 consumer warps.  The producer
-// streams one page (all 8 KV heads, 16 rows x 1 KiB of K and of V) per stage
-// into shared memory with bulk copies (cp.async.bulk, one per 1 KiB row, so each
-// row can land at a 1040-byte pitch that keeps ldmatrix conflict-free).
+// streams one page per stage into shared memory with tiled TMA loads: per KV
+// head one 2 KiB box {64 channels x 16 tokens} of K and one of V, through 2-D
+// tensor maps over the pools (rows of 512 channels), 128-byte swizzled so that
+// the consumers' ldmatrix reads of 8 tokens hit 8 different bank groups.  A
+// box is the largest unit that is contiguous in a page *and* swizzlable;
+// one bulk copy per 1 KiB token row streamed at only ~4.4 TB/s on B200,
+// these boxes stream at the copy roofline.
 // Consumer warp g of set s owns KV head g on the pages k with k % SETS == s.
 // Per page it forms S^T = K_g Q_g^T (16 tokens x 8 query columns, 4 real) and
 // O^T += V_g^T P^T with mma.m16n8k16 (BF16 in, FP32 accumulate), running an
 // online softmax in base 2 on the accumulator fragments; P^T is turned from
 // accumulator layout into operand layout with movmatrix.
+#include <cudaTypedefs.h>
+
 #include "tvp_params.cuh"
 
 namespace tvp {
 
 constexpr int kPlanMagic = 0x54565031;  // "TVP1"
-constexpr int kRowBytes = kMaxKvHeads * kHeadDim * 2;      // 1024: one token of one pool
-constexpr int kPitch = kRowBytes + 16;                      // shared-memory row pitch
-constexpr int kStageBytes = 2 * kPage * kPitch;             // K rows then V rows
+constexpr int kTileBytes = kPage * kHeadDim * 2;            // 2048: one KV head of one page
+constexpr int kStageBytes = 2 * kMaxKvHeads * kTileBytes;   // 8 K tiles, then 8 V tiles
 constexpr int kMergeFields = 20;                            // m0 m1 l0 l1 acc[16]
 
 
@@ -143,10 +149,20 @@ __device__ void combine_sequence(const DecodeParams& p, int s, int first, int en
   *reinterpret_cast<uint4*>(dst) = packed;
 }
 
-template <int STAGES, int SETS>
+// LAZY: keep the running maximum unless a score exceeds it by more than
+// kLazyMargin (base-2 exponent units).  Probabilities then stay below
+// 2^kLazyMargin (exact in FP32/BF16 range), and the cross-lane max reduction,
+// the rescale factors and the accumulator rescale leave the common path; they
+// run on the first page of a piece and when a page brings a new maximum.
+constexpr float kLazyMargin = 8.f;
+
+template <int STAGES, int SETS, bool LAZY>
 __global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
-    paged_decode_kernel(const DecodeParams p) {
-  extern __shared__ __align__(1024) unsigned char smem[];
+    paged_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap k_map,
+                        const __grid_constant__ CUtensorMap v_map) {
+  // The 128-byte swizzle pattern repeats every 1 KiB: tiles start 1 KiB aligned.
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   const int T_header_ok = (p.header[0] == kPlanMagic && p.header[1] == p.batch &&
                            p.header[2] == (int)gridDim.x && p.header[3] == kMaxKvHeads);
   if (!T_header_ok) {
@@ -157,9 +173,11 @@ __global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
   uint64_t* empty_bar = full_bar + STAGES;
   int* stage_ok = reinterpret_cast<int*>(empty_bar + STAGES);
   volatile int* abort_flag = stage_ok + STAGES;
+  // Set-merge scratch (only with two consumer sets).
   float* merge = reinterpret_cast<float*>(smem + STAGES * kStageBytes + 2 * STAGES * 8 +
                                           (STAGES + 4) * 4);
   merge = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(merge) + 15) & ~uintptr_t(15));
+  (void)merge;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -172,9 +190,13 @@ __global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
   }
   __syncthreads();
 
-  const long long C = gridDim.x, c = blockIdx.x;
+  // Only min(grid, T) CTAs take pages, so that every range holds at least one
+  // page and the pieces of a sequence are exactly the CTAs c0..c1 it spans.
   const long long T = p.cu[p.batch];
-  const int p_begin = (int)(c * T / C), p_end = (int)((c + 1) * T / C);
+  const long long C = T < (long long)gridDim.x ? T : (long long)gridDim.x;
+  const long long c = blockIdx.x;
+  const int p_begin = c < C ? (int)(c * T / C) : 0;
+  const int p_end = c < C ? (int)((c + 1) * T / C) : 0;
   const uint32_t smem_base = smem_addr(smem);
 
   // First sequence of the range: the s with cu[s] <= p_begin < cu[s + 1].
@@ -190,39 +212,60 @@ __global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
 
   if (warp == SETS * kMaxKvHeads) {
     // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      prefetch_tensor_map(&k_map);
+      prefetch_tensor_map(&v_map);
+    }
+    // The page walk (sequence s, its first page and end) lives in registers
+    // and the next page id is loaded one iteration ahead, so nothing but the
+    // empty-slot wait sits between a slot being freed and its refill.
     int s = s0;
-    int kk = 0;
-    for (int pg = p_begin; pg < p_end; ++pg, ++kk) {
-      while (pg >= __ldg(p.cu + s + 1)) ++s;
-      const int j = pg - __ldg(p.cu + s);
-      const int stage = kk % STAGES;
-      int stop = 0;
-      if (lane == 0) {
-        if (kk >= STAGES && !*abort_flag &&
-            !mbar_wait_bounded(smem_addr(&empty_bar[stage]), ((kk / STAGES) - 1) & 1)) {
-          *abort_flag = 1;
-          record_error(p.err, TVP_DEVERR_TIMEOUT);
+    int seq_first = 0, seq_end = 0;
+    if (p_begin < p_end) {
+      seq_first = __ldg(p.cu + s);
+      seq_end = __ldg(p.cu + s + 1);
+    }
+    int next_phys = p_begin < p_end
+                        ? __ldg(p.tables + (size_t)s * p.table_stride + (p_begin - seq_first))
+                        : 0;
+    for (int pg = p_begin, kk = 0; pg < p_end; ++pg, ++kk) {
+      const int phys = next_phys;
+      if (pg + 1 < p_end) {
+        while (pg + 1 >= seq_end) {
+          ++s;
+          seq_first = seq_end;
+          seq_end = __ldg(p.cu + s + 1);
         }
-        stop = *abort_flag;
+        next_phys = __ldg(p.tables + (size_t)s * p.table_stride + (pg + 1 - seq_first));
       }
-      if (__shfl_sync(0xffffffffu, stop, 0)) break;
-      const int phys = __ldg(p.tables + (size_t)s * p.table_stride + j);
+      const int stage = kk % STAGES;
+      if (kk >= STAGES) {
+        int timed_out = 0;
+        if (lane == 0)
+          timed_out = !mbar_wait_bounded(smem_addr(&empty_bar[stage]), ((kk / STAGES) - 1) & 1);
+        if (__shfl_sync(0xffffffffu, timed_out, 0)) {
+          if (lane == 0) {
+            *abort_flag = 1;
+            record_error(p.err, TVP_DEVERR_TIMEOUT);
+          }
+          break;
+        }
+      }
       const bool ok = phys >= 0 && phys < p.num_pages;
       const uint32_t full = smem_addr(&full_bar[stage]);
       if (lane == 0) {
         stage_ok[stage] = ok ? 1 : 0;
         if (!ok) record_error(p.err, TVP_DEVERR_BAD_PAGE);
-        mbar_arrive_expect_tx(full, ok ? 2u * kPage * kRowBytes : 0u);
+        mbar_arrive_expect_tx(full, ok ? (uint32_t)kStageBytes : 0u);
       }
       __syncwarp();
-      if (ok) {
-        const int row = lane & (kPage - 1);
-        const __nv_bfloat16* pool = lane < kPage ? p.k_pool : p.v_pool;
-        const __nv_bfloat16* src =
-            pool + (size_t)(p.layer_row_base + (long long)phys * kPage + row) * (kRowBytes / 2);
-        const uint32_t dst = smem_base + stage * kStageBytes + (lane < kPage ? 0 : kPage * kPitch) +
-                             row * kPitch;
-        bulk_copy_g2s(dst, src, kRowBytes, full);
+      if (ok && lane < 2 * kMaxKvHeads) {
+        // lanes 0-7: K box of head `lane`; lanes 8-15: V box of head `lane - 8`
+        const int h = lane & (kMaxKvHeads - 1);
+        const uint32_t dst = smem_base + stage * kStageBytes +
+                             (lane < kMaxKvHeads ? 0 : kMaxKvHeads * kTileBytes) + h * kTileBytes;
+        tma_load_2d(dst, lane < kMaxKvHeads ? &k_map : &v_map, h * kHeadDim,
+                    (int)(p.layer_row_base + (long long)phys * kPage), full);
       }
     }
     return;
@@ -234,9 +277,13 @@ __global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
   const int tr = lane >> 2;   // accumulator row (token) of this lane
   const int hc = lane & 3;    // accumulator column pair (query heads 2hc, 2hc+1)
   const int mat = lane >> 3, mrow = lane & 7;
-  // ldmatrix row addresses (bytes within a stage) for this lane.
-  const uint32_t k_lane = (mrow + (mat & 1) * 8) * kPitch + g * 128 + (mat >> 1) * 16;
-  const uint32_t v_lane = kPage * kPitch + (mrow + (mat >> 1) * 8) * kPitch + g * 128 + (mat & 1) * 16;
+  // ldmatrix row addresses (bytes within a stage) for this lane.  Tile rows are
+  // 128 B (one token of head g); 16-byte chunk c of row r sits at chunk c ^ (r % 8).
+  // K (A operand of S^T = K Q^T): matrix m covers tokens 8*(m&1).., chunk 2*k4+(m>>1).
+  // V (A operand of O^T = V^T P^T, transposed load): tokens 8*(m>>1).., chunk 2*d+(m&1).
+  const uint32_t k_lane = g * kTileBytes + (mrow + (mat & 1) * 8) * 128;
+  const uint32_t v_lane = kMaxKvHeads * kTileBytes + g * kTileBytes + (mrow + (mat >> 1) * 8) * 128;
+  const int k_chunk = mat >> 1, v_chunk = mat & 1;
   constexpr int kOutRow = kMaxKvHeads * kGroup * kHeadDim;  // 2048
 
   // Rows of length 0 attend to nothing: their output is zero.
@@ -286,51 +333,78 @@ __global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
         *abort_flag = 1;
         record_error(p.err, TVP_DEVERR_TIMEOUT);
       }
+      // Pull this head's K and V fragments of the page into registers, then
+      // release the stage at once: the producer refills it while the math runs,
+      // so almost every stage stays in flight (a fetch takes ~4 us at full load).
+      const bool have = ready && stage_ok[stage];
       bool zeroed = false;
-      if (ready && stage_ok[stage]) {
+      int valid = kPage;
+      uint32_t kf[4][4], vf[4][4];
+      if (have) {
         const int j = pg - first + i;
-        const int valid = min(kPage, L - j * kPage);
+        valid = min(kPage, L - j * kPage);
         const uint32_t sb = smem_base + stage * kStageBytes;
         if (valid < kPage) {
           // Rows past the sequence end hold stale data: zero this head's V slice
           // so that 0-probability rows cannot inject NaN/Inf into P.V.
-          unsigned char* vbase = smem + stage * kStageBytes + kPage * kPitch + g * 128;
+          unsigned char* vtile = smem + stage * kStageBytes + (kMaxKvHeads + g) * kTileBytes;
           for (int idx = lane; idx < (kPage - valid) * 8; idx += 32) {
-            const int r = valid + (idx >> 3);
-            *reinterpret_cast<uint4*>(vbase + r * kPitch + (idx & 7) * 16) = make_uint4(0, 0, 0, 0);
+            const int r = valid + (idx >> 3);  // whole 128-byte rows: swizzle-agnostic
+            *reinterpret_cast<uint4*>(vtile + r * 128 + (idx & 7) * 16) = make_uint4(0, 0, 0, 0);
           }
           zeroed = true;
           __syncwarp();
         }
-        // S^T = K_g Q_g^T
-        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4) {
-          uint32_t a0, a1, a2, a3;
-          ldmatrix_x4(sb + k_lane + k4 * 32, a0, a1, a2, a3);
-          mma_bf16_16816(s0, s1, s2, s3, a0, a1, a2, a3, qb[k4][0], qb[k4][1]);
+        for (int k4 = 0; k4 < 4; ++k4)
+          ldmatrix_x4(sb + k_lane + (((2 * k4 + k_chunk) ^ mrow) << 4), kf[k4][0], kf[k4][1],
+                      kf[k4][2], kf[k4][3]);
+#pragma unroll
+        for (int d = 0; d < 4; ++d)
+          ldmatrix_x4_trans(sb + v_lane + (((2 * d + v_chunk) ^ mrow) << 4), vf[d][0], vf[d][1],
+                            vf[d][2], vf[d][3]);
+      }
+      if (zeroed) fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&empty_bar[stage]));
+      if (have) {
+        // S^T = K_g Q_g^T, as two independent accumulation chains (k 0-31, 32-63)
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
+#pragma unroll
+        for (int k4 = 0; k4 < 2; ++k4) {
+          mma_bf16_16816(s0, s1, s2, s3, kf[k4][0], kf[k4][1], kf[k4][2], kf[k4][3], qb[k4][0],
+                         qb[k4][1]);
+          mma_bf16_16816(t0, t1, t2, t3, kf[k4 + 2][0], kf[k4 + 2][1], kf[k4 + 2][2],
+                         kf[k4 + 2][3], qb[k4 + 2][0], qb[k4 + 2][1]);
         }
-        float x0 = s0 * p.scale_log2, x1 = s1 * p.scale_log2;
-        float x2 = s2 * p.scale_log2, x3 = s3 * p.scale_log2;
+        float x0 = (s0 + t0) * p.scale_log2, x1 = (s1 + t1) * p.scale_log2;
+        float x2 = (s2 + t2) * p.scale_log2, x3 = (s3 + t3) * p.scale_log2;
         if (valid < kPage) {
           if (tr >= valid) x0 = x1 = -INFINITY;
           if (tr + 8 >= valid) x2 = x3 = -INFINITY;
         }
         float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+        const bool grow = !LAZY || __any_sync(0xffffffffu, mx0 > m0 + kLazyMargin ||
+                                                              mx1 > m1 + kLazyMargin);
+        float al0 = 1.f, al1 = 1.f;
+        if (grow) {
 #pragma unroll
-        for (int o = 4; o < 32; o <<= 1) {
-          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+          for (int o = 4; o < 32; o <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+          }
+          const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+          al0 = exp2f(m0 - mn0);
+          al1 = exp2f(m1 - mn1);
+          m0 = mn0;
+          m1 = mn1;
         }
-        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-        const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
-        m0 = mn0;
-        m1 = mn1;
-        const uint32_t pa = pack_bf16x2(exp2f(x0 - mn0), exp2f(x1 - mn1));
-        const uint32_t pb = pack_bf16x2(exp2f(x2 - mn0), exp2f(x3 - mn1));
+        const uint32_t pa = pack_bf16x2(exp2f(x0 - m0), exp2f(x1 - m1));
+        const uint32_t pb = pack_bf16x2(exp2f(x2 - m0), exp2f(x3 - m1));
         l0 = l0 * al0 + (bf16lo_to_f32(pa) + bf16lo_to_f32(pb));
         l1 = l1 * al1 + (bf16hi_to_f32(pa) + bf16hi_to_f32(pb));
-        if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
+        if (grow && __any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
 #pragma unroll
           for (int d = 0; d < 4; ++d) {
             acc[d][0] *= al0; acc[d][1] *= al1; acc[d][2] *= al0; acc[d][3] *= al1;
@@ -339,15 +413,10 @@ __global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
         // O^T += V_g^T P^T
         const uint32_t y0 = movmatrix_trans(pa), y1 = movmatrix_trans(pb);
 #pragma unroll
-        for (int d = 0; d < 4; ++d) {
-          uint32_t a0, a1, a2, a3;
-          ldmatrix_x4_trans(sb + v_lane + d * 32, a0, a1, a2, a3);
-          mma_bf16_16816(acc[d][0], acc[d][1], acc[d][2], acc[d][3], a0, a1, a2, a3, y0, y1);
-        }
+        for (int d = 0; d < 4; ++d)
+          mma_bf16_16816(acc[d][0], acc[d][1], acc[d][2], acc[d][3], vf[d][0], vf[d][1], vf[d][2],
+                         vf[d][3], y0, y1);
       }
-      if (zeroed) fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&empty_bar[stage]));
     }
 
     if (SETS > 1) {
@@ -442,13 +511,17 @@ __global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
   }
 }
 
-constexpr int kStages = 6;
-constexpr int kSets = 2;
+// One consumer set (8 warps, one per KV head) and 7 stages of 32 KiB: 224 KiB
+// of pages in flight per SM, which is what a B200 needs to stream at its HBM
+// roofline with ~4 us fetch latency under load.
+constexpr int kStages = 7;
+constexpr int kSets = 1;
+constexpr bool kLazy = true;
 constexpr int kDecodeThreads = (kSets * kMaxKvHeads + 1) * 32;
 
 size_t decode_smem_bytes() {
-  return (size_t)kStages * kStageBytes + 2 * kStages * 8 + (kStages + 4) * 4 + 16 +
-         (size_t)kMaxKvHeads * kMergeFields * 32 * 4;
+  return 1024 /* alignment slack */ + (size_t)kStages * kStageBytes + 2 * kStages * 8 +
+         (kStages + 4) * 4 + 16 + (kSets > 1 ? (size_t)kMaxKvHeads * kMergeFields * 32 * 4 : 0);
 }
 
 cudaError_t launch_decode_plan(const int32_t* lens, int batch, int table_stride, int num_ctas,
@@ -459,19 +532,76 @@ cudaError_t launch_decode_plan(const int32_t* lens, int batch, int table_stride,
   return cudaGetLastError();
 }
 
-cudaError_t launch_paged_decode(const DecodeParams& p, int num_ctas, cudaStream_t stream) {
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool resolved = false;
+  if (!resolved) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    resolved = true;
+  }
+  return fn;
+}
+
+// Tensor map over one pool viewed as `rows` rows of 512 BF16 channels (1 KiB
+// pitch); box = 64 channels (one KV head, 128 B) x 16 rows (one page), 128-byte
+// swizzle.  Recently used maps are kept per thread (encoding is host work).
+bool pool_tensor_map(const void* pool, long long rows, CUtensorMap* out) {
+  struct Entry {
+    const void* pool;
+    long long rows;
+    CUtensorMap map;
+  };
+  static thread_local Entry cache[4];
+  static thread_local int next = 0;
+  for (const Entry& e : cache)
+    if (e.pool == pool && e.rows == rows) {
+      *out = e.map;
+      return true;
+    }
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)(kMaxKvHeads * kHeadDim), (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(kMaxKvHeads * kHeadDim * 2)};
+  const cuuint32_t box[2] = {(cuuint32_t)kHeadDim, (cuuint32_t)kPage};
+  const cuuint32_t elem_strides[2] = {1, 1};
+  CUtensorMap map;
+  if (encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(pool), dims, strides,
+             box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  cache[next] = {pool, rows, map};
+  next = (next + 1) % 4;
+  *out = map;
+  return true;
+}
+
+}  // namespace
+
+cudaError_t launch_paged_decode(const DecodeParams& p, long long pool_rows, int num_ctas,
+                                cudaStream_t stream) {
   static bool configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const size_t smem = decode_smem_bytes();
   if (dev < 0 || dev >= 64 || !configured[dev]) {
-    e = cudaFuncSetAttribute(paged_decode_kernel<kStages, kSets>,
+    e = cudaFuncSetAttribute(paged_decode_kernel<kStages, kSets, kLazy>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  paged_decode_kernel<kStages, kSets><<<num_ctas, kDecodeThreads, smem, stream>>>(p);
+  CUtensorMap k_map, v_map;
+  if (!pool_tensor_map(p.k_pool, pool_rows, &k_map) ||
+      !pool_tensor_map(p.v_pool, pool_rows, &v_map))
+    return cudaErrorInvalidValue;
+  paged_decode_kernel<kStages, kSets, kLazy><<<num_ctas, kDecodeThreads, smem, stream>>>(p, k_map, v_map);
   return cudaGetLastError();
 }
 

@@ -68,7 +68,8 @@ cudaError_t launch_rope_append(const AppendParams& p, int num_tokens, cudaStream
 cudaError_t launch_decode_plan(const int32_t* lens, int batch, int table_stride, int num_ctas,
                                int32_t* header, int32_t* cu, int32_t* counters, int32_t* err,
                                cudaStream_t stream);
-cudaError_t launch_paged_decode(const DecodeParams& p, int num_ctas, cudaStream_t stream);
+cudaError_t launch_paged_decode(const DecodeParams& p, long long pool_rows, int num_ctas,
+                                cudaStream_t stream);
 cudaError_t launch_compat_decode(const CompatParams& p, int batch, cudaStream_t stream);
 
 }  // namespace tvp
