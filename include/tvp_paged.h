@@ -140,6 +140,35 @@ int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const 
                                int num_ctas, void* d_workspace, size_t workspace_bytes,
                                tvp_bf16* out, int32_t* d_error, tvp_stream_t stream);
 
+/*
+ * K2 without any allocation.  This entry point has no counterpart in the
+ * reference.  It is for callers that cannot call cudaMalloc: code whose
+ * device memory is owned by a host framework's pool, plug-ins running under a
+ * fixed memory budget, and threads that must not take the device-wide
+ * synchronisation cudaMalloc/cudaFree can imply.  It runs tvp_decode_plan and
+ * tvp_paged_decode_attention (FAST mode) on a workspace kept in a 4 MiB device
+ * array inside this library; that array stays resident on every GPU that
+ * loads the library until the process exits.  Inputs and outputs are the
+ * caller's, exactly as for tvp_paged_decode_attention.
+ *   - Returns TVP_ERR_WORKSPACE when batch and grid (num_ctas, 0 = one CTA per
+ *     SM) need more than 4 MiB of workspace (with one CTA per SM of a B200:
+ *     batches beyond about 40,000 rows).
+ *   - The first call on a device resolves the array's device address on that
+ *     device (cudaGetSymbolAddress); make that first call before any stream
+ *     capture.
+ *   - Every call uses the same array: calls that can overlap on the GPU (other
+ *     streams, other host threads on the same device) race and must be
+ *     serialised by the caller.  Each call re-plans, so no state from an
+ *     earlier call is read.
+ */
+int tvp_paged_decode_attention_noalloc(const tvp_bf16* q, const tvp_bf16* k_pool,
+                                       const tvp_bf16* v_pool, int num_pages, int num_layers,
+                                       int layer, int kv_heads, int q_heads,
+                                       const int32_t* d_block_tables, int table_stride,
+                                       const int32_t* d_seq_lens, int batch, float scale,
+                                       int num_ctas, tvp_bf16* out, int32_t* d_error,
+                                       tvp_stream_t stream);
+
 /* ======================================================================= *
  * Host API mirror: PagedKVCache / SequenceKVState / PagedBatchMetadata.
  * Same allocator semantics as src/model/paged_kvcache.cu:65-145 (LIFO free

@@ -59,6 +59,10 @@ _SIGNATURES = {
                                            c_int, c_int, c_void_p, c_int, c_void_p, c_int,
                                            c_float, c_int, c_int, c_void_p, c_size_t, c_void_p,
                                            c_void_p, c_void_p]),
+    "tvp_paged_decode_attention_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                                   c_int, c_int, c_int, c_void_p, c_int, c_void_p,
+                                                   c_int, c_float, c_int, c_void_p, c_void_p,
+                                                   c_void_p]),
     "tvp_cache_create": (c_int, [c_int, c_int, c_int, c_int, c_int, POINTER(c_void_p)]),
     "tvp_cache_destroy": (None, [c_void_p]),
     "tvp_cache_pools": (c_int, [c_void_p, POINTER(c_void_p), POINTER(c_void_p), POINTER(c_int)]),
