@@ -329,7 +329,7 @@ def run_ours(args, rank, world, local_rank):
         "hbm_peak_frac": round(value / world / peak, 4),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": "tvp::paged_decode_kernel<7,1,true>",
+                     "kernel": "tvp::paged_decode_kernel<7,2,true,true>",
                      "algorithmic_bytes_per_launch": nbytes["total"],
                      "avg_launch_ms": round(attn_ms, 4), "peak_source": f"{peak_kind} hbm_gbs"},
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,

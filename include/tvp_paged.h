@@ -52,6 +52,7 @@ typedef void* tvp_stream_t;  /* cudaStream_t */
 #define TVP_DEVERR_TIMEOUT 4u      /* a pipeline wait ran out its bound          */
 #define TVP_DEVERR_BAD_PLAN 8u     /* workspace planned for another batch/grid   */
 #define TVP_DEVERR_BAD_TOKEN 16u   /* append: token's sequence row or position invalid */
+#define TVP_DEVERR_SMEM_ALIGN 32u  /* decode: shared window not 1 KiB aligned; nothing ran */
 
 /* ---- fixed geometry ---------------------------------------------------- */
 #define TVP_HEAD_DIM 64

@@ -27,6 +27,7 @@ TVP_DEVERR_BAD_LENGTH = 2
 TVP_DEVERR_TIMEOUT = 4
 TVP_DEVERR_BAD_PLAN = 8
 TVP_DEVERR_BAD_TOKEN = 16
+TVP_DEVERR_SMEM_ALIGN = 32
 
 TVP_MODE_FAST = 0
 TVP_MODE_COMPAT = 1

@@ -139,6 +139,14 @@ __device__ __forceinline__ void mma_bf16_16816(float& c0, float& c1, float& c2, 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// 2^x with the SFU's approximation (ex2.approx.ftz: relative error ~2^-22,
+// 2^-inf = +0).  Used by the FAST decode path only.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Packs two floats to BF16x2 (round to nearest even); `lo` lands in bits 0..15.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;

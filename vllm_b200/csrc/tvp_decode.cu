@@ -41,7 +41,7 @@ namespace tvp {
 constexpr int kPlanMagic = 0x54565031;  // "TVP1"
 constexpr int kTileBytes = kPage * kHeadDim * 2;            // 2048: one KV head of one page
 constexpr int kStageBytes = 2 * kMaxKvHeads * kTileBytes;   // 8 K tiles, then 8 V tiles
-constexpr int kMergeFields = 20;                            // m0 m1 l0 l1 acc[16]
+constexpr int kMergeFields = 2;  // per-lane values exchanged per merge round (see below)
 
 
 // ---------------------------------------------------------------------------
@@ -156,13 +156,32 @@ __device__ void combine_sequence(const DecodeParams& p, int s, int first, int en
 // run on the first page of a piece and when a page brings a new maximum.
 constexpr float kLazyMargin = 8.f;
 
-template <int STAGES, int SETS, bool LAZY>
-__global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
+// Register split of the warp-specialised form (REGSPLIT): the producer
+// warpgroup keeps kProducerRegs per thread, the consumer warpgroups take
+// kConsumerRegs.  The launch must provide threads x registers >= the split
+// (checked on the host before every launch; an unsatisfiable increase would
+// never return).
+constexpr int kProducerRegs = 40;
+constexpr int kConsumerRegs = 104;
+
+template <int SETS, bool REGSPLIT>
+constexpr int decode_threads() {
+  return (SETS * kMaxKvHeads + (REGSPLIT ? 4 : 1)) * 32;
+}
+
+template <int STAGES, int SETS, bool LAZY, bool REGSPLIT = false>
+__global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
     paged_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap k_map,
                         const __grid_constant__ CUtensorMap v_map) {
-  // The 128-byte swizzle pattern repeats every 1 KiB: tiles start 1 KiB aligned.
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  // The 128-byte swizzle pattern repeats every 1 KiB: stage tiles must start
+  // 1 KiB aligned.  The dynamic shared window of this kernel (no static shared
+  // memory) starts 1 KiB aligned; a launch where it does not reports an error
+  // instead of running the copies.
+  extern __shared__ __align__(1024) unsigned char smem[];
+  if (smem_addr(smem) & 1023u) {
+    if (threadIdx.x == 0) record_error(p.err, TVP_DEVERR_SMEM_ALIGN);
+    return;
+  }
   const int T_header_ok = (p.header[0] == kPlanMagic && p.header[1] == p.batch &&
                            p.header[2] == (int)gridDim.x && p.header[3] == kMaxKvHeads);
   if (!T_header_ok) {
@@ -210,8 +229,12 @@ __global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
     s0 = lo;
   }
 
-  if (warp == SETS * kMaxKvHeads) {
+  if (warp >= SETS * kMaxKvHeads) {
     // ------------------------------ producer ------------------------------
+    if (REGSPLIT) {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
+      if (warp != SETS * kMaxKvHeads) return;  // the rest of the producer warpgroup idles
+    }
     if (lane == 0) {
       prefetch_tensor_map(&k_map);
       prefetch_tensor_map(&v_map);
@@ -228,6 +251,8 @@ __global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
     int next_phys = p_begin < p_end
                         ? __ldg(p.tables + (size_t)s * p.table_stride + (p_begin - seq_first))
                         : 0;
+    int stage = 0;
+    uint32_t empty_parity = 1;  // parity of the previous round of each slot
     for (int pg = p_begin, kk = 0; pg < p_end; ++pg, ++kk) {
       const int phys = next_phys;
       if (pg + 1 < p_end) {
@@ -238,11 +263,9 @@ __global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
         }
         next_phys = __ldg(p.tables + (size_t)s * p.table_stride + (pg + 1 - seq_first));
       }
-      const int stage = kk % STAGES;
       if (kk >= STAGES) {
         int timed_out = 0;
-        if (lane == 0)
-          timed_out = !mbar_wait_bounded(smem_addr(&empty_bar[stage]), ((kk / STAGES) - 1) & 1);
+        if (lane == 0) timed_out = !mbar_wait_bounded(smem_addr(&empty_bar[stage]), empty_parity);
         if (__shfl_sync(0xffffffffu, timed_out, 0)) {
           if (lane == 0) {
             *abort_flag = 1;
@@ -267,11 +290,16 @@ __global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
         tma_load_2d(dst, lane < kMaxKvHeads ? &k_map : &v_map, h * kHeadDim,
                     (int)(p.layer_row_base + (long long)phys * kPage), full);
       }
+      if (++stage == STAGES) {
+        stage = 0;
+        empty_parity ^= 1u;
+      }
     }
     return;
   }
 
   // ------------------------------ consumers -------------------------------
+  if (REGSPLIT) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
   const int set = warp / kMaxKvHeads;
   const int g = warp % kMaxKvHeads;
   const int tr = lane >> 2;   // accumulator row (token) of this lane
@@ -299,6 +327,10 @@ __global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
   int s = s0;
   int pg = p_begin;
   int kbase = 0;
+  // Slot and phase of this set's current page, advanced incrementally
+  // (page kk of the CTA sits in slot kk % STAGES, phase (kk / STAGES) & 1).
+  int c_kk = 0, c_stage = 0;
+  uint32_t c_parity = 0;
   while (pg < p_end) {
     while (pg >= __ldg(p.cu + s + 1)) ++s;
     const int first = __ldg(p.cu + s), end = __ldg(p.cu + s + 1);
@@ -323,9 +355,14 @@ __global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
     for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 
     for (int i = set; i < n; i += SETS) {
-      const int kk = kbase + i;
-      const int stage = kk % STAGES;
-      const uint32_t parity = (kk / STAGES) & 1;
+      for (const int kk = kbase + i; c_kk < kk; ++c_kk) {
+        if (++c_stage == STAGES) {
+          c_stage = 0;
+          c_parity ^= 1u;
+        }
+      }
+      const int stage = c_stage;
+      const uint32_t parity = c_parity;
       bool ready = false;
       if (!*abort_flag) ready = mbar_wait_bounded(smem_addr(&full_bar[stage]), parity);
       ready = __all_sync(0xffffffffu, ready);
@@ -395,13 +432,13 @@ __global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
             mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
           }
           const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-          al0 = exp2f(m0 - mn0);
-          al1 = exp2f(m1 - mn1);
+          al0 = fast_exp2(m0 - mn0);
+          al1 = fast_exp2(m1 - mn1);
           m0 = mn0;
           m1 = mn1;
         }
-        const uint32_t pa = pack_bf16x2(exp2f(x0 - m0), exp2f(x1 - m1));
-        const uint32_t pb = pack_bf16x2(exp2f(x2 - m0), exp2f(x3 - m1));
+        const uint32_t pa = pack_bf16x2(fast_exp2(x0 - m0), fast_exp2(x1 - m1));
+        const uint32_t pb = pack_bf16x2(fast_exp2(x2 - m0), fast_exp2(x3 - m1));
         l0 = l0 * al0 + (bf16lo_to_f32(pa) + bf16lo_to_f32(pb));
         l1 = l1 * al1 + (bf16hi_to_f32(pa) + bf16hi_to_f32(pb));
         if (grow && __any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
@@ -420,36 +457,48 @@ __global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
     }
 
     if (SETS > 1) {
+      // Set 1 hands its (m, l, O) state to set 0 through a 2 x 32-float slot
+      // per KV head, two values per lane per round (m, l, then the 16 output
+      // fragments in pairs whose columns use the two rescale weights).
       float* mg = merge + g * kMergeFields * 32;
-      if (set == 1) {
-        mg[0 * 32 + lane] = m0; mg[1 * 32 + lane] = m1;
-        mg[2 * 32 + lane] = l0; mg[3 * 32 + lane] = l1;
-#pragma unroll
-        for (int d = 0; d < 4; ++d)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) mg[(4 + d * 4 + e) * 32 + lane] = acc[d][e];
-      }
-      named_barrier_sync(1 + g, 64);
-      if (set == 0) {
-        const float mb0 = mg[0 * 32 + lane], mb1 = mg[1 * 32 + lane];
-        const float M0 = fmaxf(m0, mb0), M1 = fmaxf(m1, mb1);
-        const float wa0 = m0 == -INFINITY ? 0.f : exp2f(m0 - M0);
-        const float wa1 = m1 == -INFINITY ? 0.f : exp2f(m1 - M1);
-        const float wb0 = mb0 == -INFINITY ? 0.f : exp2f(mb0 - M0);
-        const float wb1 = mb1 == -INFINITY ? 0.f : exp2f(mb1 - M1);
-        l0 = l0 * wa0 + mg[2 * 32 + lane] * wb0;
-        l1 = l1 * wa1 + mg[3 * 32 + lane] * wb1;
-#pragma unroll
-        for (int d = 0; d < 4; ++d) {
-          acc[d][0] = acc[d][0] * wa0 + mg[(4 + d * 4 + 0) * 32 + lane] * wb0;
-          acc[d][1] = acc[d][1] * wa1 + mg[(4 + d * 4 + 1) * 32 + lane] * wb1;
-          acc[d][2] = acc[d][2] * wa0 + mg[(4 + d * 4 + 2) * 32 + lane] * wb0;
-          acc[d][3] = acc[d][3] * wa1 + mg[(4 + d * 4 + 3) * 32 + lane] * wb1;
+      float wa0 = 1.f, wa1 = 1.f, wb0 = 0.f, wb1 = 0.f;
+      auto exchange = [&](float x0, float x1, float& y0, float& y1) {
+        if (set == 1) {
+          mg[lane] = x0;
+          mg[32 + lane] = x1;
         }
+        named_barrier_sync(1 + g, 64);
+        if (set == 0) {
+          y0 = mg[lane];
+          y1 = mg[32 + lane];
+        }
+        named_barrier_sync(1 + g, 64);
+      };
+      float mb0 = 0.f, mb1 = 0.f;
+      exchange(m0, m1, mb0, mb1);
+      if (set == 0) {
+        const float M0 = fmaxf(m0, mb0), M1 = fmaxf(m1, mb1);
+        wa0 = m0 == -INFINITY ? 0.f : exp2f(m0 - M0);
+        wa1 = m1 == -INFINITY ? 0.f : exp2f(m1 - M1);
+        wb0 = mb0 == -INFINITY ? 0.f : exp2f(mb0 - M0);
+        wb1 = mb1 == -INFINITY ? 0.f : exp2f(mb1 - M1);
         m0 = M0;
         m1 = M1;
       }
-      named_barrier_sync(1 + g, 64);
+      float lb0 = 0.f, lb1 = 0.f;
+      exchange(l0, l1, lb0, lb1);
+      l0 = l0 * wa0 + lb0 * wb0;
+      l1 = l1 * wa1 + lb1 * wb1;
+#pragma unroll
+      for (int d = 0; d < 4; ++d) {
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          float b0 = 0.f, b1 = 0.f;
+          exchange(acc[d][e], acc[d][e + 1], b0, b1);
+          acc[d][e] = acc[d][e] * wa0 + b0 * wb0;      // columns 2hc
+          acc[d][e + 1] = acc[d][e + 1] * wa1 + b1 * wb1;  // columns 2hc + 1
+        }
+      }
     }
 
     if (set == 0) {
@@ -511,17 +560,19 @@ __global__ void __launch_bounds__((SETS * kMaxKvHeads + 1) * 32, 1)
   }
 }
 
-// One consumer set (8 warps, one per KV head) and 7 stages of 32 KiB: 224 KiB
-// of pages in flight per SM, which is what a B200 needs to stream at its HBM
-// roofline with ~4 us fetch latency under load.
-constexpr int kStages = 7;
-constexpr int kSets = 1;
-constexpr bool kLazy = true;
-constexpr int kDecodeThreads = (kSets * kMaxKvHeads + 1) * 32;
+// Two forms, both persistent with one CTA per SM:
+//  * split (default): 2 consumer sets (16 warps, 4 per SMSP) behind a producer
+//    warpgroup that hands its registers to them (setmaxnreg), 7 stages of
+//    32 KiB plus a 2 KiB set-merge scratch;
+//  * plain (fallback when the launch's register pool could not satisfy the
+//    split): 1 consumer set and 7 stages.
+constexpr int kSplitStages = 7;
+constexpr int kPlainStages = 7;
 
-size_t decode_smem_bytes() {
-  return 1024 /* alignment slack */ + (size_t)kStages * kStageBytes + 2 * kStages * 8 +
-         (kStages + 4) * 4 + 16 + (kSets > 1 ? (size_t)kMaxKvHeads * kMergeFields * 32 * 4 : 0);
+template <int STAGES, int SETS>
+constexpr size_t decode_smem_bytes() {
+  return (size_t)STAGES * kStageBytes + 2 * STAGES * 8 + (STAGES + 4) * 4 + 16 +
+         (SETS > 1 ? (size_t)kMaxKvHeads * kMergeFields * 32 * 4 : 0);
 }
 
 cudaError_t launch_decode_plan(const int32_t* lens, int batch, int table_stride, int num_ctas,
@@ -584,24 +635,55 @@ bool pool_tensor_map(const void* pool, long long rows, CUtensorMap* out) {
 
 }  // namespace
 
+namespace {
+
+enum class DecodeForm { kUnknown, kSplit, kPlain };
+
+// Chooses the form once per device: the split needs the launch's register
+// pool (threads x registers per thread) to cover what the warpgroups ask for.
+DecodeForm decode_form(int dev) {
+  static DecodeForm forms[64] = {};
+  if (dev >= 0 && dev < 64 && forms[dev] != DecodeForm::kUnknown) return forms[dev];
+  DecodeForm form = DecodeForm::kPlain;
+  cudaFuncAttributes fa;
+  constexpr int threads = decode_threads<2, true>();
+  if (cudaFuncGetAttributes(&fa, paged_decode_kernel<kSplitStages, 2, true, true>) == cudaSuccess &&
+      (long long)fa.numRegs * threads >=
+          128LL * kProducerRegs + (long long)(threads - 128) * kConsumerRegs &&
+      cudaFuncSetAttribute(paged_decode_kernel<kSplitStages, 2, true, true>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)decode_smem_bytes<kSplitStages, 2>()) == cudaSuccess)
+    form = DecodeForm::kSplit;
+  if (form == DecodeForm::kPlain &&
+      cudaFuncSetAttribute(paged_decode_kernel<kPlainStages, 1, true, false>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)decode_smem_bytes<kPlainStages, 1>()) != cudaSuccess)
+    form = DecodeForm::kUnknown;
+  if (dev >= 0 && dev < 64) forms[dev] = form;
+  return form;
+}
+
+}  // namespace
+
 cudaError_t launch_paged_decode(const DecodeParams& p, long long pool_rows, int num_ctas,
                                 cudaStream_t stream) {
-  static bool configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  const size_t smem = decode_smem_bytes();
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
-    e = cudaFuncSetAttribute(paged_decode_kernel<kStages, kSets, kLazy>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) configured[dev] = true;
-  }
+  const DecodeForm form = decode_form(dev);
+  if (form == DecodeForm::kUnknown) return cudaErrorInvalidDeviceFunction;
   CUtensorMap k_map, v_map;
   if (!pool_tensor_map(p.k_pool, pool_rows, &k_map) ||
       !pool_tensor_map(p.v_pool, pool_rows, &v_map))
     return cudaErrorInvalidValue;
-  paged_decode_kernel<kStages, kSets, kLazy><<<num_ctas, kDecodeThreads, smem, stream>>>(p, k_map, v_map);
+  if (form == DecodeForm::kSplit)
+    paged_decode_kernel<kSplitStages, 2, true, true>
+        <<<num_ctas, decode_threads<2, true>(), decode_smem_bytes<kSplitStages, 2>(), stream>>>(
+            p, k_map, v_map);
+  else
+    paged_decode_kernel<kPlainStages, 1, true, false>
+        <<<num_ctas, decode_threads<1, false>(), decode_smem_bytes<kPlainStages, 1>(), stream>>>(
+            p, k_map, v_map);
   return cudaGetLastError();
 }
 
