@@ -93,7 +93,8 @@ def time_cpu(rows: int, budget_s: float, threads: int = 0):
     of the workload, one layer, repeated until `budget_s` elapsed."""
     import oracle
     case = cpu_sample_case(rows)
-    cores = threads if threads > 0 else oracle.max_threads()
+    # every host core this process may run on (torchrun sets OMP_NUM_THREADS=1)
+    cores = threads if threads > 0 else len(os.sched_getaffinity(0))
     t0 = time.perf_counter()
     reps = 0
     while True:
@@ -377,7 +378,35 @@ def extras(args, dev, case, k_pool, v_pool, q_all, out, tables, seq_lens, ws):
                                 "tolerance": "1e-2 abs + 2e-2 rel"}
     res["long_context"] = bench_long_context(dev)
     res["decode_small"] = bench_decode_small(dev)
+    res["e2e_llama"] = bench_e2e_llama()
     return res
+
+
+def bench_e2e_llama():
+    """The e2e workload (Llama-3.2-1B geometry, seeded random weights, 4 requests
+    x 128 prompt + 128 greedy tokens, the reference's scheduler): tokens/s of the
+    unmodified engine and of the engine with this path dropped in (best of 2
+    runs each, same B200, separate processes)."""
+    libs = [ROOT / "oracle" / "_ref" / f"libtvp_e2e_{n}.so" for n in ("ref", "tvp")]
+    if not all(p.exists() for p in libs):
+        return {"note": "end-to-end engines not built (make -C oracle e2e)"}
+    out = {"workload": "e2e: Llama-3.2-1B geometry, random N(0,0.02) weights, B=4, 128+128 tokens"}
+    for name, args in (("reference", ["--engine", "ref"]),
+                       ("ours_compat", ["--engine", "tvp", "--mode", "compat"]),
+                       ("ours_fast", ["--engine", "tvp", "--mode", "fast"])):
+        r = subprocess.run([sys.executable, str(ROOT / "tests" / "e2e_runner.py"), *args,
+                            "--runs", "2"], capture_output=True, text=True, timeout=900)
+        if r.returncode != 0:
+            out[name] = {"error": r.stderr[-300:]}
+            continue
+        d = json.loads(r.stdout.strip().splitlines()[-1])
+        out[name] = {"tok_s": round(d["tokens_generated"] / min(d["seconds"]), 1),
+                     "seconds": [round(x, 3) for x in d["seconds"]]}
+    try:
+        out["speedup_compat"] = round(out["ours_compat"]["tok_s"] / out["reference"]["tok_s"], 2)
+    except (KeyError, TypeError, ZeroDivisionError):
+        pass
+    return out
 
 
 def bench_long_context(dev, iters=20):

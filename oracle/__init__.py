@@ -37,7 +37,7 @@ def build(with_reference: bool = True) -> None:
         raise RuntimeError("make not found")
     subprocess.run([make, "-C", str(HERE)], check=True)
     if with_reference and (REFERENCE_DIR / "src" / "model" / "paged_attention.cu").exists():
-        subprocess.run([make, "-C", str(HERE), "ref", f"REF={REFERENCE_DIR}"], check=True)
+        subprocess.run([make, "-C", str(HERE), "ref", "e2e", f"REF={REFERENCE_DIR}"], check=True)
 
 
 def load() -> ctypes.CDLL:
