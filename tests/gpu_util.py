@@ -32,7 +32,8 @@ def run_decode(case, layer=0, mode=0, num_ctas=0, q=None, error=None, workspace=
     tables = dev_i32(case.tables)
     lens = dev_i32(case.lens)
     err = error if error is not None else ops.new_error_word("cuda")
-    ws = workspace or ops.DecodeWorkspace(case.batch, "cuda", num_ctas=num_ctas)
+    ws = workspace or ops.DecodeWorkspace(case.batch, "cuda", num_ctas=num_ctas,
+                                          kv_heads=case.k_pool.shape[3] // 64)
     if mode == 0:
         ops.decode_plan(lens, case.tables.shape[1], ws, error=err)
     out = ops.paged_decode_attention(qd, k, v, layer, tables, lens, ws if mode == 0 else None,

@@ -71,8 +71,10 @@ def test_decode_rejects_bad_arguments_on_host(native):
     assert call(layer=16) == N.TVP_ERR_INVALID_ARGUMENT
     assert call(batch=0) == N.TVP_ERR_INVALID_ARGUMENT
     assert call(scale=float("nan")) == N.TVP_ERR_INVALID_ARGUMENT
-    assert call(kvh=4) == N.TVP_ERR_UNSUPPORTED
-    assert call(qh=16) == N.TVP_ERR_UNSUPPORTED
+    assert call(kvh=3, qh=12) == N.TVP_ERR_UNSUPPORTED   # head shards are 1, 2, 4 or 8 heads
+    assert call(kvh=16, qh=64) == N.TVP_ERR_UNSUPPORTED
+    assert call(qh=16) == N.TVP_ERR_UNSUPPORTED          # q heads must be 4 per KV head
+    assert call(kvh=4, qh=32) == N.TVP_ERR_UNSUPPORTED
     assert call(mode=7) == N.TVP_ERR_UNSUPPORTED
     assert call(ws=None) == N.TVP_ERR_WORKSPACE
     assert call(wsb=16) == N.TVP_ERR_WORKSPACE
@@ -86,9 +88,13 @@ def test_workspace_size_grows_with_batch_and_grid(native):
     assert 0 < a < b < c
     assert a % 256 == 0
     assert native.tvp_decode_workspace_bytes(0, 8, 148) == 0
-    assert native.tvp_decode_workspace_bytes(4, 4, 148) == 0
+    assert native.tvp_decode_workspace_bytes(4, 3, 148) == 0
+    assert native.tvp_decode_workspace_bytes(4, 16, 148) == 0
     # partials: 2 slots x 8 KV heads x (4 + 4 + 256) floats per CTA
     assert c - b >= 148 * 2 * 8 * 264 * 4
+    # a head shard's workspace holds counters and partials for its heads only
+    sizes = [native.tvp_decode_workspace_bytes(256, h, 148) for h in (1, 2, 4, 8)]
+    assert 0 < sizes[0] < sizes[1] < sizes[2] < sizes[3] == b
 
 
 def test_python_layer_maps_codes_to_reference_exceptions():

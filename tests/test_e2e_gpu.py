@@ -36,6 +36,9 @@ def test_dropped_in_path_matches_reference_up_to_bf16_ties(summary, mode):
     s = summary[mode]
     assert s["first_tokens_match"]          # prefill: RoPE + pages are bit-exact
     assert s["argmax_agreement"] >= (0.90 if mode == "compat" else 0.85)
-    # every disagreement is a near-tie in the reference's own BF16-rounded logits
-    assert max(s["gap_at_disagreement_bf16_ulps"], default=0.0) <= 4.0
+    # every disagreement is a near-tie in the reference's own BF16-rounded logits;
+    # FAST keeps FP32 scores where the reference rounds them to BF16 and
+    # normalises once at the end, so its logits sit further from the
+    # reference's and wider ties flip
+    assert max(s["gap_at_disagreement_bf16_ulps"], default=0.0) <= (4.0 if mode == "compat" else 8.0)
     assert s["max_abs_logit_diff"] <= 0.05 * s["max_abs_reference_logit"]

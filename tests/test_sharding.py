@@ -1,6 +1,8 @@
 """Multi-process host logic of the multi-GPU decode path, on CPU (gloo,
 world size 2): request sharding covers every row exactly once and balances the
-attended tokens; the bench's max-over-ranks timing reduction."""
+attended tokens; the bench's max-over-ranks timing reduction; KV-head
+sharding's slices, all-gather and interleave reassemble the 8-head attention
+(per-rank attention from the oracle)."""
 import os
 import socket
 
@@ -9,6 +11,7 @@ import pytest
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
+import oracle
 import workloads as W
 from vllm_b200 import sharding
 
@@ -77,3 +80,57 @@ def test_two_rank_gloo_partition_agreement_and_max_timing():
     assert rows == list(range(256))
     assert t0 == t1 == 11.0
     assert abs(load0 - load1) <= 8192
+
+
+def test_head_slices_and_interleave_reassemble_the_oracle():
+    """Single process: the oracle on each rank's head slice, interleaved,
+    is bit-identical to the oracle on all 8 heads (heads are independent)."""
+    case = W.decode_random(80, [300, 17, 129, 64])
+    full = oracle.decode_attention(case.q, case.k_pool, case.v_pool, 0, case.tables, case.lens)
+    for world in (1, 2, 4, 8):
+        parts = []
+        for heads in sharding.shard_by_kv_head(world):
+            q = np.ascontiguousarray(sharding.slice_q_heads(case.q, heads))
+            k = np.ascontiguousarray(sharding.slice_kv_heads(case.k_pool, heads))
+            v = np.ascontiguousarray(sharding.slice_kv_heads(case.v_pool, heads))
+            parts.append(oracle.decode_attention(q, k, v, 0, case.tables, case.lens))
+        assert np.array_equal(sharding.interleave_head_shards(np.stack(parts)), full)
+
+
+def _head_worker(rank, world, port, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import torch
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        case = W.decode_random(81, [500, 33, 1, 260, 90])
+        heads = sharding.shard_by_kv_head(world)[rank]
+        q = np.ascontiguousarray(sharding.slice_q_heads(case.q, heads))
+        k = np.ascontiguousarray(sharding.slice_kv_heads(case.k_pool, heads))
+        v = np.ascontiguousarray(sharding.slice_kv_heads(case.v_pool, heads))
+        mine = oracle.decode_attention(q, k, v, 0, case.tables, case.lens)
+        local = torch.from_numpy(mine.view(np.int16)).view(torch.bfloat16)
+        flat = torch.empty((world * 8, local.shape[1]), dtype=torch.bfloat16)  # room for B <= 8
+        rows = sharding.all_gather_head_shards(local, flat)
+        results[rank] = rows.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gloo_head_sharded_gather():
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    procs = [ctx.Process(target=_head_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    case = W.decode_random(81, [500, 33, 1, 260, 90])
+    full = oracle.decode_attention(case.q, case.k_pool, case.v_pool, 0, case.tables, case.lens)
+    assert np.array_equal(results[0], full)
+    assert np.array_equal(results[1], full)

@@ -23,7 +23,8 @@ import numpy as np
 HEAD_DIM = 64
 PAGE = 16
 KV_HEADS = 8
-Q_HEADS = 32
+GROUP = 4
+Q_HEADS = KV_HEADS * GROUP  # 32
 KV_DIM = KV_HEADS * HEAD_DIM  # 512
 Q_DIM = Q_HEADS * HEAD_DIM    # 2048
 
@@ -101,7 +102,8 @@ def decode_small(seed: int = 1, with_data: bool = True) -> DecodeCase:
 
 
 def decode_random(seed: int, lens, num_pages: int | None = None, num_layers: int = 1,
-                  slack_pages: int = 3, with_data: bool = True) -> DecodeCase:
+                  slack_pages: int = 3, with_data: bool = True, kv_heads: int = KV_HEADS) -> DecodeCase:
+    """Random decode case; kv_heads < 8 gives the pools and q of one KV-head shard."""
     rng = np.random.default_rng(seed)
     lens = np.asarray(lens, dtype=np.int32)
     need = sum(pages_for(int(L)) for L in lens)
@@ -109,9 +111,9 @@ def decode_random(seed: int, lens, num_pages: int | None = None, num_layers: int
     tables = scattered_tables(rng, lens, num_pages)
     case = DecodeCase(lens=lens, tables=tables, num_pages=num_pages, num_layers=num_layers)
     if with_data:
-        case.q = normal_bf16(rng, (lens.size, Q_DIM))
-        case.k_pool = normal_bf16(rng, (num_layers, num_pages, PAGE, KV_DIM))
-        case.v_pool = normal_bf16(rng, (num_layers, num_pages, PAGE, KV_DIM))
+        case.q = normal_bf16(rng, (lens.size, kv_heads * GROUP * HEAD_DIM))
+        case.k_pool = normal_bf16(rng, (num_layers, num_pages, PAGE, kv_heads * HEAD_DIM))
+        case.v_pool = normal_bf16(rng, (num_layers, num_pages, PAGE, kv_heads * HEAD_DIM))
     return case
 
 

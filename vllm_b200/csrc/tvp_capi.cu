@@ -15,14 +15,21 @@ struct WorkspaceLayout {
   size_t header, cu, counters, partials, total;
 };
 
-WorkspaceLayout workspace_layout(int batch, int num_ctas) {
+// header | cu[batch + 1] | counters[batch][kv_heads] | partials[2 num_ctas][kv_heads]
+WorkspaceLayout workspace_layout(int batch, int kv_heads, int num_ctas) {
   WorkspaceLayout w;
   w.header = 0;
   w.cu = 256;
   w.counters = align_up(w.cu + (size_t)(batch + 1) * 4, 256);
-  w.partials = align_up(w.counters + (size_t)batch * kMaxKvHeads * 4, 256);
-  w.total = align_up(w.partials + (size_t)num_ctas * 2 * kMaxKvHeads * kPartialFloats * 4, 256);
+  w.partials = align_up(w.counters + (size_t)batch * kv_heads * 4, 256);
+  w.total = align_up(w.partials + (size_t)num_ctas * 2 * kv_heads * kPartialFloats * 4, 256);
   return w;
+}
+
+// KV heads per pool the decode kernels provide: the model's 8, or the 4, 2 or
+// 1 that each GPU holds when the heads are sharded over 2, 4 or 8 GPUs.
+inline bool decode_heads_supported(int kv_heads) {
+  return kv_heads == 1 || kv_heads == 2 || kv_heads == 4 || kv_heads == kMaxKvHeads;
 }
 
 int sm_count_cached(int* out) {
@@ -116,10 +123,10 @@ int tvp_rope_append(tvp_bf16* k_pool, tvp_bf16* v_pool, int num_pages, int num_l
 }
 
 size_t tvp_decode_workspace_bytes(int batch, int kv_heads, int num_ctas) {
-  if (batch <= 0 || kv_heads != kMaxKvHeads) return 0;
+  if (batch <= 0 || !decode_heads_supported(kv_heads)) return 0;
   int ctas = 0;
   if (resolve_ctas(num_ctas, &ctas) != TVP_OK) return 0;
-  return workspace_layout(batch, ctas).total;
+  return workspace_layout(batch, kv_heads, ctas).total;
 }
 
 int tvp_decode_plan(const int32_t* d_seq_lens, int batch, int table_stride, int kv_heads,
@@ -127,14 +134,14 @@ int tvp_decode_plan(const int32_t* d_seq_lens, int batch, int table_stride, int 
                     tvp_stream_t stream) {
   if (!d_seq_lens || batch <= 0 || table_stride <= 0 || num_ctas < 0)
     return TVP_ERR_INVALID_ARGUMENT;
-  if (kv_heads != kMaxKvHeads) return TVP_ERR_UNSUPPORTED;
+  if (!decode_heads_supported(kv_heads)) return TVP_ERR_UNSUPPORTED;
   int ctas = 0;
   int rc = resolve_ctas(num_ctas, &ctas);
   if (rc != TVP_OK) return rc;
-  const WorkspaceLayout w = workspace_layout(batch, ctas);
+  const WorkspaceLayout w = workspace_layout(batch, kv_heads, ctas);
   if (!d_workspace || workspace_bytes < w.total || !aligned(d_workspace, 256)) return TVP_ERR_WORKSPACE;
   char* base = static_cast<char*>(d_workspace);
-  return map_cuda(launch_decode_plan(d_seq_lens, batch, table_stride, ctas,
+  return map_cuda(launch_decode_plan(d_seq_lens, batch, table_stride, ctas, kv_heads,
                                      reinterpret_cast<int32_t*>(base + w.header),
                                      reinterpret_cast<int32_t*>(base + w.cu),
                                      reinterpret_cast<int32_t*>(base + w.counters), d_error,
@@ -151,7 +158,7 @@ int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const 
       num_layers <= 0 || layer < 0 || layer >= num_layers || table_stride <= 0 || batch <= 0 ||
       num_ctas < 0 || !std::isfinite(scale))
     return TVP_ERR_INVALID_ARGUMENT;
-  if (kv_heads != kMaxKvHeads || q_heads != kMaxKvHeads * kGroup) return TVP_ERR_UNSUPPORTED;
+  if (!decode_heads_supported(kv_heads) || q_heads != kv_heads * kGroup) return TVP_ERR_UNSUPPORTED;
   if (mode != TVP_MODE_FAST && mode != TVP_MODE_COMPAT) return TVP_ERR_UNSUPPORTED;
   // TMA row coordinates are 32-bit: the pools may hold at most 2^31 - 1 token rows.
   if ((long long)num_layers * num_pages * kPage > 0x7fffffffLL) return TVP_ERR_UNSUPPORTED;
@@ -170,6 +177,7 @@ int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const 
     p.layer_row_base = layer_row_base;
     p.num_pages = num_pages;
     p.table_stride = table_stride;
+    p.kv_heads = kv_heads;
     p.scale = scale;
     p.err = d_error;
     return map_cuda(launch_compat_decode(p, batch, st));
@@ -177,7 +185,7 @@ int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const 
   int ctas = 0;
   int rc = resolve_ctas(num_ctas, &ctas);
   if (rc != TVP_OK) return rc;
-  const WorkspaceLayout w = workspace_layout(batch, ctas);
+  const WorkspaceLayout w = workspace_layout(batch, kv_heads, ctas);
   if (!d_workspace || workspace_bytes < w.total || !aligned(d_workspace, 256)) return TVP_ERR_WORKSPACE;
   char* base = static_cast<char*>(d_workspace);
   DecodeParams p;
@@ -195,6 +203,7 @@ int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const 
   p.num_pages = num_pages;
   p.table_stride = table_stride;
   p.batch = batch;
+  p.kv_heads = kv_heads;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = d_error;
   return map_cuda(launch_paged_decode(p, (long long)num_layers * num_pages * kPage, ctas, st));

@@ -8,7 +8,8 @@
 // BF16 (src/model/attention.cu:95-142).  This kernel keeps every one of those
 // rounding points and the tree order of the sum; only the FP32 order inside the
 // two dot products is its own (sequential FMA), which cuBLAS does not specify.
-// One CTA per (sequence, KV head); pages are read in place.  Used where greedy
+// One CTA per (sequence, KV head) of a pool of 1, 2, 4 or 8 KV heads; pages are
+// read in place.  Used where greedy
 // token identity with the reference matters more than bandwidth.
 #include "tvp_params.cuh"
 
@@ -31,15 +32,16 @@ __global__ void __launch_bounds__(kCompatThreads) compat_decode_kernel(const Com
   __shared__ float row_max[kGroup], row_sum[kGroup];
 
   const int s = blockIdx.x, g = blockIdx.y, tid = threadIdx.x;
-  constexpr int kOutRow = kMaxKvHeads * kGroup * kHeadDim;
+  const int kv_dim = p.kv_heads * kHeadDim;
+  const int out_row = p.kv_heads * kGroup * kHeadDim;
   const int L = p.seq_lens[s];
-  __nv_bfloat16* out = p.out + (size_t)s * kOutRow + g * kGroup * kHeadDim;
+  __nv_bfloat16* out = p.out + (size_t)s * out_row + g * kGroup * kHeadDim;
   if (L <= 0 || L > kCompatMaxLen || L > p.table_stride * kPage) {
     if (L != 0 && tid == 0) record_error(p.err, TVP_DEVERR_BAD_LENGTH);
     out[tid] = __float2bfloat16_rn(0.f);
     return;
   }
-  qs[tid] = __bfloat162float(p.q[(size_t)s * kOutRow + g * kGroup * kHeadDim + tid]);
+  qs[tid] = __bfloat162float(p.q[(size_t)s * out_row + g * kGroup * kHeadDim + tid]);
   __syncthreads();
 
   // Scores: s = bf16(scale * (q . k)), FP32 accumulation.
@@ -51,8 +53,7 @@ __global__ void __launch_bounds__(kCompatThreads) compat_decode_kernel(const Com
       continue;
     }
     const uint4* krow = reinterpret_cast<const uint4*>(
-        p.k_pool + (size_t)(p.layer_row_base + (long long)phys * kPage + t % kPage) *
-                       (kMaxKvHeads * kHeadDim) +
+        p.k_pool + (size_t)(p.layer_row_base + (long long)phys * kPage + t % kPage) * kv_dim +
         g * kHeadDim);
     float k[kHeadDim];
 #pragma unroll
@@ -127,8 +128,7 @@ __global__ void __launch_bounds__(kCompatThreads) compat_decode_kernel(const Com
     const int phys = __ldg(p.tables + (size_t)s * p.table_stride + t / kPage);
     if (phys < 0 || phys >= p.num_pages) continue;
     const float v = __bfloat162float(
-        p.v_pool[(size_t)(p.layer_row_base + (long long)phys * kPage + t % kPage) *
-                     (kMaxKvHeads * kHeadDim) +
+        p.v_pool[(size_t)(p.layer_row_base + (long long)phys * kPage + t % kPage) * kv_dim +
                  g * kHeadDim + d]);
     acc = fmaf(sc[h * kCompatMaxLen + t], v, acc);
   }
@@ -150,7 +150,7 @@ cudaError_t launch_compat_decode(const CompatParams& p, int batch, cudaStream_t 
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  compat_decode_kernel<<<dim3(batch, kMaxKvHeads), kCompatThreads, compat_smem_bytes(), stream>>>(p);
+  compat_decode_kernel<<<dim3(batch, p.kv_heads), kCompatThreads, compat_smem_bytes(), stream>>>(p);
   return cudaGetLastError();
 }
 

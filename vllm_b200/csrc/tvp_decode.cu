@@ -34,13 +34,10 @@
 // accumulator layout into operand layout with movmatrix.
 #include <cudaTypedefs.h>
 
-#include "tvp_params.cuh"
+#include "tvp_tile.cuh"
 
 namespace tvp {
 
-constexpr int kPlanMagic = 0x54565031;  // "TVP1"
-constexpr int kTileBytes = kPage * kHeadDim * 2;            // 2048: one KV head of one page
-constexpr int kStageBytes = 2 * kMaxKvHeads * kTileBytes;   // 8 K tiles, then 8 V tiles
 constexpr int kMergeFields = 2;  // per-lane values exchanged per merge round (see below)
 
 
@@ -95,78 +92,6 @@ __global__ void __launch_bounds__(1024)
     header[3] = groups;
   }
   for (int i = tid; i < batch * groups; i += blockDim.x) counters[i] = 0;
-}
-
-// CTA whose page range holds flattened page p (ranges [floor(cT/C), floor((c+1)T/C))).
-__device__ __forceinline__ int cta_of_page(long long p, long long T, long long C) {
-  return (int)(((p + 1) * C - 1) / T);
-}
-__device__ __forceinline__ int range_begin(long long c, long long T, long long C) {
-  return (int)(c * T / C);
-}
-// Partial slot of sequence [first, end) inside CTA c: slot 0 when the
-// sequence started at or before the CTA's range, slot 1 otherwise.
-__device__ __forceinline__ int partial_slot(int c, int first, long long T, long long C) {
-  return c * 2 + (range_begin(c, T, C) < first ? 1 : 0);
-}
-
-// Merge of all partial pieces of one sequence for KV head g (32 lanes: lane
-// -> query head lane/8 of the group, channels (lane%8)*8 .. +7).
-__device__ void combine_sequence(const DecodeParams& p, int s, int first, int end, int g,
-                                 long long T, long long C, int lane) {
-  const int c0 = cta_of_page(first, T, C), c1 = cta_of_page(end - 1, T, C);
-  const int h = lane >> 3, d0 = (lane & 7) * 8;
-  float M = -INFINITY;
-  for (int c = c0; c <= c1; ++c) {
-    const int slot = (c == c0) ? partial_slot(c, first, T, C) : c * 2;
-    const float* part = p.partials + ((size_t)slot * kMaxKvHeads + g) * kPartialFloats;
-    M = fmaxf(M, __ldcg(part + h));
-  }
-  float o[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) o[i] = 0.f;
-  float lsum = 0.f;
-  for (int c = c0; c <= c1; ++c) {
-    const int slot = (c == c0) ? partial_slot(c, first, T, C) : c * 2;
-    const float* part = p.partials + ((size_t)slot * kMaxKvHeads + g) * kPartialFloats;
-    const float m = __ldcg(part + h);
-    const float w = (m == -INFINITY) ? 0.f : exp2f(m - M);
-    lsum += w * __ldcg(part + kGroup + h);
-    const float4 a = __ldcg(reinterpret_cast<const float4*>(part + 2 * kGroup + h * kHeadDim + d0));
-    const float4 b =
-        __ldcg(reinterpret_cast<const float4*>(part + 2 * kGroup + h * kHeadDim + d0 + 4));
-    o[0] += w * a.x; o[1] += w * a.y; o[2] += w * a.z; o[3] += w * a.w;
-    o[4] += w * b.x; o[5] += w * b.y; o[6] += w * b.z; o[7] += w * b.w;
-  }
-  const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-  uint4 packed;
-  packed.x = pack_bf16x2(o[0] * inv, o[1] * inv);
-  packed.y = pack_bf16x2(o[2] * inv, o[3] * inv);
-  packed.z = pack_bf16x2(o[4] * inv, o[5] * inv);
-  packed.w = pack_bf16x2(o[6] * inv, o[7] * inv);
-  __nv_bfloat16* dst = p.out + (size_t)s * (kMaxKvHeads * kGroup * kHeadDim) +
-                       (g * kGroup + h) * kHeadDim + d0;
-  *reinterpret_cast<uint4*>(dst) = packed;
-}
-
-// LAZY: keep the running maximum unless a score exceeds it by more than
-// kLazyMargin (base-2 exponent units).  Probabilities then stay below
-// 2^kLazyMargin (exact in FP32/BF16 range), and the cross-lane max reduction,
-// the rescale factors and the accumulator rescale leave the common path; they
-// run on the first page of a piece and when a page brings a new maximum.
-constexpr float kLazyMargin = 8.f;
-
-// Register split of the warp-specialised form (REGSPLIT): the producer
-// warpgroup keeps kProducerRegs per thread, the consumer warpgroups take
-// kConsumerRegs.  The launch must provide threads x registers >= the split
-// (checked on the host before every launch; an unsatisfiable increase would
-// never return).
-constexpr int kProducerRegs = 40;
-constexpr int kConsumerRegs = 104;
-
-template <int SETS, bool REGSPLIT>
-constexpr int decode_threads() {
-  return (SETS * kMaxKvHeads + (REGSPLIT ? 4 : 1)) * 32;
 }
 
 template <int STAGES, int SETS, bool LAZY, bool REGSPLIT = false>
@@ -302,16 +227,9 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
   if (REGSPLIT) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
   const int set = warp / kMaxKvHeads;
   const int g = warp % kMaxKvHeads;
-  const int tr = lane >> 2;   // accumulator row (token) of this lane
-  const int hc = lane & 3;    // accumulator column pair (query heads 2hc, 2hc+1)
-  const int mat = lane >> 3, mrow = lane & 7;
-  // ldmatrix row addresses (bytes within a stage) for this lane.  Tile rows are
-  // 128 B (one token of head g); 16-byte chunk c of row r sits at chunk c ^ (r % 8).
-  // K (A operand of S^T = K Q^T): matrix m covers tokens 8*(m&1).., chunk 2*k4+(m>>1).
-  // V (A operand of O^T = V^T P^T, transposed load): tokens 8*(m>>1).., chunk 2*d+(m&1).
-  const uint32_t k_lane = g * kTileBytes + (mrow + (mat & 1) * 8) * 128;
-  const uint32_t v_lane = kMaxKvHeads * kTileBytes + g * kTileBytes + (mrow + (mat >> 1) * 8) * 128;
-  const int k_chunk = mat >> 1, v_chunk = mat & 1;
+  const TileLane tl(lane);
+  // This warp's K and V tiles within a stage: head g of the 8 K, then 8 V tiles.
+  const uint32_t k_off = g * kTileBytes, v_off = (kMaxKvHeads + g) * kTileBytes;
   constexpr int kOutRow = kMaxKvHeads * kGroup * kHeadDim;  // 2048
 
   // Rows of length 0 attend to nothing: their output is zero.
@@ -341,18 +259,9 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
 
     // Q_g^T operand fragments: column n = tr holds query head 4g + tr (tr < 4).
     uint32_t qb[4][2];
-    {
-      const __nv_bfloat16* qrow = p.q + (size_t)s * kOutRow + (g * kGroup + tr) * kHeadDim + 2 * hc;
-#pragma unroll
-      for (int k4 = 0; k4 < 4; ++k4) {
-        qb[k4][0] = tr < kGroup ? __ldg(reinterpret_cast<const uint32_t*>(qrow + k4 * 16)) : 0u;
-        qb[k4][1] = tr < kGroup ? __ldg(reinterpret_cast<const uint32_t*>(qrow + k4 * 16 + 8)) : 0u;
-      }
-    }
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    float acc[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    load_q_frags(p.q + (size_t)s * kOutRow + g * kGroup * kHeadDim, tl, qb);
+    HeadState st;
+    st.reset();
 
     for (int i = set; i < n; i += SETS) {
       for (const int kk = kbase + i; c_kk < kk; ++c_kk) {
@@ -380,80 +289,18 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
       if (have) {
         const int j = pg - first + i;
         valid = min(kPage, L - j * kPage);
-        const uint32_t sb = smem_base + stage * kStageBytes;
         if (valid < kPage) {
-          // Rows past the sequence end hold stale data: zero this head's V slice
-          // so that 0-probability rows cannot inject NaN/Inf into P.V.
-          unsigned char* vtile = smem + stage * kStageBytes + (kMaxKvHeads + g) * kTileBytes;
-          for (int idx = lane; idx < (kPage - valid) * 8; idx += 32) {
-            const int r = valid + (idx >> 3);  // whole 128-byte rows: swizzle-agnostic
-            *reinterpret_cast<uint4*>(vtile + r * 128 + (idx & 7) * 16) = make_uint4(0, 0, 0, 0);
-          }
+          zero_stale_v_rows(smem + stage * kStageBytes + v_off, valid, lane);
           zeroed = true;
           __syncwarp();
         }
-#pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4)
-          ldmatrix_x4(sb + k_lane + (((2 * k4 + k_chunk) ^ mrow) << 4), kf[k4][0], kf[k4][1],
-                      kf[k4][2], kf[k4][3]);
-#pragma unroll
-        for (int d = 0; d < 4; ++d)
-          ldmatrix_x4_trans(sb + v_lane + (((2 * d + v_chunk) ^ mrow) << 4), vf[d][0], vf[d][1],
-                            vf[d][2], vf[d][3]);
+        const uint32_t sb = smem_base + stage * kStageBytes;
+        load_tile_frags(sb + k_off, sb + v_off, tl, kf, vf);
       }
       if (zeroed) fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_addr(&empty_bar[stage]));
-      if (have) {
-        // S^T = K_g Q_g^T, as two independent accumulation chains (k 0-31, 32-63)
-        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-        float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
-#pragma unroll
-        for (int k4 = 0; k4 < 2; ++k4) {
-          mma_bf16_16816(s0, s1, s2, s3, kf[k4][0], kf[k4][1], kf[k4][2], kf[k4][3], qb[k4][0],
-                         qb[k4][1]);
-          mma_bf16_16816(t0, t1, t2, t3, kf[k4 + 2][0], kf[k4 + 2][1], kf[k4 + 2][2],
-                         kf[k4 + 2][3], qb[k4 + 2][0], qb[k4 + 2][1]);
-        }
-        float x0 = (s0 + t0) * p.scale_log2, x1 = (s1 + t1) * p.scale_log2;
-        float x2 = (s2 + t2) * p.scale_log2, x3 = (s3 + t3) * p.scale_log2;
-        if (valid < kPage) {
-          if (tr >= valid) x0 = x1 = -INFINITY;
-          if (tr + 8 >= valid) x2 = x3 = -INFINITY;
-        }
-        float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
-        const bool grow = !LAZY || __any_sync(0xffffffffu, mx0 > m0 + kLazyMargin ||
-                                                              mx1 > m1 + kLazyMargin);
-        float al0 = 1.f, al1 = 1.f;
-        if (grow) {
-#pragma unroll
-          for (int o = 4; o < 32; o <<= 1) {
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-          }
-          const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-          al0 = fast_exp2(m0 - mn0);
-          al1 = fast_exp2(m1 - mn1);
-          m0 = mn0;
-          m1 = mn1;
-        }
-        const uint32_t pa = pack_bf16x2(fast_exp2(x0 - m0), fast_exp2(x1 - m1));
-        const uint32_t pb = pack_bf16x2(fast_exp2(x2 - m0), fast_exp2(x3 - m1));
-        l0 = l0 * al0 + (bf16lo_to_f32(pa) + bf16lo_to_f32(pb));
-        l1 = l1 * al1 + (bf16hi_to_f32(pa) + bf16hi_to_f32(pb));
-        if (grow && __any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
-#pragma unroll
-          for (int d = 0; d < 4; ++d) {
-            acc[d][0] *= al0; acc[d][1] *= al1; acc[d][2] *= al0; acc[d][3] *= al1;
-          }
-        }
-        // O^T += V_g^T P^T
-        const uint32_t y0 = movmatrix_trans(pa), y1 = movmatrix_trans(pb);
-#pragma unroll
-        for (int d = 0; d < 4; ++d)
-          mma_bf16_16816(acc[d][0], acc[d][1], acc[d][2], acc[d][3], vf[d][0], vf[d][1], vf[d][2],
-                         vf[d][3], y0, y1);
-      }
+      if (have) attend_tile<LAZY>(st, kf, vf, qb, valid, tl, p.scale_log2);
     }
 
     if (SETS > 1) {
@@ -475,85 +322,40 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
         named_barrier_sync(1 + g, 64);
       };
       float mb0 = 0.f, mb1 = 0.f;
-      exchange(m0, m1, mb0, mb1);
+      exchange(st.m0, st.m1, mb0, mb1);
       if (set == 0) {
-        const float M0 = fmaxf(m0, mb0), M1 = fmaxf(m1, mb1);
-        wa0 = m0 == -INFINITY ? 0.f : exp2f(m0 - M0);
-        wa1 = m1 == -INFINITY ? 0.f : exp2f(m1 - M1);
+        const float M0 = fmaxf(st.m0, mb0), M1 = fmaxf(st.m1, mb1);
+        wa0 = st.m0 == -INFINITY ? 0.f : exp2f(st.m0 - M0);
+        wa1 = st.m1 == -INFINITY ? 0.f : exp2f(st.m1 - M1);
         wb0 = mb0 == -INFINITY ? 0.f : exp2f(mb0 - M0);
         wb1 = mb1 == -INFINITY ? 0.f : exp2f(mb1 - M1);
-        m0 = M0;
-        m1 = M1;
+        st.m0 = M0;
+        st.m1 = M1;
       }
       float lb0 = 0.f, lb1 = 0.f;
-      exchange(l0, l1, lb0, lb1);
-      l0 = l0 * wa0 + lb0 * wb0;
-      l1 = l1 * wa1 + lb1 * wb1;
+      exchange(st.l0, st.l1, lb0, lb1);
+      st.l0 = st.l0 * wa0 + lb0 * wb0;
+      st.l1 = st.l1 * wa1 + lb1 * wb1;
 #pragma unroll
       for (int d = 0; d < 4; ++d) {
 #pragma unroll
         for (int e = 0; e < 4; e += 2) {
           float b0 = 0.f, b1 = 0.f;
-          exchange(acc[d][e], acc[d][e + 1], b0, b1);
-          acc[d][e] = acc[d][e] * wa0 + b0 * wb0;      // columns 2hc
-          acc[d][e + 1] = acc[d][e + 1] * wa1 + b1 * wb1;  // columns 2hc + 1
+          exchange(st.acc[d][e], st.acc[d][e + 1], b0, b1);
+          st.acc[d][e] = st.acc[d][e] * wa0 + b0 * wb0;          // columns 2hc
+          st.acc[d][e + 1] = st.acc[d][e + 1] * wa1 + b1 * wb1;  // columns 2hc + 1
         }
       }
     }
 
     if (set == 0) {
-#pragma unroll
-      for (int o = 4; o < 32; o <<= 1) {
-        l0 += __shfl_xor_sync(0xffffffffu, l0, o);
-        l1 += __shfl_xor_sync(0xffffffffu, l1, o);
-      }
-      const int h0 = 2 * hc, h1 = 2 * hc + 1;
-      if (complete) {
-        if (hc < 2) {
-          const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
-          __nv_bfloat16* o = p.out + (size_t)s * kOutRow + g * kGroup * kHeadDim;
-#pragma unroll
-          for (int d = 0; d < 4; ++d) {
-            const int ch = 16 * d + tr;
-            o[h0 * kHeadDim + ch] = __float2bfloat16_rn(acc[d][0] * inv0);
-            o[h1 * kHeadDim + ch] = __float2bfloat16_rn(acc[d][1] * inv1);
-            o[h0 * kHeadDim + ch + 8] = __float2bfloat16_rn(acc[d][2] * inv0);
-            o[h1 * kHeadDim + ch + 8] = __float2bfloat16_rn(acc[d][3] * inv1);
-          }
-        }
-      } else {
-        const int slot = (int)c * 2 + (first <= p_begin ? 0 : 1);
-        float* part = p.partials + ((size_t)slot * kMaxKvHeads + g) * kPartialFloats;
-        if (hc < 2) {
-          if (tr == 0) {
-            part[h0] = m0; part[h1] = m1;
-            part[kGroup + h0] = l0; part[kGroup + h1] = l1;
-          }
-          float* po = part + 2 * kGroup;
-#pragma unroll
-          for (int d = 0; d < 4; ++d) {
-            const int ch = 16 * d + tr;
-            po[h0 * kHeadDim + ch] = acc[d][0];
-            po[h1 * kHeadDim + ch] = acc[d][1];
-            po[h0 * kHeadDim + ch + 8] = acc[d][2];
-            po[h1 * kHeadDim + ch + 8] = acc[d][3];
-          }
-        }
-        __threadfence();
-        __syncwarp();
-        int last = 0;
-        if (lane == 0) {
-          const int pieces = cta_of_page(end - 1, T, C) - cta_of_page(first, T, C) + 1;
-          const int old = atomicAdd(p.counters + (size_t)s * kMaxKvHeads + g, 1);
-          last = (old == pieces - 1);
-          if (last) {
-            atomicExch(p.counters + (size_t)s * kMaxKvHeads + g, 0);
-            __threadfence();
-          }
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) combine_sequence(p, s, first, end, g, T, C, lane);
-      }
+      reduce_l(st);
+      __nv_bfloat16* out_group = p.out + (size_t)s * kOutRow + g * kGroup * kHeadDim;
+      if (complete)
+        write_output(st, out_group, tl);
+      else
+        finish_partial(st, p.partials, p.counters, kMaxKvHeads, g, s,
+                       partial_slot((int)c, first, T, C), first, end, T, C, out_group, tl, lane);
     }
     kbase += n;
     pg = piece_end;
@@ -576,9 +378,9 @@ constexpr size_t decode_smem_bytes() {
 }
 
 cudaError_t launch_decode_plan(const int32_t* lens, int batch, int table_stride, int num_ctas,
-                               int32_t* header, int32_t* cu, int32_t* counters, int32_t* err,
-                               cudaStream_t stream) {
-  decode_plan_kernel<<<1, 1024, 0, stream>>>(lens, batch, table_stride, num_ctas, kMaxKvHeads,
+                               int kv_heads, int32_t* header, int32_t* cu, int32_t* counters,
+                               int32_t* err, cudaStream_t stream) {
+  decode_plan_kernel<<<1, 1024, 0, stream>>>(lens, batch, table_stride, num_ctas, kv_heads,
                                              header, cu, counters, err);
   return cudaGetLastError();
 }
@@ -600,26 +402,30 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// Tensor map over one pool viewed as `rows` rows of 512 BF16 channels (1 KiB
-// pitch); box = 64 channels (one KV head, 128 B) x 16 rows (one page), 128-byte
-// swizzle.  Recently used maps are kept per thread (encoding is host work).
-bool pool_tensor_map(const void* pool, long long rows, CUtensorMap* out) {
+}  // namespace
+
+// Tensor map over one pool viewed as `rows` rows of kv_heads x 64 BF16
+// channels; box = 64 channels (one KV head, 128 B) x 16 rows (one page),
+// 128-byte swizzle.  Recently used maps are kept per thread (encoding is host
+// work).
+bool pool_tensor_map(const void* pool, long long rows, int kv_heads, CUtensorMap* out) {
   struct Entry {
     const void* pool;
     long long rows;
+    int kv_heads;
     CUtensorMap map;
   };
   static thread_local Entry cache[4];
   static thread_local int next = 0;
   for (const Entry& e : cache)
-    if (e.pool == pool && e.rows == rows) {
+    if (e.pool == pool && e.rows == rows && e.kv_heads == kv_heads) {
       *out = e.map;
       return true;
     }
   PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   if (!encode) return false;
-  const cuuint64_t dims[2] = {(cuuint64_t)(kMaxKvHeads * kHeadDim), (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)(kMaxKvHeads * kHeadDim * 2)};
+  const cuuint64_t dims[2] = {(cuuint64_t)(kv_heads * kHeadDim), (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(kv_heads * kHeadDim * 2)};
   const cuuint32_t box[2] = {(cuuint32_t)kHeadDim, (cuuint32_t)kPage};
   const cuuint32_t elem_strides[2] = {1, 1};
   CUtensorMap map;
@@ -627,13 +433,11 @@ bool pool_tensor_map(const void* pool, long long rows, CUtensorMap* out) {
              box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return false;
-  cache[next] = {pool, rows, map};
+  cache[next] = {pool, rows, kv_heads, map};
   next = (next + 1) % 4;
   *out = map;
   return true;
 }
-
-}  // namespace
 
 namespace {
 
@@ -648,8 +452,7 @@ DecodeForm decode_form(int dev) {
   cudaFuncAttributes fa;
   constexpr int threads = decode_threads<2, true>();
   if (cudaFuncGetAttributes(&fa, paged_decode_kernel<kSplitStages, 2, true, true>) == cudaSuccess &&
-      (long long)fa.numRegs * threads >=
-          128LL * kProducerRegs + (long long)(threads - 128) * kConsumerRegs &&
+      regsplit_fits(fa.numRegs, threads) &&
       cudaFuncSetAttribute(paged_decode_kernel<kSplitStages, 2, true, true>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)decode_smem_bytes<kSplitStages, 2>()) == cudaSuccess)
@@ -670,12 +473,13 @@ cudaError_t launch_paged_decode(const DecodeParams& p, long long pool_rows, int 
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  CUtensorMap k_map, v_map;
+  if (!pool_tensor_map(p.k_pool, pool_rows, p.kv_heads, &k_map) ||
+      !pool_tensor_map(p.v_pool, pool_rows, p.kv_heads, &v_map))
+    return cudaErrorInvalidValue;
+  if (p.kv_heads != kMaxKvHeads) return launch_paged_decode_heads(p, k_map, v_map, num_ctas, stream);
   const DecodeForm form = decode_form(dev);
   if (form == DecodeForm::kUnknown) return cudaErrorInvalidDeviceFunction;
-  CUtensorMap k_map, v_map;
-  if (!pool_tensor_map(p.k_pool, pool_rows, &k_map) ||
-      !pool_tensor_map(p.v_pool, pool_rows, &v_map))
-    return cudaErrorInvalidValue;
   if (form == DecodeForm::kSplit)
     paged_decode_kernel<kSplitStages, 2, true, true>
         <<<num_ctas, decode_threads<2, true>(), decode_smem_bytes<kSplitStages, 2>(), stream>>>(

@@ -56,7 +56,10 @@ int tvp_paged_decode_attention_noalloc(const tvp_bf16* q, const tvp_bf16* k_pool
                                        tvp_stream_t stream) {
   if (batch <= 0 || num_ctas < 0) return TVP_ERR_INVALID_ARGUMENT;
   const size_t need = tvp_decode_workspace_bytes(batch, kv_heads, num_ctas);
-  if (need == 0) return kv_heads != TVP_KV_HEADS ? TVP_ERR_UNSUPPORTED : TVP_ERR_RUNTIME;
+  if (need == 0)
+    return (kv_heads == 1 || kv_heads == 2 || kv_heads == 4 || kv_heads == TVP_KV_HEADS)
+               ? TVP_ERR_RUNTIME
+               : TVP_ERR_UNSUPPORTED;
   if (need > kStaticWorkspaceBytes) return TVP_ERR_WORKSPACE;  // batch or grid too large
   void* ws = nullptr;
   const int rc = static_workspace(&ws);

@@ -42,6 +42,7 @@ struct DecodeParams {
   int num_pages;
   int table_stride;
   int batch;
+  int kv_heads;      // KV heads the pools hold (1, 2, 4 or 8)
   float scale_log2;  // scale * log2(e)
   int32_t* err;
 };
@@ -57,6 +58,7 @@ struct CompatParams {
   long long layer_row_base;
   int num_pages;
   int table_stride;
+  int kv_heads;
   float scale;
   int32_t* err;
 };
@@ -66,10 +68,16 @@ constexpr int kPartialFloats = 2 * kGroup + kGroup * kHeadDim;
 
 cudaError_t launch_rope_append(const AppendParams& p, int num_tokens, cudaStream_t stream);
 cudaError_t launch_decode_plan(const int32_t* lens, int batch, int table_stride, int num_ctas,
-                               int32_t* header, int32_t* cu, int32_t* counters, int32_t* err,
-                               cudaStream_t stream);
+                               int kv_heads, int32_t* header, int32_t* cu, int32_t* counters,
+                               int32_t* err, cudaStream_t stream);
+// Dispatches on p.kv_heads: 8 -> tvp_decode.cu, 1, 2, 4 -> tvp_decode_heads.cu.
 cudaError_t launch_paged_decode(const DecodeParams& p, long long pool_rows, int num_ctas,
                                 cudaStream_t stream);
+cudaError_t launch_paged_decode_heads(const DecodeParams& p, const CUtensorMap& k_map,
+                                      const CUtensorMap& v_map, int num_ctas,
+                                      cudaStream_t stream);
+// 2-D tensor map over a pool of `rows` token rows of kv_heads x 64 channels.
+bool pool_tensor_map(const void* pool, long long rows, int kv_heads, CUtensorMap* out);
 cudaError_t launch_compat_decode(const CompatParams& p, int batch, cudaStream_t stream);
 
 }  // namespace tvp

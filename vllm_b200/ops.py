@@ -7,7 +7,10 @@ Shapes (reference geometry, src/model/paged_kvcache.cu:10-11):
   k_pool, v_pool : bf16 [num_layers, num_pages, 16, kv_heads * 64]
   block_tables   : int32 [batch, table_stride]   (-1 = no page)
   seq_lens       : int32 [batch]                 attended length L per row
-  q, out         : bf16 [batch, 32 * 64]         head h at h * 64
+  q, out         : bf16 [batch, 4 * kv_heads * 64]  head h at h * 64
+
+kv_heads is the model's 8, or the 4, 2 or 1 heads one GPU holds when the KV
+heads are sharded over 2, 4 or 8 GPUs (``vllm_b200.sharding``).
 """
 from __future__ import annotations
 
@@ -97,20 +100,22 @@ def rope_append(k_pool, v_pool, layer, block_tables, token_pos, k, v, q=None, to
 
 
 class DecodeWorkspace:
-    """Device workspace of the decode path for up to ``max_batch`` rows and a
-    fixed grid (``num_ctas`` CTAs, 0 = one per SM)."""
+    """Device workspace of the decode path for up to ``max_batch`` rows of a
+    pool of ``kv_heads`` KV heads and a fixed grid (``num_ctas`` CTAs, 0 = one
+    per SM)."""
 
-    def __init__(self, max_batch: int, device=None, num_ctas: int = 0):
+    def __init__(self, max_batch: int, device=None, num_ctas: int = 0, kv_heads: int = N.KV_HEADS):
         lib = N.load()
         device = torch.device(device if device is not None else "cuda")
         with torch.cuda.device(device):
             sms = ctypes.c_int(0)
             N.check(lib.tvp_device_sm_count(ctypes.byref(sms)), "tvp_device_sm_count")
             self.num_ctas = num_ctas if num_ctas > 0 else sms.value
-            self.nbytes = int(lib.tvp_decode_workspace_bytes(max_batch, N.KV_HEADS, self.num_ctas))
+            self.nbytes = int(lib.tvp_decode_workspace_bytes(max_batch, kv_heads, self.num_ctas))
         if self.nbytes == 0:
             raise ValueError("invalid workspace request")
         self.max_batch = max_batch
+        self.kv_heads = kv_heads
         self.buffer = torch.empty(self.nbytes, dtype=torch.uint8, device=device)
         self.batch = None
 
@@ -122,8 +127,10 @@ def decode_plan(seq_lens, table_stride, workspace: DecodeWorkspace, error=None, 
     batch = seq_lens.numel()
     if batch > workspace.max_batch:
         raise ValueError("batch larger than the workspace was sized for")
-    workspace.nbytes_needed = int(lib.tvp_decode_workspace_bytes(batch, N.KV_HEADS, workspace.num_ctas))
-    rc = lib.tvp_decode_plan(_ptr(seq_lens), batch, table_stride, N.KV_HEADS, workspace.num_ctas,
+    workspace.nbytes_needed = int(lib.tvp_decode_workspace_bytes(batch, workspace.kv_heads,
+                                                                 workspace.num_ctas))
+    rc = lib.tvp_decode_plan(_ptr(seq_lens), batch, table_stride, workspace.kv_heads,
+                             workspace.num_ctas,
                              _ptr(workspace.buffer), workspace.nbytes, _ptr(error), _stream(stream))
     N.check(rc, "tvp_decode_plan")
     workspace.batch = batch
@@ -143,7 +150,7 @@ def paged_decode_attention(q, k_pool, v_pool, layer, block_tables, seq_lens, wor
     _need(seq_lens, "seq_lens", torch.int32, dev)
     batch = seq_lens.numel()
     if q.shape != (batch, kv_heads * N.GQA_GROUP * N.HEAD_DIM):
-        raise ValueError("q must be [batch, 32*64]")
+        raise ValueError("q must be [batch, 4*kv_heads*64]")
     if block_tables.dim() != 2 or block_tables.shape[0] < batch:
         raise ValueError("block_tables must be [>=batch, table_stride]")
     if out is None:
@@ -153,6 +160,8 @@ def paged_decode_attention(q, k_pool, v_pool, layer, block_tables, seq_lens, wor
     if mode == N.TVP_MODE_FAST:
         if workspace is None or workspace.batch != batch:
             raise ValueError("FAST mode needs a workspace planned for this batch")
+        if workspace.kv_heads != kv_heads:
+            raise ValueError(f"workspace was sized for {workspace.kv_heads} KV heads, pools hold {kv_heads}")
         ws_ptr, ws_bytes, ctas = _ptr(workspace.buffer), workspace.nbytes, workspace.num_ctas
     rc = lib.tvp_paged_decode_attention(_ptr(q), _ptr(k_pool), _ptr(v_pool), num_pages, num_layers,
                                         layer, kv_heads, kv_heads * N.GQA_GROUP,

@@ -5,7 +5,9 @@ of requests, its own page pool and block tables, and no data-path collective
 is needed.  Rows are assigned longest-first to the GPU with the least attended
 tokens so far (greedy LPT), which bounds the slowest GPU to within one row of
 the mean.  KV-head sharding splits the 8 KV heads (and their 4 query heads
-each) evenly over 1, 2, 4 or 8 GPUs.
+each) evenly over 1, 2, 4 or 8 GPUs: every GPU keeps all pages and the same
+block tables, but only its heads' channels, and the per-rank attention
+outputs are all-gathered into the model's [B, 2048] rows.
 """
 from __future__ import annotations
 
@@ -34,6 +36,94 @@ def shard_by_kv_head(world: int, kv_heads: int = 8) -> list[range]:
         raise ValueError("world must divide the number of KV heads")
     per = kv_heads // world
     return [range(r * per, (r + 1) * per) for r in range(world)]
+
+
+def head_channels(heads: range, head_dim: int = 64, group: int = 1) -> slice:
+    """Channel slice of ``heads`` in a row of ``group`` x head_dim channels per head
+    (group 1: a KV pool row; group 4: a q or attention-output row)."""
+    return slice(heads.start * group * head_dim, heads.stop * group * head_dim)
+
+
+def slice_kv_heads(pool, heads: range):
+    """A rank's pool [layers, pages, 16, len(heads) * 64] cut from the model's
+    [layers, pages, 16, 8 * 64]: same pages, same block tables, fewer channels."""
+    return pool[..., head_channels(heads)]
+
+
+def slice_q_heads(q, heads: range):
+    """A rank's query rows [B, 4 * len(heads) * 64] (query heads 4k .. 4k + 3 of
+    each of its KV heads k)."""
+    return q[..., head_channels(heads, group=4)]
+
+
+def interleave_head_shards(gathered):
+    """[world, B, 4 * kv_per_rank * 64] -> [B, world * 4 * kv_per_rank * 64]:
+    the all-gathered per-rank outputs back in the model's head-major row
+    layout (rank r's heads are contiguous and ranks own increasing heads)."""
+    world, batch, width = gathered.shape
+    if hasattr(gathered, "permute"):
+        return gathered.permute(1, 0, 2).reshape(batch, world * width)
+    return gathered.transpose(1, 0, 2).reshape(batch, world * width)
+
+
+def all_gather_head_shards(local, gathered_flat, group=None):
+    """All-gathers every rank's [B, width] attention slice over ``group`` into
+    the first world * B rows of ``gathered_flat`` ([>= world * B, width]) and
+    returns the [B, world * width] model rows."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    batch, width = local.shape
+    gathered = gathered_flat[:world * batch]
+    dist.all_gather_into_tensor(gathered, local, group=group)
+    return interleave_head_shards(gathered.view(world, batch, width))
+
+
+class HeadShardedDecode:
+    """One rank of KV-head-sharded decode attention: rank r holds KV heads
+    ``shard_by_kv_head(world)[r]`` of every page, runs the fused decode over
+    them and all-gathers the [B, 4 * kv_per_rank * 64] slices over the process
+    group (NCCL on GPUs) into the model's [B, 2048] rows.
+
+    The gather buffers are allocated once for ``max_batch`` rows.
+    """
+
+    def __init__(self, max_batch: int, group=None, device=None, num_ctas: int = 0):
+        import torch
+        import torch.distributed as dist
+
+        from . import ops
+
+        self.dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.heads = shard_by_kv_head(self.world)[self.rank]
+        self.kv_heads = len(self.heads)
+        self.device = torch.device(device if device is not None else "cuda")
+        self.workspace = ops.DecodeWorkspace(max_batch, self.device, num_ctas=num_ctas,
+                                             kv_heads=self.kv_heads)
+        self.width = 4 * self.kv_heads * 64
+        self.local = torch.empty((max_batch, self.width), dtype=torch.bfloat16, device=self.device)
+        # flat [world * B, width]: rank r's rows at [r B, (r + 1) B) for any B <= max_batch
+        self.gathered = torch.empty((self.world * max_batch, self.width), dtype=torch.bfloat16,
+                                    device=self.device)
+
+    def plan(self, seq_lens, table_stride: int, error=None, stream=None):
+        from . import ops
+        ops.decode_plan(seq_lens, table_stride, self.workspace, error=error, stream=stream)
+
+    def attend(self, q_local, k_pool, v_pool, layer, block_tables, seq_lens, error=None,
+               gather=True):
+        """Decode attention of this rank's heads; with ``gather`` the all-gather
+        over the group follows and the [B, 2048] rows are returned."""
+        from . import ops
+        batch = seq_lens.numel()
+        local = self.local[:batch]
+        ops.paged_decode_attention(q_local, k_pool, v_pool, layer, block_tables, seq_lens,
+                                   self.workspace, out=local, error=error)
+        if not gather:
+            return local
+        return all_gather_head_shards(local, self.gathered, self.group)
 
 
 def imbalance(lens, shards) -> float:
