@@ -310,6 +310,14 @@ def run_ours(args, rank, world, local_rank):
     e2e_value = kv_step * world / (e2e_ms / 1e3) / 1e9
     assert int(err.item()) == 0, f"device error bits {int(err.item())}"
 
+    # KV-head-sharded long_context (every rank takes part; after the timed runs)
+    head_sharded = None
+    if world > 1 and W.KV_HEADS % world == 0 and not args.no_extras:
+        del k_pool, v_pool
+        torch.cuda.empty_cache()
+        k_pool = v_pool = None
+        head_sharded = bench_head_sharded(dev, rank, world, local_rank)
+
     if rank != 0:
         return
     peak, peak_kind = hbm_peak()
@@ -340,6 +348,8 @@ def run_ours(args, rank, world, local_rank):
     }
     if world == 1 and not args.no_extras:
         line.update(extras(args, dev, case, k_pool, v_pool, q_all, out, tables, seq_lens, ws))
+    if head_sharded is not None:
+        line["long_context_head_sharded"] = head_sharded
     if world == 1 and not args.no_cpu_baseline:
         cb, _ = time_cpu(32, args.cpu_seconds)
         line["cpu_baseline"] = cb
@@ -377,6 +387,7 @@ def extras(args, dev, case, k_pool, v_pool, q_all, out, tables, seq_lens, ws):
     res["parity_spot_check"] = {"rows": rows, "layer": layer, "max_abs_err_vs_exact": worst,
                                 "tolerance": "1e-2 abs + 2e-2 rel"}
     res["long_context"] = bench_long_context(dev)
+    res["long_context_head_shards"] = bench_long_context_heads(dev)
     res["decode_small"] = bench_decode_small(dev)
     res["e2e_llama"] = bench_e2e_llama()
     return res
@@ -443,6 +454,107 @@ def bench_long_context(dev, iters=20):
     return {"workload": "long_context 16 x 32768, 1 layer, split-K", "us_per_launch": round(ms * 1e3, 2),
             "GBps": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4), "peak_source": kind,
             "inputs": "larger than L2 (1.07 GB per launch)"}
+
+
+def long_context_pools(dev, kv_heads, seed=99):
+    """long_context geometry (16 x 32768, 1 layer) with pools of kv_heads heads."""
+    import torch
+    case = W.long_context(seed=5, batch=16, L=32768, num_layers=1)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    shape = (1, case.num_pages, 16, kv_heads * W.HEAD_DIM)
+    kp = torch.empty(shape, dtype=torch.bfloat16, device=dev).normal_(generator=gen)
+    vp = torch.empty(shape, dtype=torch.bfloat16, device=dev).normal_(generator=gen)
+    q = torch.randn((16, kv_heads * W.GROUP * W.HEAD_DIM), generator=gen, device=dev)
+    return case, kp, vp, q.to(torch.bfloat16)
+
+
+def head_shard_bytes(lens, kv_heads):
+    """Algorithmic bytes of one decode launch over kv_heads of the 8 KV heads."""
+    nb = algorithmic_bytes(lens)
+    kv = nb["kv"] * kv_heads // W.KV_HEADS
+    return kv + nb["q_out"] * kv_heads // W.KV_HEADS + nb["tables"], kv
+
+
+def bench_long_context_heads(dev, iters=20):
+    """One GPU's share of KV-head-sharded long_context: the head-shard kernel on
+    pools of 4, 2 and 1 KV heads (the 2-, 4- and 8-GPU shards)."""
+    import torch
+    from vllm_b200 import ops
+    peak, kind = hbm_peak()
+    res = {"workload": "long_context 16 x 32768, 1 layer, pools of kv_heads of the 8 heads",
+           "peak_source": kind}
+    for kv_heads in (4, 2, 1):
+        case, kp, vp, q = long_context_pools(dev, kv_heads)
+        tables = torch.from_numpy(case.tables).to(dev)
+        lens = torch.from_numpy(case.lens).to(dev)
+        ws = ops.DecodeWorkspace(16, dev, kv_heads=kv_heads)
+        ops.decode_plan(lens, case.tables.shape[1], ws)
+        out = torch.empty_like(q)
+        for _ in range(3):
+            ops.paged_decode_attention(q, kp, vp, 0, tables, lens, ws, out=out)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(iters)]
+        torch.cuda.synchronize(dev)
+        for a, b in ev:
+            a.record()
+            ops.paged_decode_attention(q, kp, vp, 0, tables, lens, ws, out=out)
+            b.record()
+        torch.cuda.synchronize(dev)
+        ms = statistics.median(a.elapsed_time(b) for a, b in ev)
+        total, _ = head_shard_bytes(case.lens, kv_heads)
+        gbs = total / (ms / 1e3) / 1e9
+        res[f"kv_heads_{kv_heads}"] = {"us_per_launch": round(ms * 1e3, 2), "GBps": round(gbs, 1),
+                                       "frac_of_peak": round(gbs / peak, 4),
+                                       "bytes_per_launch": total}
+        del kp, vp
+        torch.cuda.empty_cache()
+    return res
+
+
+def bench_head_sharded(dev, rank, world, local_rank, iters=20):
+    """KV-head-sharded long_context over `world` GPUs: rank r holds 8 / world
+    KV heads of every page, runs the head-shard kernel and all-gathers the
+    attention slices over NCCL into [16, 2048].  Per-layer time is the max over
+    ranks of CUDA-event time on the launching stream."""
+    import torch
+    import torch.distributed as dist
+    from vllm_b200 import sharding
+    kv_heads = W.KV_HEADS // world
+    case, kp, vp, q = long_context_pools(dev, kv_heads, seed=99 + rank)
+    tables = torch.from_numpy(case.tables).to(dev)
+    lens = torch.from_numpy(case.lens).to(dev)
+    dec = sharding.HeadShardedDecode(16, device=dev)
+    dec.plan(lens, case.tables.shape[1])
+    for _ in range(3):
+        dec.attend(q, kp, vp, 0, tables, lens)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(gather):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(iters)]
+        dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(dev)
+        for a, b in ev:
+            a.record(stream)
+            dec.attend(q, kp, vp, 0, tables, lens, gather=gather)
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = statistics.median(a.elapsed_time(b) for a, b in ev)
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms_decode = timed(False)
+    ms_total = timed(True)
+    del kp, vp
+    torch.cuda.empty_cache()
+    nb = algorithmic_bytes(case.lens)
+    return {"workload": f"long_context 16 x 32768, 1 layer, {kv_heads} KV head(s) per GPU",
+            "us_per_layer": round(ms_total * 1e3, 2), "us_decode_only": round(ms_decode * 1e3, 2),
+            "aggregate_kv_GBps": round(nb["kv"] / (ms_total / 1e3) / 1e9, 1),
+            "all_gather_bytes_per_rank": 16 * kv_heads * W.GROUP * W.HEAD_DIM * 2,
+            "collective": "NCCL all_gather_into_tensor"}
 
 
 def bench_decode_small(dev, iters=50):
@@ -513,6 +625,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--only", choices=["long_context", "long_context_heads", "decode_small"],
+                    help="run one single-GPU sub-measurement alone and print its JSON (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -521,6 +635,14 @@ def main():
     local_rank = env_int("LOCAL_RANK", 0)
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
+        return
+    if args.only:
+        import torch
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        fn = {"long_context": bench_long_context, "long_context_heads": bench_long_context_heads,
+              "decode_small": bench_decode_small}[args.only]
+        print(json.dumps({args.only: fn(dev)}), flush=True)
         return
     import torch
     import torch.distributed as dist

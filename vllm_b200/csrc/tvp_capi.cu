@@ -12,15 +12,17 @@ namespace {
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct WorkspaceLayout {
-  size_t header, cu, counters, partials, total;
+  size_t header, cu, cta_seq, counters, partials, total;
 };
 
-// header | cu[batch + 1] | counters[batch][kv_heads] | partials[2 num_ctas][kv_heads]
+// header | cu[batch + 1] | cta_seq[num_ctas] | counters[batch][kv_heads] |
+// partials[2 num_ctas][kv_heads]
 WorkspaceLayout workspace_layout(int batch, int kv_heads, int num_ctas) {
   WorkspaceLayout w;
   w.header = 0;
   w.cu = 256;
-  w.counters = align_up(w.cu + (size_t)(batch + 1) * 4, 256);
+  w.cta_seq = align_up(w.cu + (size_t)(batch + 1) * 4, 256);
+  w.counters = align_up(w.cta_seq + (size_t)num_ctas * 4, 256);
   w.partials = align_up(w.counters + (size_t)batch * kv_heads * 4, 256);
   w.total = align_up(w.partials + (size_t)num_ctas * 2 * kv_heads * kPartialFloats * 4, 256);
   return w;
@@ -144,6 +146,7 @@ int tvp_decode_plan(const int32_t* d_seq_lens, int batch, int table_stride, int 
   return map_cuda(launch_decode_plan(d_seq_lens, batch, table_stride, ctas, kv_heads,
                                      reinterpret_cast<int32_t*>(base + w.header),
                                      reinterpret_cast<int32_t*>(base + w.cu),
+                                     reinterpret_cast<int32_t*>(base + w.cta_seq),
                                      reinterpret_cast<int32_t*>(base + w.counters), d_error,
                                      static_cast<cudaStream_t>(stream)));
 }
@@ -197,6 +200,7 @@ int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const 
   p.seq_lens = d_seq_lens;
   p.header = reinterpret_cast<const int32_t*>(base + w.header);
   p.cu = reinterpret_cast<const int32_t*>(base + w.cu);
+  p.cta_seq = reinterpret_cast<const int32_t*>(base + w.cta_seq);
   p.counters = reinterpret_cast<int32_t*>(base + w.counters);
   p.partials = reinterpret_cast<float*>(base + w.partials);
   p.layer_row_base = layer_row_base;

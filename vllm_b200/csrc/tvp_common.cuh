@@ -72,7 +72,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
   }
 }
 
-// ---- bulk copy global -> shared (TMA, no tensor map, no multicast) --------
+// ---- bulk copy global -> shared (TMA, no tensor map, this CTA only) -------
 __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uint32_t bytes,
                                               uint32_t bar) {
   asm volatile(
@@ -82,7 +82,7 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uin
       : "memory");
 }
 
-// ---- tiled TMA load of a 2-D box (tensor map, no multicast) ---------------
+// ---- tiled TMA load of a 2-D box (tensor map, this CTA only) --------------
 // x is the innermost (element) coordinate; x * sizeof(element) must be a
 // multiple of 16 bytes.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,

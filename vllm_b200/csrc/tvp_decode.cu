@@ -42,11 +42,12 @@ constexpr int kMergeFields = 2;  // per-lane values exchanged per merge round (s
 
 
 // ---------------------------------------------------------------------------
-// Plan: cu[b] = sum_{i<b} ceil(L_i / 16), header, counters = 0.
+// Plan: cu[b] = sum_{i<b} ceil(L_i / 16), cta_seq[c] = the sequence holding
+// CTA c's first page, header, counters = 0.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024)
     decode_plan_kernel(const int32_t* __restrict__ lens, int batch, int table_stride,
-                       int num_ctas, int groups, int32_t* header, int32_t* cu,
+                       int num_ctas, int groups, int32_t* header, int32_t* cu, int32_t* cta_seq,
                        int32_t* counters, int32_t* err) {
   __shared__ int warp_sums[32];
   __shared__ int carry;
@@ -83,6 +84,17 @@ __global__ void __launch_bounds__(1024)
     __syncthreads();
     if (tid == 0) carry += warp_sums[31];
     __syncthreads();
+  }
+  // CTA c of C = min(num_ctas, T) starts at page floor(c T / C), which lies in
+  // sequence s exactly when ceil(cu[s] C / T) <= c < ceil(cu[s + 1] C / T):
+  // every sequence writes its own CTAs (empty sequences none).  cu[] was
+  // written by this block before the last barrier of the scan: plain loads.
+  const long long T = carry;
+  const long long C = T < num_ctas ? T : num_ctas;
+  for (int s = tid; s < batch && C > 0; s += blockDim.x) {
+    const long long a = cu[s];
+    const long long b = s + 1 < batch ? (long long)cu[s + 1] : T;
+    for (long long c = (a * C + T - 1) / T; c < (b * C + T - 1) / T; ++c) cta_seq[c] = s;
   }
   if (tid == 0) {
     cu[batch] = carry;
@@ -143,16 +155,8 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
   const int p_end = c < C ? (int)((c + 1) * T / C) : 0;
   const uint32_t smem_base = smem_addr(smem);
 
-  // First sequence of the range: the s with cu[s] <= p_begin < cu[s + 1].
-  int s0 = 0;
-  if (p_begin < p_end) {
-    int lo = 0, hi = p.batch;  // invariant: cu[lo] <= p_begin < cu[hi]
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      if (__ldg(p.cu + mid) <= p_begin) lo = mid; else hi = mid;
-    }
-    s0 = lo;
-  }
+  // First sequence of the range (the s with cu[s] <= p_begin < cu[s + 1]), from the plan.
+  const int s0 = p_begin < p_end ? __ldg(p.cta_seq + c) : 0;
 
   if (warp >= SETS * kMaxKvHeads) {
     // ------------------------------ producer ------------------------------
@@ -176,7 +180,7 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
     int next_phys = p_begin < p_end
                         ? __ldg(p.tables + (size_t)s * p.table_stride + (p_begin - seq_first))
                         : 0;
-    int stage = 0;
+    int stage = 0, issued = 0;
     uint32_t empty_parity = 1;  // parity of the previous round of each slot
     for (int pg = p_begin, kk = 0; pg < p_end; ++pg, ++kk) {
       const int phys = next_phys;
@@ -188,6 +192,7 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
         }
         next_phys = __ldg(p.tables + (size_t)s * p.table_stride + (pg + 1 - seq_first));
       }
+      if (*abort_flag) break;  // a consumer gave up: issue nothing more
       if (kk >= STAGES) {
         int timed_out = 0;
         if (lane == 0) timed_out = !mbar_wait_bounded(smem_addr(&empty_bar[stage]), empty_parity);
@@ -215,11 +220,13 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
         tma_load_2d(dst, lane < kMaxKvHeads ? &k_map : &v_map, h * kHeadDim,
                     (int)(p.layer_row_base + (long long)phys * kPage), full);
       }
+      issued = kk + 1;
       if (++stage == STAGES) {
         stage = 0;
         empty_parity ^= 1u;
       }
     }
+    drain_issued_stages<STAGES>(full_bar, issued, lane, p.err);
     return;
   }
 
@@ -299,7 +306,9 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
       }
       if (zeroed) fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&empty_bar[stage]));
+      // A stage is released only after its copies landed (a consumer that gave
+      // up keeps it, so the producer cannot reuse a slot with a copy in flight).
+      if (ready && lane == 0) mbar_arrive(smem_addr(&empty_bar[stage]));
       if (have) attend_tile<LAZY>(st, kf, vf, qb, valid, tl, p.scale_log2);
     }
 
@@ -378,10 +387,10 @@ constexpr size_t decode_smem_bytes() {
 }
 
 cudaError_t launch_decode_plan(const int32_t* lens, int batch, int table_stride, int num_ctas,
-                               int kv_heads, int32_t* header, int32_t* cu, int32_t* counters,
-                               int32_t* err, cudaStream_t stream) {
+                               int kv_heads, int32_t* header, int32_t* cu, int32_t* cta_seq,
+                               int32_t* counters, int32_t* err, cudaStream_t stream) {
   decode_plan_kernel<<<1, 1024, 0, stream>>>(lens, batch, table_stride, num_ctas, kv_heads,
-                                             header, cu, counters, err);
+                                             header, cu, cta_seq, counters, err);
   return cudaGetLastError();
 }
 

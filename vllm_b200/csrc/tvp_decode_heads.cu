@@ -145,15 +145,7 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
   const int n = p_end - p_begin;
   const uint32_t smem_base = smem_addr(smem);
 
-  int s0 = 0;
-  if (n > 0) {
-    int lo = 0, hi = p.batch;  // invariant: cu[lo] <= p_begin < cu[hi]
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      if (__ldg(p.cu + mid) <= p_begin) lo = mid; else hi = mid;
-    }
-    s0 = lo;
-  }
+  const int s0 = n > 0 ? __ldg(p.cta_seq + c) : 0;  // sequence of the range's first page
 
   if (warp >= 2 * kStageTiles) {
     // ------------------------------ producer ------------------------------
@@ -184,13 +176,14 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
       walk();
     }
     const int n_stages = (n + PS - 1) / PS;
-    int stage = 0;
+    int stage = 0, issued = 0;
     uint32_t empty_parity = 1;
     for (int kk = 0; kk < n_stages; ++kk) {
       const int cur_phys = phys;
       const bool mine = lane < PS && i < n;
       i += PS;
       if (lane < PS && i < n) walk();
+      if (*abort_flag) break;  // a consumer gave up: issue nothing more
       if (kk >= STAGES) {
         int timed_out = 0;
         if (lane == 0) timed_out = !mbar_wait_bounded(smem_addr(&empty_bar[stage]), empty_parity);
@@ -220,11 +213,13 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
         tma_load_2d(dst, lane < kStageTiles ? &k_map : &v_map, h * kHeadDim,
                     (int)(p.layer_row_base + (long long)tile_phys * kPage), full);
       }
+      issued = kk + 1;
       if (++stage == STAGES) {
         stage = 0;
         empty_parity ^= 1u;
       }
     }
+    drain_issued_stages<STAGES>(full_bar, issued, lane, p.err);
     return;
   }
 
@@ -295,7 +290,9 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
       }
       if (zeroed) fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&empty_bar[stage]));
+      // A stage is released only after its copies landed (a consumer that gave
+      // up keeps it, so the producer cannot reuse a slot with a copy in flight).
+      if (ready && lane == 0) mbar_arrive(smem_addr(&empty_bar[stage]));
       if (have) attend_tile<true>(st, kf, vf, qb, valid, tl, p.scale_log2);
     }
 

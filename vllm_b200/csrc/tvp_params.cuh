@@ -36,6 +36,7 @@ struct DecodeParams {
   const int32_t* seq_lens;
   const int32_t* header;
   const int32_t* cu;
+  const int32_t* cta_seq;  // per CTA: the sequence holding its first page
   int32_t* counters;
   float* partials;
   long long layer_row_base;  // layer * num_pages * 16
@@ -68,8 +69,8 @@ constexpr int kPartialFloats = 2 * kGroup + kGroup * kHeadDim;
 
 cudaError_t launch_rope_append(const AppendParams& p, int num_tokens, cudaStream_t stream);
 cudaError_t launch_decode_plan(const int32_t* lens, int batch, int table_stride, int num_ctas,
-                               int kv_heads, int32_t* header, int32_t* cu, int32_t* counters,
-                               int32_t* err, cudaStream_t stream);
+                               int kv_heads, int32_t* header, int32_t* cu, int32_t* cta_seq,
+                               int32_t* counters, int32_t* err, cudaStream_t stream);
 // Dispatches on p.kv_heads: 8 -> tvp_decode.cu, 1, 2, 4 -> tvp_decode_heads.cu.
 cudaError_t launch_paged_decode(const DecodeParams& p, long long pool_rows, int num_ctas,
                                 cudaStream_t stream);

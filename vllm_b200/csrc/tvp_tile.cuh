@@ -65,6 +65,25 @@ struct TileLane {
   }
 };
 
+// Abort-safe end of a producer: no copy into this CTA's shared memory may be in
+// flight when the CTA exits.  After a wait gave up, consumers stop releasing
+// stages and the producer stops issuing, so every slot has at most one use
+// outstanding: the last min(STAGES, issued) stages issued.  Lane 0 waits, each
+// wait bounded, for their full barriers (on the normal path these have
+// completed or are about to).
+template <int STAGES>
+__device__ __forceinline__ void drain_issued_stages(const uint64_t* full_bar, int issued, int lane,
+                                                    int32_t* err) {
+  if (lane == 0) {
+    for (int k = issued > STAGES ? issued - STAGES : 0; k < issued; ++k)
+      if (!mbar_wait_bounded(smem_addr(&full_bar[k % STAGES]), (uint32_t)((k / STAGES) & 1))) {
+        record_error(err, TVP_DEVERR_TIMEOUT);
+        break;
+      }
+  }
+  __syncwarp();
+}
+
 // Online-softmax state of one (KV head, piece) in accumulator layout.
 struct HeadState {
   float m0, m1, l0, l1;
@@ -234,33 +253,50 @@ __device__ __forceinline__ int partial_slot(int r, int first, long long T, long 
 
 // Merges the partial pieces of sequence [first, end) for KV head group g from
 // the slots of ranges r0..r1 (lane -> query head lane/8 of the group, channels
-// (lane%8)*8 .. +7) and writes the normalised output at out_group.
+// (lane%8)*8 .. +7) and writes the normalised output at out_group.  One pass
+// with an online rescale; the loads of kBatch pieces are issued before any is
+// used, so a fan-in of n pieces costs about n / kBatch L2 round trips.
+template <int kBatch>
 __device__ __forceinline__ void combine_partials(const float* partials, int groups, int g,
                                                  int first, int end, long long T, long long R,
                                                  __nv_bfloat16* out_group, int lane) {
   const int r0 = range_of_page(first, T, R), r1 = range_of_page(end - 1, T, R);
   const int h = lane >> 3, d0 = (lane & 7) * 8;
-  float M = -INFINITY;
-  for (int r = r0; r <= r1; ++r) {
-    const int slot = (r == r0) ? partial_slot(r, first, T, R) : r * 2;
-    const float* part = partials + ((size_t)slot * groups + g) * kPartialFloats;
-    M = fmaxf(M, __ldcg(part + h));
-  }
+  float M = -INFINITY, lsum = 0.f;
   float o[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) o[i] = 0.f;
-  float lsum = 0.f;
-  for (int r = r0; r <= r1; ++r) {
-    const int slot = (r == r0) ? partial_slot(r, first, T, R) : r * 2;
-    const float* part = partials + ((size_t)slot * groups + g) * kPartialFloats;
-    const float m = __ldcg(part + h);
-    const float w = (m == -INFINITY) ? 0.f : exp2f(m - M);
-    lsum += w * __ldcg(part + kGroup + h);
-    const float4 a = __ldcg(reinterpret_cast<const float4*>(part + 2 * kGroup + h * kHeadDim + d0));
-    const float4 b =
-        __ldcg(reinterpret_cast<const float4*>(part + 2 * kGroup + h * kHeadDim + d0 + 4));
-    o[0] += w * a.x; o[1] += w * a.y; o[2] += w * a.z; o[3] += w * a.w;
-    o[4] += w * b.x; o[5] += w * b.y; o[6] += w * b.z; o[7] += w * b.w;
+  for (int rb = r0; rb <= r1; rb += kBatch) {
+    float m[kBatch], l[kBatch];
+    float4 a[kBatch], b[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int r = rb + k;
+      m[k] = -INFINITY;
+      if (r <= r1) {
+        const int slot = (r == r0) ? partial_slot(r, first, T, R) : r * 2;
+        const float* part = partials + ((size_t)slot * groups + g) * kPartialFloats;
+        m[k] = __ldcg(part + h);
+        l[k] = __ldcg(part + kGroup + h);
+        a[k] = __ldcg(reinterpret_cast<const float4*>(part + 2 * kGroup + h * kHeadDim + d0));
+        b[k] = __ldcg(reinterpret_cast<const float4*>(part + 2 * kGroup + h * kHeadDim + d0 + 4));
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      if (m[k] == -INFINITY) continue;  // past r1, or a piece that attended nothing
+      if (m[k] > M) {
+        const float sc = (M == -INFINITY) ? 0.f : exp2f(M - m[k]);
+        lsum *= sc;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] *= sc;
+        M = m[k];
+      }
+      const float w = exp2f(m[k] - M);
+      lsum += w * l[k];
+      o[0] += w * a[k].x; o[1] += w * a[k].y; o[2] += w * a[k].z; o[3] += w * a[k].w;
+      o[4] += w * b[k].x; o[5] += w * b[k].y; o[6] += w * b[k].z; o[7] += w * b[k].w;
+    }
   }
   const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
   uint4 packed;
@@ -270,6 +306,11 @@ __device__ __forceinline__ void combine_partials(const float* partials, int grou
   packed.w = pack_bf16x2(o[6] * inv, o[7] * inv);
   *reinterpret_cast<uint4*>(out_group + h * kHeadDim + d0) = packed;
 }
+
+// Pieces whose partials the combine loads at once.  Inside the decode kernels
+// (96 registers a consumer thread) a batch of 2 already spills; a batch of 1
+// still costs one L2 round trip per piece, where a two-pass merge costs two.
+constexpr int kCombineBatch = 1;
 
 // Publishes a partial piece and, when it is the last of its sequence to arrive,
 // merges all of them (a counter per (sequence, KV head group); no waiting).
@@ -292,7 +333,7 @@ __device__ __forceinline__ void finish_partial(const HeadState& st, float* parti
     }
   }
   last = __shfl_sync(0xffffffffu, last, 0);
-  if (last) combine_partials(partials, groups, g, first, end, T, R, out_group, lane);
+  if (last) combine_partials<kCombineBatch>(partials, groups, g, first, end, T, R, out_group, lane);
 }
 
 }  // namespace tvp
