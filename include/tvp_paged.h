@@ -106,14 +106,18 @@ int tvp_rope_append(tvp_bf16* k_pool, tvp_bf16* v_pool, int num_pages, int num_l
 
 /*
  * Workspace of the decode path: plan header, per-sequence page prefix sums,
- * last-arriver counters and split-K partials for `num_ctas` CTAs (0 = one per SM).
+ * each CTA's first sequence, last-arriver counters and split-K partials for
+ * `num_ctas` CTAs (0 = one per SM).  kv_heads is the number of KV heads the
+ * pools hold: the model's 8, or 4, 2 or 1 for a GPU that holds a shard of the
+ * heads (every page, only its heads' channels).  0 for any other value.
  */
 size_t tvp_decode_workspace_bytes(int batch, int kv_heads, int num_ctas);
 
 /*
  * Per-step plan (the device side of preparePagedBatch,
- * src/model/paged_attention.cu:30-87): page prefix sums over d_seq_lens and a
- * reset of the split-K counters.  One plan serves every layer of a decode step.
+ * src/model/paged_attention.cu:30-87): page prefix sums over d_seq_lens, the
+ * sequence holding each CTA's first page, and a reset of the split-K
+ * counters.  One plan serves every layer of a decode step.
  * d_seq_lens[b] = attended length L (= current_seq_len + 1 after the append).
  */
 int tvp_decode_plan(const int32_t* d_seq_lens, int batch, int table_stride, int kv_heads,
@@ -127,12 +131,14 @@ int tvp_decode_plan(const int32_t* d_seq_lens, int batch, int table_stride, int 
  *   computePagedAttentionScores (gather + 32*B cuBLAS GEMVs)  src/model/paged_attention.cu:133-146
  *   softmaxRows per (row, head)                               src/model/softmax.cu:47-72
  *   pagedAttentionScoresTimesV (gather + 32*B cuBLAS GEMVs)   src/model/paged_attention.cu:148-161
+ * kv_heads: 8 (the model), or 4, 2, 1 for a KV-head shard; q_heads = 4 * kv_heads.
  * q:   [batch][q_heads * 64] BF16, already RoPE'd.
  * out: [batch][q_heads * 64] BF16, head-major (head h at h*64), as the reference.
  * out[b, h] = softmax(scale * q[b,h] . K[b, kv(h)]^T) . V[b, kv(h)] over the
  * first d_seq_lens[b] tokens of row b's pages, kv(h) = h / 4.
  * Pages are read in place.  The workspace must hold a plan made by
- * tvp_decode_plan with the same d_seq_lens contents, batch and num_ctas.
+ * tvp_decode_plan with the same d_seq_lens contents, batch, kv_heads and
+ * num_ctas.
  */
 int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const tvp_bf16* v_pool,
                                int num_pages, int num_layers, int layer, int kv_heads, int q_heads,

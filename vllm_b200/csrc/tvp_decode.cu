@@ -363,7 +363,8 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
       if (complete)
         write_output(st, out_group, tl);
       else
-        finish_partial(st, p.partials, p.counters, kMaxKvHeads, g, s,
+        // combine batch 2: the largest that fits this consumer's registers
+        finish_partial<2>(st, p.partials, p.counters, kMaxKvHeads, g, s,
                        partial_slot((int)c, first, T, C), first, end, T, C, out_group, tl, lane);
     }
     kbase += n;

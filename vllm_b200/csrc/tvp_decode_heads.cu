@@ -90,16 +90,6 @@ __device__ __forceinline__ void merge_ways(HeadState& st, float* scratch, int wa
   }
 }
 
-// The split-K finish, out of line: inlined, its combine loop pushed the
-// KVH = 1 consumer past its register budget.  It runs once per partial piece.
-__device__ __noinline__ void finish_partial_cold(const HeadState& st, float* partials, int* counters,
-                                               int groups, int g, int s, int slot, int first,
-                                               int end, long long T, long long R,
-                                               __nv_bfloat16* out_group, int lane) {
-  finish_partial(st, partials, counters, groups, g, s, slot, first, end, T, R, out_group,
-                 TileLane(lane), lane);
-}
-
 template <int KVH, bool REGSPLIT>
 __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
     paged_decode_heads_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap k_map,
@@ -303,8 +293,10 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
       if (complete)
         write_output(st, out_group, tl);
       else
-        finish_partial_cold(st, p.partials, p.counters, KVH, h, s,
-                            partial_slot((int)c, first, T, C), first, end, T, C, out_group, lane);
+        // combine batch: 2 fits the KVH = 1 consumer's registers, 1 the others'
+        finish_partial<KVH == 1 ? 2 : 1>(st, p.partials, p.counters, KVH, h, s,
+                                         partial_slot((int)c, first, T, C), first, end, T, C,
+                                         out_group, tl, lane);
     }
     kbase += np;
     pg = piece_end;

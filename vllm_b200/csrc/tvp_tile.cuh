@@ -253,51 +253,96 @@ __device__ __forceinline__ int partial_slot(int r, int first, long long T, long 
 
 // Merges the partial pieces of sequence [first, end) for KV head group g from
 // the slots of ranges r0..r1 (lane -> query head lane/8 of the group, channels
-// (lane%8)*8 .. +7) and writes the normalised output at out_group.  One pass
-// with an online rescale; the loads of kBatch pieces are issued before any is
-// used, so a fan-in of n pieces costs about n / kBatch L2 round trips.
-template <int kBatch>
+// (lane%8)*8 .. +7) and writes the normalised output at out_group.
+// Phase A: lane j reads m[4], l[4] of pieces j, j + 32, ... (all in flight at
+// once); the warp reduces the maxima and the normalisers.  Phase B: each lane
+// sums its 8 channels over the pieces, loading piece j + 1 before folding j;
+// piece j's weight comes from lane j % 32 by shuffle.  About 1 + n L2 round
+// trips at most, n / 2 when loads overlap.
+__device__ __forceinline__ const float* partial_of(const float* partials, int groups, int g, int r,
+                                                   int r0, int first, long long T, long long R) {
+  const int slot = (r == r0) ? partial_slot(r, first, T, R) : r * 2;
+  return partials + ((size_t)slot * groups + g) * kPartialFloats;
+}
+
+__device__ __forceinline__ float pick(const float4& v, int h) {
+  return h == 0 ? v.x : h == 1 ? v.y : h == 2 ? v.z : v.w;
+}
+
+// BATCH: pieces whose output partials one lane loads at once in Phase B; each
+// kernel takes the largest that fits its register budget without spilling.
+template <int BATCH>
 __device__ __forceinline__ void combine_partials(const float* partials, int groups, int g,
                                                  int first, int end, long long T, long long R,
                                                  __nv_bfloat16* out_group, int lane) {
   const int r0 = range_of_page(first, T, R), r1 = range_of_page(end - 1, T, R);
+  const int n = r1 - r0 + 1;
   const int h = lane >> 3, d0 = (lane & 7) * 8;
-  float M = -INFINITY, lsum = 0.f;
+  // Phase A: per-head maximum over all pieces.
+  float4 M = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+  for (int j = lane; j < n; j += 32) {
+    const float4 m = __ldcg(reinterpret_cast<const float4*>(
+        partial_of(partials, groups, g, r0 + j, r0, first, T, R)));
+    M.x = fmaxf(M.x, m.x); M.y = fmaxf(M.y, m.y); M.z = fmaxf(M.z, m.z); M.w = fmaxf(M.w, m.w);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    M.x = fmaxf(M.x, __shfl_xor_sync(0xffffffffu, M.x, o));
+    M.y = fmaxf(M.y, __shfl_xor_sync(0xffffffffu, M.y, o));
+    M.z = fmaxf(M.z, __shfl_xor_sync(0xffffffffu, M.z, o));
+    M.w = fmaxf(M.w, __shfl_xor_sync(0xffffffffu, M.w, o));
+  }
+  float4 ls = make_float4(0.f, 0.f, 0.f, 0.f);  // this lane's share of the normalisers
   float o[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) o[i] = 0.f;
-  for (int rb = r0; rb <= r1; rb += kBatch) {
-    float m[kBatch], l[kBatch];
-    float4 a[kBatch], b[kBatch];
-#pragma unroll
-    for (int k = 0; k < kBatch; ++k) {
-      const int r = rb + k;
-      m[k] = -INFINITY;
-      if (r <= r1) {
-        const int slot = (r == r0) ? partial_slot(r, first, T, R) : r * 2;
-        const float* part = partials + ((size_t)slot * groups + g) * kPartialFloats;
-        m[k] = __ldcg(part + h);
-        l[k] = __ldcg(part + kGroup + h);
-        a[k] = __ldcg(reinterpret_cast<const float4*>(part + 2 * kGroup + h * kHeadDim + d0));
-        b[k] = __ldcg(reinterpret_cast<const float4*>(part + 2 * kGroup + h * kHeadDim + d0 + 4));
-      }
+  for (int base = 0; base < n; base += 32) {
+    // Lane j: weights of piece base + j for the 4 heads (0 past the last piece).
+    float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (base + lane < n) {
+      const float* part = partial_of(partials, groups, g, r0 + base + lane, r0, first, T, R);
+      const float4 m = __ldcg(reinterpret_cast<const float4*>(part));
+      const float4 l = __ldcg(reinterpret_cast<const float4*>(part + kGroup));
+      w.x = m.x == -INFINITY ? 0.f : exp2f(m.x - M.x);
+      w.y = m.y == -INFINITY ? 0.f : exp2f(m.y - M.y);
+      w.z = m.z == -INFINITY ? 0.f : exp2f(m.z - M.z);
+      w.w = m.w == -INFINITY ? 0.f : exp2f(m.w - M.w);
+      ls.x += w.x * l.x; ls.y += w.y * l.y; ls.z += w.z * l.z; ls.w += w.w * l.w;
     }
+    // Phase B: this lane's 8 channels over the chunk, BATCH pieces' loads in
+    // flight at once; piece j's weight comes from lane j by shuffle.
+    const int cnt = min(32, n - base);
+    for (int j0 = 0; j0 < cnt; j0 += BATCH) {
+      float4 a[BATCH], b[BATCH];
 #pragma unroll
-    for (int k = 0; k < kBatch; ++k) {
-      if (m[k] == -INFINITY) continue;  // past r1, or a piece that attended nothing
-      if (m[k] > M) {
-        const float sc = (M == -INFINITY) ? 0.f : exp2f(M - m[k]);
-        lsum *= sc;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] *= sc;
-        M = m[k];
+      for (int k = 0; k < BATCH; ++k) {
+        a[k] = b[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j0 + k < cnt) {
+          const float* src = partial_of(partials, groups, g, r0 + base + j0 + k, r0, first, T, R) +
+                             2 * kGroup + h * kHeadDim + d0;
+          a[k] = __ldcg(reinterpret_cast<const float4*>(src));
+          b[k] = __ldcg(reinterpret_cast<const float4*>(src + 4));
+        }
       }
-      const float w = exp2f(m[k] - M);
-      lsum += w * l[k];
-      o[0] += w * a[k].x; o[1] += w * a[k].y; o[2] += w * a[k].z; o[3] += w * a[k].w;
-      o[4] += w * b[k].x; o[5] += w * b[k].y; o[6] += w * b[k].z; o[7] += w * b[k].w;
+#pragma unroll
+      for (int k = 0; k < BATCH; ++k) {
+        const int j = min(j0 + k, 31);
+        const float4 wj = make_float4(__shfl_sync(0xffffffffu, w.x, j), __shfl_sync(0xffffffffu, w.y, j),
+                                      __shfl_sync(0xffffffffu, w.z, j), __shfl_sync(0xffffffffu, w.w, j));
+        const float wh = j0 + k < cnt ? pick(wj, h) : 0.f;
+        o[0] += wh * a[k].x; o[1] += wh * a[k].y; o[2] += wh * a[k].z; o[3] += wh * a[k].w;
+        o[4] += wh * b[k].x; o[5] += wh * b[k].y; o[6] += wh * b[k].z; o[7] += wh * b[k].w;
+      }
     }
   }
+#pragma unroll
+  for (int k = 16; k > 0; k >>= 1) {
+    ls.x += __shfl_xor_sync(0xffffffffu, ls.x, k);
+    ls.y += __shfl_xor_sync(0xffffffffu, ls.y, k);
+    ls.z += __shfl_xor_sync(0xffffffffu, ls.z, k);
+    ls.w += __shfl_xor_sync(0xffffffffu, ls.w, k);
+  }
+  const float lsum = pick(ls, h);
   const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
   uint4 packed;
   packed.x = pack_bf16x2(o[0] * inv, o[1] * inv);
@@ -307,13 +352,9 @@ __device__ __forceinline__ void combine_partials(const float* partials, int grou
   *reinterpret_cast<uint4*>(out_group + h * kHeadDim + d0) = packed;
 }
 
-// Pieces whose partials the combine loads at once.  Inside the decode kernels
-// (96 registers a consumer thread) a batch of 2 already spills; a batch of 1
-// still costs one L2 round trip per piece, where a two-pass merge costs two.
-constexpr int kCombineBatch = 1;
-
 // Publishes a partial piece and, when it is the last of its sequence to arrive,
 // merges all of them (a counter per (sequence, KV head group); no waiting).
+template <int BATCH>
 __device__ __forceinline__ void finish_partial(const HeadState& st, float* partials, int* counters,
                                                int groups, int g, int s, int slot, int first,
                                                int end, long long T, long long R,
@@ -333,7 +374,7 @@ __device__ __forceinline__ void finish_partial(const HeadState& st, float* parti
     }
   }
   last = __shfl_sync(0xffffffffu, last, 0);
-  if (last) combine_partials<kCombineBatch>(partials, groups, g, first, end, T, R, out_group, lane);
+  if (last) combine_partials<BATCH>(partials, groups, g, first, end, T, R, out_group, lane);
 }
 
 }  // namespace tvp
