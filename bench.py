@@ -514,9 +514,11 @@ def bench_long_context_heads(dev, iters=20):
 
 def bench_head_sharded(dev, rank, world, local_rank, iters=20):
     """KV-head-sharded long_context over `world` GPUs: rank r holds 8 / world
-    KV heads of every page, runs the head-shard kernel and all-gathers the
-    attention slices over NCCL into [16, 2048].  Per-layer time is the max over
-    ranks of CUDA-event time on the launching stream."""
+    KV heads of every page and every rank ends with the [16, 2048] rows.  Two
+    forms: the all-gather fused into the decode kernel (p2p: stores into every
+    rank's rows over NVLink, then a bounded wait), and the decode followed by
+    an NCCL all-gather.  Per-layer time is the max over ranks of CUDA-event
+    time on the launching stream; layers alternate the gather buffers."""
     import torch
     import torch.distributed as dist
     from vllm_b200 import sharding
@@ -524,20 +526,20 @@ def bench_head_sharded(dev, rank, world, local_rank, iters=20):
     case, kp, vp, q = long_context_pools(dev, kv_heads, seed=99 + rank)
     tables = torch.from_numpy(case.tables).to(dev)
     lens = torch.from_numpy(case.lens).to(dev)
-    dec = sharding.HeadShardedDecode(16, device=dev)
-    dec.plan(lens, case.tables.shape[1])
-    for _ in range(3):
-        dec.attend(q, kp, vp, 0, tables, lens)
     stream = torch.cuda.current_stream(dev)
+    res = {"workload": f"long_context 16 x 32768, 1 layer, {kv_heads} KV head(s) per GPU",
+           "all_gather_bytes_per_rank": 16 * kv_heads * W.GROUP * W.HEAD_DIM * 2}
 
-    def timed(gather):
+    def timed(fn):
+        for _ in range(3):
+            fn()
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(iters)]
         dist.barrier(device_ids=[local_rank])
         torch.cuda.synchronize(dev)
         for a, b in ev:
             a.record(stream)
-            dec.attend(q, kp, vp, 0, tables, lens, gather=gather)
+            fn()
             b.record(stream)
         torch.cuda.synchronize(dev)
         ms = statistics.median(a.elapsed_time(b) for a, b in ev)
@@ -545,16 +547,22 @@ def bench_head_sharded(dev, rank, world, local_rank, iters=20):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    ms_decode = timed(False)
-    ms_total = timed(True)
+    nb = algorithmic_bytes(case.lens)
+    for mode in ("p2p", "nccl"):
+        dec = sharding.HeadShardedDecode(16, device=dev, mode=mode)
+        dec.plan(lens, case.tables.shape[1])
+        ms = timed(lambda: dec.attend(q, kp, vp, 0, tables, lens))
+        if mode == "nccl":
+            res["us_decode_only"] = round(timed(lambda: dec.attend(q, kp, vp, 0, tables, lens,
+                                                                   gather=False)) * 1e3, 2)
+        res[mode] = {"us_per_layer": round(ms * 1e3, 2),
+                     "aggregate_kv_GBps": round(nb["kv"] / (ms / 1e3) / 1e9, 1)}
+        dec.close()
+    res["p2p"]["collective"] = "fused into the decode kernel: peer stores over NVLink + flag wait"
+    res["nccl"]["collective"] = "NCCL all_gather_into_tensor + interleave"
     del kp, vp
     torch.cuda.empty_cache()
-    nb = algorithmic_bytes(case.lens)
-    return {"workload": f"long_context 16 x 32768, 1 layer, {kv_heads} KV head(s) per GPU",
-            "us_per_layer": round(ms_total * 1e3, 2), "us_decode_only": round(ms_decode * 1e3, 2),
-            "aggregate_kv_GBps": round(nb["kv"] / (ms_total / 1e3) / 1e9, 1),
-            "all_gather_bytes_per_rank": 16 * kv_heads * W.GROUP * W.HEAD_DIM * 2,
-            "collective": "NCCL all_gather_into_tensor"}
+    return res
 
 
 def bench_decode_small(dev, iters=50):

@@ -177,6 +177,60 @@ int tvp_paged_decode_attention_noalloc(const tvp_bf16* q, const tvp_bf16* k_pool
                                        tvp_stream_t stream);
 
 /* ======================================================================= *
+ * KV-head-sharded decode with the all-gather fused into the decode kernel.
+ * No counterpart in the reference (its engine runs on one GPU); this is the
+ * multi-GPU form of src/model/paged_transformer.cu:85-94 for long contexts:
+ * GPU r of `world` (2, 4 or 8; one process per GPU) holds KV heads
+ * [r K, (r + 1) K), K = 8 / world, of every page (pools of K x 64 channels,
+ * the same block tables on every rank) and the [batch][2048] attention rows
+ * end up on every rank.  The decode kernel stores each finished output group
+ * straight into every rank's gathered rows over NVLink (peer memory opened
+ * through CUDA IPC) and its last CTA bumps every rank's flag; a wait launch
+ * orders the stream after all ranks' stores.  Every rank makes the same calls
+ * in the same order (SPMD).
+ * ======================================================================= */
+#define TVP_IPC_HANDLE_BYTES 64
+typedef struct tvp_head_gather tvp_head_gather;
+
+/* This rank's gathered rows (two buffers of [max_batch][2048] BF16) and flag
+ * words, zero-initialised, on the current device. */
+int tvp_head_gather_create(int world, int rank, int kv_heads, int max_batch,
+                           tvp_head_gather** out);
+/* The IPC handle of this rank's allocation (TVP_IPC_HANDLE_BYTES bytes), to be
+ * sent to every other rank (e.g. by an all-gather over the process group). */
+int tvp_head_gather_export(const tvp_head_gather* g, void* handle_out);
+/* Opens every other rank's allocation; handles = world x TVP_IPC_HANDLE_BYTES
+ * in rank order (this rank's own entry is ignored).  Once per group. */
+int tvp_head_gather_connect(tvp_head_gather* g, const void* handles);
+/* Device address of this rank's gathered rows of buffer 0 or 1. */
+int tvp_head_gather_rows(const tvp_head_gather* g, int buffer, tvp_bf16** rows_out);
+/* FAST decode attention of this rank's heads (arguments as for
+ * tvp_paged_decode_attention, kv_heads = 8 / world, no `out`), written into
+ * every rank's gathered rows of `buffer`.  Alternate the buffers from one
+ * layer to the next: a rank may start the next layer while another rank still
+ * reads this one's rows. */
+int tvp_paged_decode_attention_gather(const tvp_bf16* q, const tvp_bf16* k_pool,
+                                      const tvp_bf16* v_pool, int num_pages, int num_layers,
+                                      int layer, int kv_heads, int q_heads,
+                                      const int32_t* d_block_tables, int table_stride,
+                                      const int32_t* d_seq_lens, int batch, float scale,
+                                      int num_ctas, void* d_workspace, size_t workspace_bytes,
+                                      tvp_head_gather* g, int buffer, int32_t* d_error,
+                                      tvp_stream_t stream);
+/* Orders `stream` after every rank's stores of the last gather into
+ * `buffer`: a one-thread kernel polls this rank's flag, bounded by 2 s, after
+ * which it sets TVP_DEVERR_TIMEOUT in *d_error and returns (a rank that
+ * stopped never hangs the others; the group is then unusable). */
+int tvp_head_gather_wait(const tvp_head_gather* g, int buffer, int32_t* d_error,
+                         tvp_stream_t stream);
+/* Teardown, in two steps on every rank: disconnect (waits for this device,
+ * then closes the peers' allocations), a barrier across ranks, destroy (frees
+ * this rank's allocation, which no peer maps any more).  Destroy alone also
+ * disconnects, for a rank whose peers never connected. */
+int tvp_head_gather_disconnect(tvp_head_gather* g);
+int tvp_head_gather_destroy(tvp_head_gather* g);
+
+/* ======================================================================= *
  * Host API mirror: PagedKVCache / SequenceKVState / PagedBatchMetadata.
  * Same allocator semantics as src/model/paged_kvcache.cu:65-145 (LIFO free
  * list seeded descending, lazy ceil(L/16) pages, exhaustion checked before

@@ -118,3 +118,18 @@ def test_cxx_header_compiles_against_c_header(tmp_path):
     src.write_text("#include \"tvp_paged.h\"\nint main(void){return tvp_version() == 0;}\n")
     subprocess.run([gcc, "-std=c99", "-Wall", "-Werror", "-I", str(N.HEADER_PATH.parent), "-c",
                     str(src), "-o", str(tmp_path / "t.o")], check=True)
+
+
+def test_head_gather_rejects_bad_arguments_on_host(native):
+    h = ctypes.c_void_p()
+    assert native.tvp_head_gather_create(3, 0, 2, 16, ctypes.byref(h)) == N.TVP_ERR_UNSUPPORTED
+    assert native.tvp_head_gather_create(2, 0, 2, 16, ctypes.byref(h)) == N.TVP_ERR_UNSUPPORTED
+    assert native.tvp_head_gather_create(2, 2, 4, 16, ctypes.byref(h)) == N.TVP_ERR_INVALID_ARGUMENT
+    assert native.tvp_head_gather_create(2, 0, 4, 0, ctypes.byref(h)) == N.TVP_ERR_INVALID_ARGUMENT
+    assert native.tvp_head_gather_create(2, 0, 4, 16, None) == N.TVP_ERR_INVALID_ARGUMENT
+    assert native.tvp_head_gather_wait(None, 0, None, None) == N.TVP_ERR_INVALID_ARGUMENT
+    assert native.tvp_head_gather_destroy(None) == N.TVP_ERR_INVALID_ARGUMENT
+    fake = ctypes.c_void_p(0x10000)
+    assert native.tvp_paged_decode_attention_gather(
+        fake, fake, fake, 8, 1, 0, 4, 16, fake, 4, fake, 2, 0.125, 148, fake, 1 << 20, None, 0,
+        None, None) == N.TVP_ERR_INVALID_ARGUMENT

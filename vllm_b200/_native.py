@@ -36,6 +36,8 @@ TVP_APPEND_ROPE_K = 1
 TVP_APPEND_ROPE_Q = 2
 TVP_APPEND_WRITEBACK_K = 4
 
+TVP_IPC_HANDLE_BYTES = 64
+
 HEAD_DIM = 64
 PAGE_TOKENS = 16
 GQA_GROUP = 4
@@ -64,6 +66,17 @@ _SIGNATURES = {
                                                    c_int, c_int, c_int, c_void_p, c_int, c_void_p,
                                                    c_int, c_float, c_int, c_void_p, c_void_p,
                                                    c_void_p]),
+    "tvp_head_gather_create": (c_int, [c_int, c_int, c_int, c_int, POINTER(c_void_p)]),
+    "tvp_head_gather_export": (c_int, [c_void_p, c_void_p]),
+    "tvp_head_gather_connect": (c_int, [c_void_p, c_void_p]),
+    "tvp_head_gather_rows": (c_int, [c_void_p, c_int, POINTER(c_void_p)]),
+    "tvp_paged_decode_attention_gather": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                                  c_int, c_int, c_void_p, c_int, c_void_p, c_int,
+                                                  ctypes.c_float, c_int, c_void_p, c_size_t,
+                                                  c_void_p, c_int, c_void_p, c_void_p]),
+    "tvp_head_gather_wait": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
+    "tvp_head_gather_disconnect": (c_int, [c_void_p]),
+    "tvp_head_gather_destroy": (c_int, [c_void_p]),
     "tvp_cache_create": (c_int, [c_int, c_int, c_int, c_int, c_int, POINTER(c_void_p)]),
     "tvp_cache_destroy": (None, [c_void_p]),
     "tvp_cache_pools": (c_int, [c_void_p, POINTER(c_void_p), POINTER(c_void_p), POINTER(c_int)]),

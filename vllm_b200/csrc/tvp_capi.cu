@@ -64,6 +64,49 @@ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_
 inline int map_cuda(cudaError_t e) { return e == cudaSuccess ? TVP_OK : TVP_ERR_RUNTIME; }
 
 }  // namespace
+
+int prepare_decode(const void* q, const void* k_pool, const void* v_pool, int num_pages,
+                   int num_layers, int layer, int kv_heads, int q_heads,
+                   const int32_t* d_block_tables, int table_stride, const int32_t* d_seq_lens,
+                   int batch, float scale, int num_ctas, void* d_workspace,
+                   size_t workspace_bytes, int32_t* d_error, DecodeParams* p, long long* pool_rows,
+                   int* ctas) {
+  if (!q || !k_pool || !v_pool || !d_block_tables || !d_seq_lens || num_pages <= 0 ||
+      num_layers <= 0 || layer < 0 || layer >= num_layers || table_stride <= 0 || batch <= 0 ||
+      num_ctas < 0 || !std::isfinite(scale))
+    return TVP_ERR_INVALID_ARGUMENT;
+  if (!decode_heads_supported(kv_heads) || q_heads != kv_heads * kGroup) return TVP_ERR_UNSUPPORTED;
+  if ((long long)num_layers * num_pages * kPage > 0x7fffffffLL) return TVP_ERR_UNSUPPORTED;
+  if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(q, 4))
+    return TVP_ERR_INVALID_ARGUMENT;
+  const int rc = resolve_ctas(num_ctas, ctas);
+  if (rc != TVP_OK) return rc;
+  const WorkspaceLayout w = workspace_layout(batch, kv_heads, *ctas);
+  if (!d_workspace || workspace_bytes < w.total || !aligned(d_workspace, 256)) return TVP_ERR_WORKSPACE;
+  char* base = static_cast<char*>(d_workspace);
+  *p = DecodeParams{};
+  p->q = reinterpret_cast<const __nv_bfloat16*>(q);
+  p->k_pool = reinterpret_cast<const __nv_bfloat16*>(k_pool);
+  p->v_pool = reinterpret_cast<const __nv_bfloat16*>(v_pool);
+  p->tables = d_block_tables;
+  p->seq_lens = d_seq_lens;
+  p->header = reinterpret_cast<const int32_t*>(base + w.header);
+  p->cu = reinterpret_cast<const int32_t*>(base + w.cu);
+  p->cta_seq = reinterpret_cast<const int32_t*>(base + w.cta_seq);
+  p->counters = reinterpret_cast<int32_t*>(base + w.counters);
+  p->partials = reinterpret_cast<float*>(base + w.partials);
+  p->layer_row_base = (long long)layer * num_pages * kPage;
+  p->num_pages = num_pages;
+  p->table_stride = table_stride;
+  p->batch = batch;
+  p->kv_heads = kv_heads;
+  p->scale_log2 = scale * 1.4426950408889634f;
+  p->err = d_error;
+  p->world = 1;
+  *pool_rows = (long long)num_layers * num_pages * kPage;
+  return TVP_OK;
+}
+
 }  // namespace tvp
 
 using namespace tvp;
@@ -168,7 +211,6 @@ int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const 
   if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(q, 4) || !aligned(out, 16))
     return TVP_ERR_INVALID_ARGUMENT;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const long long layer_row_base = (long long)layer * num_pages * kPage;
   if (mode == TVP_MODE_COMPAT) {
     CompatParams p;
     p.q = reinterpret_cast<const __nv_bfloat16*>(q);
@@ -177,7 +219,7 @@ int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const 
     p.out = reinterpret_cast<__nv_bfloat16*>(out);
     p.tables = d_block_tables;
     p.seq_lens = d_seq_lens;
-    p.layer_row_base = layer_row_base;
+    p.layer_row_base = (long long)layer * num_pages * kPage;
     p.num_pages = num_pages;
     p.table_stride = table_stride;
     p.kv_heads = kv_heads;
@@ -185,32 +227,15 @@ int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const 
     p.err = d_error;
     return map_cuda(launch_compat_decode(p, batch, st));
   }
-  int ctas = 0;
-  int rc = resolve_ctas(num_ctas, &ctas);
-  if (rc != TVP_OK) return rc;
-  const WorkspaceLayout w = workspace_layout(batch, kv_heads, ctas);
-  if (!d_workspace || workspace_bytes < w.total || !aligned(d_workspace, 256)) return TVP_ERR_WORKSPACE;
-  char* base = static_cast<char*>(d_workspace);
   DecodeParams p;
-  p.q = reinterpret_cast<const __nv_bfloat16*>(q);
-  p.k_pool = reinterpret_cast<const __nv_bfloat16*>(k_pool);
-  p.v_pool = reinterpret_cast<const __nv_bfloat16*>(v_pool);
+  long long pool_rows = 0;
+  int ctas = 0;
+  const int rc = prepare_decode(q, k_pool, v_pool, num_pages, num_layers, layer, kv_heads, q_heads,
+                                d_block_tables, table_stride, d_seq_lens, batch, scale, num_ctas,
+                                d_workspace, workspace_bytes, d_error, &p, &pool_rows, &ctas);
+  if (rc != TVP_OK) return rc;
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
-  p.tables = d_block_tables;
-  p.seq_lens = d_seq_lens;
-  p.header = reinterpret_cast<const int32_t*>(base + w.header);
-  p.cu = reinterpret_cast<const int32_t*>(base + w.cu);
-  p.cta_seq = reinterpret_cast<const int32_t*>(base + w.cta_seq);
-  p.counters = reinterpret_cast<int32_t*>(base + w.counters);
-  p.partials = reinterpret_cast<float*>(base + w.partials);
-  p.layer_row_base = layer_row_base;
-  p.num_pages = num_pages;
-  p.table_stride = table_stride;
-  p.batch = batch;
-  p.kv_heads = kv_heads;
-  p.scale_log2 = scale * 1.4426950408889634f;
-  p.err = d_error;
-  return map_cuda(launch_paged_decode(p, (long long)num_layers * num_pages * kPage, ctas, st));
+  return map_cuda(launch_paged_decode(p, pool_rows, ctas, st));
 }
 
 }  // extern "C"

@@ -359,7 +359,7 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
 
     if (set == 0) {
       reduce_l(st);
-      __nv_bfloat16* out_group = p.out + (size_t)s * kOutRow + g * kGroup * kHeadDim;
+      const OutGroup out_group = local_out(p.out + (size_t)s * kOutRow + g * kGroup * kHeadDim);
       if (complete)
         write_output(st, out_group, tl);
       else

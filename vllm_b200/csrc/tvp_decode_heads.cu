@@ -27,6 +27,7 @@
 namespace tvp {
 
 constexpr int kHeadsStages = 6;
+constexpr int kDoneBarrier = 15;  // named barrier of the 16 consumer warps at a gather's end
 constexpr int kStateFloats = 20;  // m0, m1, l0, l1, acc[16] per lane
 constexpr int kMergeSlots = 8;    // senders of the widest merge level (W / 2 x KVH)
 
@@ -90,7 +91,13 @@ __device__ __forceinline__ void merge_ways(HeadState& st, float* scratch, int wa
   }
 }
 
-template <int KVH, bool REGSPLIT>
+// GATHER: the KV-head-shard all-gather fused into the kernel.  Each output
+// group is stored straight into every rank's gathered rows [B][2048] at this
+// rank's heads (plain stores to peer memory over NVLink, issued as soon as the
+// group is final); every thread fences at system scope after its last store,
+// each CTA counts itself done, and the last CTA of the launch adds 1 to every
+// rank's flag.  A rank whose flag reached launches x world has all rows.
+template <int KVH, bool REGSPLIT, bool GATHER>
 __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
     paged_decode_heads_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap k_map,
                               const __grid_constant__ CUtensorMap v_map) {
@@ -221,13 +228,20 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
   const int way = set * PS + o;
   const TileLane tl(lane);
   const uint32_t k_off = t * kTileBytes, v_off = (kStageTiles + t) * kTileBytes;
-  constexpr int kOutRow = KVH * kGroup * kHeadDim;
+  constexpr int kOutRow = KVH * kGroup * kHeadDim;                  // this rank's rows
+  constexpr int kGatherRow = kMaxKvHeads * kGroup * kHeadDim;       // gathered rows (2048)
+  // Destination of sequence s's output for KV head h.
+  auto out_of = [&](int s) -> OutGroup {
+    if (GATHER)
+      return OutGroup{nullptr, p.peer_rows,
+                      (size_t)s * kGatherRow + (size_t)(p.rank * KVH + h) * kGroup * kHeadDim,
+                      p.world};
+    return local_out(p.out + (size_t)s * kOutRow + h * kGroup * kHeadDim);
+  };
 
   if (way == 0) {
     for (int s = blockIdx.x; s < p.batch; s += gridDim.x)
-      if (__ldg(p.cu + s) == __ldg(p.cu + s + 1))
-        *reinterpret_cast<uint4*>(p.out + (size_t)s * kOutRow + h * kGroup * kHeadDim + lane * 8) =
-            make_uint4(0, 0, 0, 0);
+      if (__ldg(p.cu + s) == __ldg(p.cu + s + 1)) out_of(s).store16(lane * 8, make_uint4(0, 0, 0, 0));
   }
 
   int s = s0;
@@ -289,7 +303,7 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
     merge_ways<KVH>(st, scratch, way, h, lane);
     if (way == 0) {
       reduce_l(st);
-      __nv_bfloat16* out_group = p.out + (size_t)s * kOutRow + h * kGroup * kHeadDim;
+      const OutGroup out_group = out_of(s);
       if (complete)
         write_output(st, out_group, tl);
       else
@@ -301,26 +315,45 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
     kbase += np;
     pg = piece_end;
   }
+
+  if (GATHER) {
+    // Every row this CTA stored is visible system-wide before the CTA counts
+    // itself done; the last CTA then signals every rank (its own included).
+    __threadfence_system();
+    named_barrier_sync(kDoneBarrier, 2 * kStageTiles * 32);
+    if (threadIdx.x == 0) {
+      __threadfence_system();  // release: the stores this thread saw through the barrier
+      const int done = atomicAdd(p.done_counter, 1);
+      if (done == (int)gridDim.x - 1) {
+        atomicExch(p.done_counter, 0);  // ready for the next launch
+        __threadfence_system();         // acquire the other CTAs' releases, release to the peers
+        for (int r = 0; r < p.world; ++r)
+          atomicAdd_system(reinterpret_cast<int*>(
+                               __ldg(reinterpret_cast<const unsigned long long*>(p.peer_flags) + r)),
+                           1);
+      }
+    }
+  }
 }
 
 namespace {
 
 enum class HeadsForm { kUnknown, kSplit, kPlain };
 
-template <int KVH>
+template <int KVH, bool GATHER>
 HeadsForm heads_form(int dev) {
   static HeadsForm forms[64] = {};
   if (dev >= 0 && dev < 64 && forms[dev] != HeadsForm::kUnknown) return forms[dev];
   HeadsForm form = HeadsForm::kPlain;
   cudaFuncAttributes fa;
-  if (cudaFuncGetAttributes(&fa, paged_decode_heads_kernel<KVH, true>) == cudaSuccess &&
+  if (cudaFuncGetAttributes(&fa, paged_decode_heads_kernel<KVH, true, GATHER>) == cudaSuccess &&
       regsplit_fits(fa.numRegs, decode_threads<2, true>()) &&
-      cudaFuncSetAttribute(paged_decode_heads_kernel<KVH, true>,
+      cudaFuncSetAttribute(paged_decode_heads_kernel<KVH, true, GATHER>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)heads_smem_bytes()) == cudaSuccess)
     form = HeadsForm::kSplit;
   if (form == HeadsForm::kPlain &&
-      cudaFuncSetAttribute(paged_decode_heads_kernel<KVH, false>,
+      cudaFuncSetAttribute(paged_decode_heads_kernel<KVH, false, GATHER>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)heads_smem_bytes()) != cudaSuccess)
     form = HeadsForm::kUnknown;
@@ -328,21 +361,49 @@ HeadsForm heads_form(int dev) {
   return form;
 }
 
-template <int KVH>
+template <int KVH, bool GATHER>
 cudaError_t launch_heads(const DecodeParams& p, const CUtensorMap& k_map, const CUtensorMap& v_map,
                          int num_ctas, cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  const HeadsForm form = heads_form<KVH>(dev);
+  const HeadsForm form = heads_form<KVH, GATHER>(dev);
   if (form == HeadsForm::kUnknown) return cudaErrorInvalidDeviceFunction;
   if (form == HeadsForm::kSplit)
-    paged_decode_heads_kernel<KVH, true>
+    paged_decode_heads_kernel<KVH, true, GATHER>
         <<<num_ctas, decode_threads<2, true>(), heads_smem_bytes(), stream>>>(p, k_map, v_map);
   else
-    paged_decode_heads_kernel<KVH, false>
+    paged_decode_heads_kernel<KVH, false, GATHER>
         <<<num_ctas, decode_threads<2, false>(), heads_smem_bytes(), stream>>>(p, k_map, v_map);
   return cudaGetLastError();
+}
+
+template <bool GATHER>
+cudaError_t launch_heads_any(const DecodeParams& p, const CUtensorMap& k_map,
+                             const CUtensorMap& v_map, int num_ctas, cudaStream_t stream) {
+  switch (p.kv_heads) {
+    case 1: return launch_heads<1, GATHER>(p, k_map, v_map, num_ctas, stream);
+    case 2: return launch_heads<2, GATHER>(p, k_map, v_map, num_ctas, stream);
+    case 4: return launch_heads<4, GATHER>(p, k_map, v_map, num_ctas, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// The wait of a gather: one thread polls the flag with acquire loads at
+// system scope, bounded by kWaitLimitNs (then TVP_DEVERR_TIMEOUT, no hang).
+__global__ void peer_wait_kernel(const int32_t* flag, int32_t target, int32_t* err) {
+  if (threadIdx.x != 0) return;
+  const unsigned long long start = global_timer_ns();
+  while (true) {
+    int32_t v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if ((int32_t)((uint32_t)v - (uint32_t)target) >= 0) return;
+    if (global_timer_ns() - start > kWaitLimitNs) {
+      record_error(err, TVP_DEVERR_TIMEOUT);
+      return;
+    }
+    __nanosleep(256);
+  }
 }
 
 }  // namespace
@@ -350,12 +411,14 @@ cudaError_t launch_heads(const DecodeParams& p, const CUtensorMap& k_map, const 
 cudaError_t launch_paged_decode_heads(const DecodeParams& p, const CUtensorMap& k_map,
                                       const CUtensorMap& v_map, int num_ctas,
                                       cudaStream_t stream) {
-  switch (p.kv_heads) {
-    case 1: return launch_heads<1>(p, k_map, v_map, num_ctas, stream);
-    case 2: return launch_heads<2>(p, k_map, v_map, num_ctas, stream);
-    case 4: return launch_heads<4>(p, k_map, v_map, num_ctas, stream);
-    default: return cudaErrorInvalidValue;
-  }
+  if (p.peer_rows != nullptr) return launch_heads_any<true>(p, k_map, v_map, num_ctas, stream);
+  return launch_heads_any<false>(p, k_map, v_map, num_ctas, stream);
+}
+
+cudaError_t launch_peer_wait(const int32_t* flag, int32_t target, int32_t* err,
+                             cudaStream_t stream) {
+  peer_wait_kernel<<<1, 32, 0, stream>>>(flag, target, err);
+  return cudaGetLastError();
 }
 
 }  // namespace tvp

@@ -46,6 +46,13 @@ struct DecodeParams {
   int kv_heads;      // KV heads the pools hold (1, 2, 4 or 8)
   float scale_log2;  // scale * log2(e)
   int32_t* err;
+  // KV-head-shard gather (tvp_paged_decode_attention_gather), else null / 0:
+  // outputs go to every rank's gathered rows [B][2048] at this rank's heads
+  // instead of `out`, and the last CTA to finish adds 1 to every rank's flag.
+  __nv_bfloat16* const* peer_rows;  // [world] device pointers
+  int32_t* const* peer_flags;       // [world] device pointers
+  int32_t* done_counter;            // CTAs finished in this launch (the last resets it)
+  int world, rank;
 };
 
 // K2c (tvp_compat.cu)
@@ -77,6 +84,18 @@ cudaError_t launch_paged_decode(const DecodeParams& p, long long pool_rows, int 
 cudaError_t launch_paged_decode_heads(const DecodeParams& p, const CUtensorMap& k_map,
                                       const CUtensorMap& v_map, int num_ctas,
                                       cudaStream_t stream);
+// Argument checks, workspace layout and parameter block of the FAST decode
+// (shared by tvp_paged_decode_attention and its gather form); TVP_OK or an error.
+int prepare_decode(const void* q, const void* k_pool, const void* v_pool, int num_pages,
+                   int num_layers, int layer, int kv_heads, int q_heads,
+                   const int32_t* d_block_tables, int table_stride, const int32_t* d_seq_lens,
+                   int batch, float scale, int num_ctas, void* d_workspace,
+                   size_t workspace_bytes, int32_t* d_error, DecodeParams* p, long long* pool_rows,
+                   int* ctas);
+// The wait of a KV-head-shard gather: until *flag - target >= 0 (bounded).
+cudaError_t launch_peer_wait(const int32_t* flag, int32_t target, int32_t* err,
+                             cudaStream_t stream);
+
 // 2-D tensor map over a pool of `rows` token rows of kv_heads x 64 channels.
 bool pool_tensor_map(const void* pool, long long rows, int kv_heads, CUtensorMap* out);
 cudaError_t launch_compat_decode(const CompatParams& p, int batch, cudaStream_t stream);

@@ -199,8 +199,40 @@ __device__ __forceinline__ void reduce_l(HeadState& st) {
   }
 }
 
-// Normalised BF16 output of a whole sequence for the 4 query heads at out_group.
-__device__ __forceinline__ void write_output(const HeadState& st, __nv_bfloat16* out_group,
+// Destination of one (sequence, KV head group) output of 4 x 64 channels:
+// this rank's rows at `local`, or, for a KV-head-shard gather, element `off`
+// of every rank's gathered rows (peers[0 .. world), plain stores over NVLink).
+struct OutGroup {
+  __device__ __forceinline__ static __nv_bfloat16* peer(__nv_bfloat16* const* peers, int r) {
+    return reinterpret_cast<__nv_bfloat16*>(
+        __ldg(reinterpret_cast<const unsigned long long*>(peers) + r));
+  }
+  __nv_bfloat16* local;
+  __nv_bfloat16* const* peers;
+  size_t off;
+  int world;
+  __device__ __forceinline__ void store(int i, __nv_bfloat16 v) const {
+    if (peers == nullptr) {
+      local[i] = v;
+      return;
+    }
+    for (int r = 0; r < world; ++r) peer(peers, r)[off + i] = v;
+  }
+  __device__ __forceinline__ void store16(int i, uint4 v) const {
+    if (peers == nullptr) {
+      *reinterpret_cast<uint4*>(local + i) = v;
+      return;
+    }
+    for (int r = 0; r < world; ++r) *reinterpret_cast<uint4*>(peer(peers, r) + off + i) = v;
+  }
+};
+
+__device__ __forceinline__ OutGroup local_out(__nv_bfloat16* group) {
+  return OutGroup{group, nullptr, 0, 1};
+}
+
+// Normalised BF16 output of a whole sequence for the 4 query heads of `out`.
+__device__ __forceinline__ void write_output(const HeadState& st, const OutGroup& out,
                                              const TileLane& tl) {
   if (tl.hc >= 2) return;  // columns 4-7 are padding
   const int h0 = 2 * tl.hc, h1 = 2 * tl.hc + 1;
@@ -208,10 +240,10 @@ __device__ __forceinline__ void write_output(const HeadState& st, __nv_bfloat16*
 #pragma unroll
   for (int d = 0; d < 4; ++d) {
     const int ch = 16 * d + tl.tr;
-    out_group[h0 * kHeadDim + ch] = __float2bfloat16_rn(st.acc[d][0] * inv0);
-    out_group[h1 * kHeadDim + ch] = __float2bfloat16_rn(st.acc[d][1] * inv1);
-    out_group[h0 * kHeadDim + ch + 8] = __float2bfloat16_rn(st.acc[d][2] * inv0);
-    out_group[h1 * kHeadDim + ch + 8] = __float2bfloat16_rn(st.acc[d][3] * inv1);
+    out.store(h0 * kHeadDim + ch, __float2bfloat16_rn(st.acc[d][0] * inv0));
+    out.store(h1 * kHeadDim + ch, __float2bfloat16_rn(st.acc[d][1] * inv1));
+    out.store(h0 * kHeadDim + ch + 8, __float2bfloat16_rn(st.acc[d][2] * inv0));
+    out.store(h1 * kHeadDim + ch + 8, __float2bfloat16_rn(st.acc[d][3] * inv1));
   }
 }
 
@@ -253,7 +285,7 @@ __device__ __forceinline__ int partial_slot(int r, int first, long long T, long 
 
 // Merges the partial pieces of sequence [first, end) for KV head group g from
 // the slots of ranges r0..r1 (lane -> query head lane/8 of the group, channels
-// (lane%8)*8 .. +7) and writes the normalised output at out_group.
+// (lane%8)*8 .. +7) and writes the normalised output to `out`.
 // Phase A: lane j reads m[4], l[4] of pieces j, j + 32, ... (all in flight at
 // once); the warp reduces the maxima and the normalisers.  Phase B: each lane
 // sums its 8 channels over the pieces, loading piece j + 1 before folding j;
@@ -274,7 +306,7 @@ __device__ __forceinline__ float pick(const float4& v, int h) {
 template <int BATCH>
 __device__ __forceinline__ void combine_partials(const float* partials, int groups, int g,
                                                  int first, int end, long long T, long long R,
-                                                 __nv_bfloat16* out_group, int lane) {
+                                                 const OutGroup& out, int lane) {
   const int r0 = range_of_page(first, T, R), r1 = range_of_page(end - 1, T, R);
   const int n = r1 - r0 + 1;
   const int h = lane >> 3, d0 = (lane & 7) * 8;
@@ -349,7 +381,7 @@ __device__ __forceinline__ void combine_partials(const float* partials, int grou
   packed.y = pack_bf16x2(o[2] * inv, o[3] * inv);
   packed.z = pack_bf16x2(o[4] * inv, o[5] * inv);
   packed.w = pack_bf16x2(o[6] * inv, o[7] * inv);
-  *reinterpret_cast<uint4*>(out_group + h * kHeadDim + d0) = packed;
+  out.store16(h * kHeadDim + d0, packed);
 }
 
 // Publishes a partial piece and, when it is the last of its sequence to arrive,
@@ -358,7 +390,7 @@ template <int BATCH>
 __device__ __forceinline__ void finish_partial(const HeadState& st, float* partials, int* counters,
                                                int groups, int g, int s, int slot, int first,
                                                int end, long long T, long long R,
-                                               __nv_bfloat16* out_group, const TileLane& tl,
+                                               const OutGroup& out, const TileLane& tl,
                                                int lane) {
   write_partial(st, partials + ((size_t)slot * groups + g) * kPartialFloats, tl);
   __threadfence();
@@ -374,7 +406,7 @@ __device__ __forceinline__ void finish_partial(const HeadState& st, float* parti
     }
   }
   last = __shfl_sync(0xffffffffu, last, 0);
-  if (last) combine_partials<BATCH>(partials, groups, g, first, end, T, R, out_group, lane);
+  if (last) combine_partials<BATCH>(partials, groups, g, first, end, T, R, out, lane);
 }
 
 }  // namespace tvp

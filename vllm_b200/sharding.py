@@ -80,19 +80,34 @@ def all_gather_head_shards(local, gathered_flat, group=None):
 
 class HeadShardedDecode:
     """One rank of KV-head-sharded decode attention: rank r holds KV heads
-    ``shard_by_kv_head(world)[r]`` of every page, runs the fused decode over
-    them and all-gathers the [B, 4 * kv_per_rank * 64] slices over the process
-    group (NCCL on GPUs) into the model's [B, 2048] rows.
+    ``shard_by_kv_head(world)[r]`` of every page and ``attend`` returns the
+    model's [B, 2048] attention rows on every rank.
 
-    The gather buffers are allocated once for ``max_batch`` rows.
+    mode "p2p": the all-gather is fused into the decode kernel
+    (``tvp_paged_decode_attention_gather``): each output group is stored
+    straight into every rank's gathered rows over NVLink and a bounded wait
+    orders the stream after all ranks' stores.  The rows live in two buffers
+    used alternately, so the rows ``attend`` returns stay valid until the call
+    after next.  mode "nccl": the decode writes this rank's slice and an NCCL
+    all-gather plus an interleave assembles the rows.
+
+    Every rank makes the same calls in the same order.  Buffers are allocated
+    once for ``max_batch`` rows.
     """
 
-    def __init__(self, max_batch: int, group=None, device=None, num_ctas: int = 0):
+    def __init__(self, max_batch: int, group=None, device=None, num_ctas: int = 0,
+                 mode: str = "p2p"):
+        import ctypes
+
         import torch
         import torch.distributed as dist
 
+        from . import _native as N
         from . import ops
 
+        if mode not in ("p2p", "nccl"):
+            raise ValueError("mode must be 'p2p' or 'nccl'")
+        self.mode = mode
         self.dist = dist
         self.group = group
         self.world = dist.get_world_size(group)
@@ -100,30 +115,99 @@ class HeadShardedDecode:
         self.heads = shard_by_kv_head(self.world)[self.rank]
         self.kv_heads = len(self.heads)
         self.device = torch.device(device if device is not None else "cuda")
+        self.max_batch = max_batch
         self.workspace = ops.DecodeWorkspace(max_batch, self.device, num_ctas=num_ctas,
                                              kv_heads=self.kv_heads)
         self.width = 4 * self.kv_heads * 64
-        self.local = torch.empty((max_batch, self.width), dtype=torch.bfloat16, device=self.device)
-        # flat [world * B, width]: rank r's rows at [r B, (r + 1) B) for any B <= max_batch
-        self.gathered = torch.empty((self.world * max_batch, self.width), dtype=torch.bfloat16,
-                                    device=self.device)
+        self._h = None
+        if mode == "nccl":
+            self.local = torch.empty((max_batch, self.width), dtype=torch.bfloat16,
+                                     device=self.device)
+            # flat [world * B, width]: rank r's rows at [r B, (r + 1) B) for any B <= max_batch
+            self.gathered = torch.empty((self.world * max_batch, self.width),
+                                        dtype=torch.bfloat16, device=self.device)
+            return
+        lib = N.load()
+        with torch.cuda.device(self.device):
+            h = ctypes.c_void_p()
+            N.check(lib.tvp_head_gather_create(self.world, self.rank, self.kv_heads, max_batch,
+                                               ctypes.byref(h)), "tvp_head_gather_create")
+            self._h = h
+            mine = (ctypes.c_char * N.TVP_IPC_HANDLE_BYTES)()
+            N.check(lib.tvp_head_gather_export(h, mine), "tvp_head_gather_export")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(mine), group=group)
+            blob = b"".join(handles)
+            N.check(lib.tvp_head_gather_connect(h, blob), "tvp_head_gather_connect")
+            self.rows = []
+            for b in (0, 1):
+                ptr = ctypes.c_void_p()
+                N.check(lib.tvp_head_gather_rows(h, b, ctypes.byref(ptr)), "tvp_head_gather_rows")
+                from .cache import _CudaArray
+                self.rows.append(torch.as_tensor(
+                    _CudaArray(ptr.value, (max_batch, 2048), "<u2"), device=self.device
+                ).view(torch.bfloat16))
+        self.buffer = 0
 
     def plan(self, seq_lens, table_stride: int, error=None, stream=None):
         from . import ops
         ops.decode_plan(seq_lens, table_stride, self.workspace, error=error, stream=stream)
 
     def attend(self, q_local, k_pool, v_pool, layer, block_tables, seq_lens, error=None,
-               gather=True):
-        """Decode attention of this rank's heads; with ``gather`` the all-gather
-        over the group follows and the [B, 2048] rows are returned."""
+               gather=True, stream=None, scale=0.125):
+        """Decode attention of this rank's heads, then the rows of all heads
+        ([B, 2048] on every rank).  ``gather=False`` (nccl mode) returns this
+        rank's [B, 4 * kv_heads * 64] slice without the collective."""
+        from . import _native as N
         from . import ops
         batch = seq_lens.numel()
-        local = self.local[:batch]
-        ops.paged_decode_attention(q_local, k_pool, v_pool, layer, block_tables, seq_lens,
-                                   self.workspace, out=local, error=error)
-        if not gather:
-            return local
-        return all_gather_head_shards(local, self.gathered, self.group)
+        if self.mode == "nccl" or not gather:
+            if self.mode != "nccl":
+                raise ValueError("gather=False needs mode='nccl'")
+            local = self.local[:batch]
+            ops.paged_decode_attention(q_local, k_pool, v_pool, layer, block_tables, seq_lens,
+                                       self.workspace, out=local, scale=scale, error=error,
+                                       stream=stream)
+            if not gather:
+                return local
+            return all_gather_head_shards(local, self.gathered, self.group)
+        if self.workspace.batch != batch:
+            raise ValueError("plan() this batch first")
+        lib = N.load()
+        num_layers, num_pages, kv_heads = ops._pool_geometry(k_pool, v_pool)
+        if kv_heads != self.kv_heads or q_local.shape != (batch, self.width):
+            raise ValueError("pools / q do not hold this rank's heads")
+        st = ops._stream(stream)
+        rc = lib.tvp_paged_decode_attention_gather(
+            ops._ptr(q_local), ops._ptr(k_pool), ops._ptr(v_pool), num_pages, num_layers, layer,
+            kv_heads, 4 * kv_heads, ops._ptr(block_tables), block_tables.shape[1],
+            ops._ptr(seq_lens), batch, float(scale), self.workspace.num_ctas,
+            ops._ptr(self.workspace.buffer), self.workspace.nbytes, self._h, self.buffer,
+            ops._ptr(error), st)
+        N.check(rc, "tvp_paged_decode_attention_gather")
+        N.check(lib.tvp_head_gather_wait(self._h, self.buffer, ops._ptr(error), st),
+                "tvp_head_gather_wait")
+        rows = self.rows[self.buffer][:batch]
+        self.buffer ^= 1
+        return rows
+
+    def close(self):
+        """Frees the gather buffers; every rank calls it.  Every rank first
+        stops writing and closes its peers' buffers, then (after a barrier)
+        frees its own, which no peer maps any more."""
+        if self._h is None:
+            return
+        import torch
+
+        from . import _native as N
+        lib = N.load()
+        torch.cuda.synchronize(self.device)
+        self.dist.barrier(group=self.group)
+        N.check(lib.tvp_head_gather_disconnect(self._h), "tvp_head_gather_disconnect")
+        self.dist.barrier(group=self.group)
+        N.check(lib.tvp_head_gather_destroy(self._h), "tvp_head_gather_destroy")
+        self._h = None
+        self.rows = []
 
 
 def imbalance(lens, shards) -> float:
