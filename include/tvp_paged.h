@@ -185,9 +185,8 @@ int tvp_paged_decode_attention_noalloc(const tvp_bf16* q, const tvp_bf16* k_pool
  * the same block tables on every rank) and the [batch][2048] attention rows
  * end up on every rank.  The decode kernel stores each finished output group
  * straight into every rank's gathered rows over NVLink (peer memory opened
- * through CUDA IPC) and its last CTA bumps every rank's flag; a wait launch
- * orders the stream after all ranks' stores.  Every rank makes the same calls
- * in the same order (SPMD).
+ * through CUDA IPC); its last CTA bumps every rank's flag and waits for all
+ * ranks' signals.  Every rank makes the same calls in the same order (SPMD).
  * ======================================================================= */
 #define TVP_IPC_HANDLE_BYTES 64
 typedef struct tvp_head_gather tvp_head_gather;
@@ -206,9 +205,12 @@ int tvp_head_gather_connect(tvp_head_gather* g, const void* handles);
 int tvp_head_gather_rows(const tvp_head_gather* g, int buffer, tvp_bf16** rows_out);
 /* FAST decode attention of this rank's heads (arguments as for
  * tvp_paged_decode_attention, kv_heads = 8 / world, no `out`), written into
- * every rank's gathered rows of `buffer`.  Alternate the buffers from one
- * layer to the next: a rank may start the next layer while another rank still
- * reads this one's rows. */
+ * every rank's gathered rows of `buffer`.  The launch ends once every rank's
+ * rows of this call are in this rank's buffer: its last CTA waits for all
+ * ranks' signals, bounded by 2 s, after which it sets TVP_DEVERR_TIMEOUT in
+ * *d_error and ends (a rank that stopped never hangs the others; the group is
+ * then unusable).  Alternate the buffers from one layer to the next: a rank
+ * may start the next layer while another rank still reads this one's rows. */
 int tvp_paged_decode_attention_gather(const tvp_bf16* q, const tvp_bf16* k_pool,
                                       const tvp_bf16* v_pool, int num_pages, int num_layers,
                                       int layer, int kv_heads, int q_heads,
@@ -217,12 +219,6 @@ int tvp_paged_decode_attention_gather(const tvp_bf16* q, const tvp_bf16* k_pool,
                                       int num_ctas, void* d_workspace, size_t workspace_bytes,
                                       tvp_head_gather* g, int buffer, int32_t* d_error,
                                       tvp_stream_t stream);
-/* Orders `stream` after every rank's stores of the last gather into
- * `buffer`: a one-thread kernel polls this rank's flag, bounded by 2 s, after
- * which it sets TVP_DEVERR_TIMEOUT in *d_error and returns (a rank that
- * stopped never hangs the others; the group is then unusable). */
-int tvp_head_gather_wait(const tvp_head_gather* g, int buffer, int32_t* d_error,
-                         tvp_stream_t stream);
 /* Teardown, in two steps on every rank: disconnect (waits for this device,
  * then closes the peers' allocations), a barrier across ranks, destroy (frees
  * this rank's allocation, which no peer maps any more).  Destroy alone also

@@ -127,7 +127,6 @@ def test_head_gather_rejects_bad_arguments_on_host(native):
     assert native.tvp_head_gather_create(2, 2, 4, 16, ctypes.byref(h)) == N.TVP_ERR_INVALID_ARGUMENT
     assert native.tvp_head_gather_create(2, 0, 4, 0, ctypes.byref(h)) == N.TVP_ERR_INVALID_ARGUMENT
     assert native.tvp_head_gather_create(2, 0, 4, 16, None) == N.TVP_ERR_INVALID_ARGUMENT
-    assert native.tvp_head_gather_wait(None, 0, None, None) == N.TVP_ERR_INVALID_ARGUMENT
     assert native.tvp_head_gather_destroy(None) == N.TVP_ERR_INVALID_ARGUMENT
     fake = ctypes.c_void_p(0x10000)
     assert native.tvp_paged_decode_attention_gather(

@@ -1,10 +1,10 @@
-"""The wait of the fused KV-head-shard gather gives up instead of hanging.
-Two processes share one GPU: rank 1 connects and then launches nothing, so
-rank 0's flag never reaches the count of both ranks' signals.  Rank 0's wait
-must end after its bound (2 s) with TVP_DEVERR_TIMEOUT set, the rows of its own
-heads must be right (the gather's stores reached its own buffer), and the
-context must stay usable.  Only one kernel waits, on a flag nothing else will
-set; no two waiting kernels share the GPU."""
+"""The wait at the end of the fused KV-head-shard gather gives up instead of
+hanging.  Two processes share one GPU: rank 1 connects and then launches
+nothing, so rank 0's flag never reaches the count of both ranks' signals.
+Rank 0's gather launch must end after its bound (2 s) with TVP_DEVERR_TIMEOUT
+set, the rows of its own heads must be right (the gather's stores reached its
+own buffer), and the context must stay usable.  Only one kernel waits, on a
+flag nothing else will set; no two waiting kernels share the GPU."""
 import ctypes
 
 import numpy as np
@@ -55,7 +55,6 @@ def _rank(rank, q_out, q_in, mine_done, other_done, results):
         N.check(lib.tvp_paged_decode_attention_gather(
             P(q), P(kp), P(vp), case.num_pages, 1, 0, 4, 16, P(tables), case.tables.shape[1],
             P(lens), len(LENS), 0.125, ws.num_ctas, P(ws.buffer), ws.nbytes, h, 0, P(err), stream))
-        N.check(lib.tvp_head_gather_wait(h, 0, P(err), stream))
         torch.cuda.synchronize()
         bits = int(err.item())
         rows_ptr = ctypes.c_void_p()

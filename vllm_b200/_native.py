@@ -74,7 +74,6 @@ _SIGNATURES = {
                                                   c_int, c_int, c_void_p, c_int, c_void_p, c_int,
                                                   ctypes.c_float, c_int, c_void_p, c_size_t,
                                                   c_void_p, c_int, c_void_p, c_void_p]),
-    "tvp_head_gather_wait": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
     "tvp_head_gather_disconnect": (c_int, [c_void_p]),
     "tvp_head_gather_destroy": (c_int, [c_void_p]),
     "tvp_cache_create": (c_int, [c_int, c_int, c_int, c_int, c_int, POINTER(c_void_p)]),

@@ -94,9 +94,9 @@ __device__ __forceinline__ void merge_ways(HeadState& st, float* scratch, int wa
 // GATHER: the KV-head-shard all-gather fused into the kernel.  Each output
 // group is stored straight into every rank's gathered rows [B][2048] at this
 // rank's heads (plain stores to peer memory over NVLink, issued as soon as the
-// group is final); every thread fences at system scope after its last store,
-// each CTA counts itself done, and the last CTA of the launch adds 1 to every
-// rank's flag.  A rank whose flag reached launches x world has all rows.
+// group is final); each CTA counts itself done, the last CTA of the launch
+// adds 1 to every rank's flag and waits until its own flag reached
+// launches x world, i.e. until every rank's rows of this launch have landed.
 template <int KVH, bool REGSPLIT, bool GATHER>
 __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
     paged_decode_heads_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap k_map,
@@ -317,20 +317,32 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
   }
 
   if (GATHER) {
-    // Every row this CTA stored is visible system-wide before the CTA counts
-    // itself done; the last CTA then signals every rank (its own included).
-    __threadfence_system();
+    // The CTA's row stores are ordered before thread 0's fence by the barrier;
+    // the fence releases them (system scope) before the CTA counts itself
+    // done.  The last CTA acquires every CTA's release, signals every rank
+    // (its own included) and waits, bounded, until all ranks have signalled:
+    // when the kernel ends, every rank's rows of this launch are here.
     named_barrier_sync(kDoneBarrier, 2 * kStageTiles * 32);
     if (threadIdx.x == 0) {
-      __threadfence_system();  // release: the stores this thread saw through the barrier
+      __threadfence_system();
       const int done = atomicAdd(p.done_counter, 1);
       if (done == (int)gridDim.x - 1) {
         atomicExch(p.done_counter, 0);  // ready for the next launch
-        __threadfence_system();         // acquire the other CTAs' releases, release to the peers
-        for (int r = 0; r < p.world; ++r)
-          atomicAdd_system(reinterpret_cast<int*>(
-                               __ldg(reinterpret_cast<const unsigned long long*>(p.peer_flags) + r)),
-                           1);
+        __threadfence_system();
+        const unsigned long long* flags = reinterpret_cast<const unsigned long long*>(p.peer_flags);
+        for (int r = 0; r < p.world; ++r) atomicAdd_system(reinterpret_cast<int*>(__ldg(flags + r)), 1);
+        const int32_t* mine = reinterpret_cast<const int32_t*>(__ldg(flags + p.rank));
+        const unsigned long long start = global_timer_ns();
+        while (true) {
+          int32_t v;
+          asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+          if ((int32_t)((uint32_t)v - (uint32_t)p.flag_target) >= 0) break;
+          if (global_timer_ns() - start > kWaitLimitNs) {
+            record_error(p.err, TVP_DEVERR_TIMEOUT);
+            break;
+          }
+          __nanosleep(128);
+        }
       }
     }
   }
@@ -389,23 +401,6 @@ cudaError_t launch_heads_any(const DecodeParams& p, const CUtensorMap& k_map,
   }
 }
 
-// The wait of a gather: one thread polls the flag with acquire loads at
-// system scope, bounded by kWaitLimitNs (then TVP_DEVERR_TIMEOUT, no hang).
-__global__ void peer_wait_kernel(const int32_t* flag, int32_t target, int32_t* err) {
-  if (threadIdx.x != 0) return;
-  const unsigned long long start = global_timer_ns();
-  while (true) {
-    int32_t v;
-    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-    if ((int32_t)((uint32_t)v - (uint32_t)target) >= 0) return;
-    if (global_timer_ns() - start > kWaitLimitNs) {
-      record_error(err, TVP_DEVERR_TIMEOUT);
-      return;
-    }
-    __nanosleep(256);
-  }
-}
-
 }  // namespace
 
 cudaError_t launch_paged_decode_heads(const DecodeParams& p, const CUtensorMap& k_map,
@@ -413,12 +408,6 @@ cudaError_t launch_paged_decode_heads(const DecodeParams& p, const CUtensorMap& 
                                       cudaStream_t stream) {
   if (p.peer_rows != nullptr) return launch_heads_any<true>(p, k_map, v_map, num_ctas, stream);
   return launch_heads_any<false>(p, k_map, v_map, num_ctas, stream);
-}
-
-cudaError_t launch_peer_wait(const int32_t* flag, int32_t target, int32_t* err,
-                             cudaStream_t stream) {
-  peer_wait_kernel<<<1, 32, 0, stream>>>(flag, target, err);
-  return cudaGetLastError();
 }
 
 }  // namespace tvp

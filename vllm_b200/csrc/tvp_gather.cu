@@ -7,8 +7,8 @@
 // assembled on every GPU.  Instead of a decode followed by a collective, the
 // decode kernel stores each finished output group straight into every rank's
 // gathered rows (peer memory opened through CUDA IPC, plain stores over
-// NVLink) and its last CTA adds 1 to every rank's flag; a one-thread wait
-// kernel on each rank then orders the stream after all ranks' stores.
+// NVLink); its last CTA adds 1 to every rank's flag and waits, bounded, until
+// every rank has signalled, so the launch ends with all ranks' rows in place.
 //
 // Per rank, one device allocation, exported once:
 //   [flag 0 | flag 1 | done counter | pad to 256 B][rows 0][rows 1]
@@ -160,21 +160,11 @@ int tvp_paged_decode_attention_gather(const tvp_bf16* q, const tvp_bf16* k_pool,
   p.done_counter = done_of(g->base);
   p.world = g->world;
   p.rank = g->rank;
+  p.flag_target = (int32_t)((g->epoch[buffer] + 1u) * (uint32_t)g->world);
   if (launch_paged_decode(p, pool_rows, ctas, static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return TVP_ERR_RUNTIME;
   ++g->epoch[buffer];
   return TVP_OK;
-}
-
-int tvp_head_gather_wait(const tvp_head_gather* g, int buffer, int32_t* d_error,
-                         tvp_stream_t stream) {
-  if (!g || !g->connected || buffer < 0 || buffer > 1 || !on_device(g))
-    return TVP_ERR_INVALID_ARGUMENT;
-  const int32_t target = (int32_t)(g->epoch[buffer] * (uint32_t)g->world);
-  return launch_peer_wait(flag_of(g->base, buffer), target, d_error,
-                          static_cast<cudaStream_t>(stream)) == cudaSuccess
-             ? TVP_OK
-             : TVP_ERR_RUNTIME;
 }
 
 int tvp_head_gather_disconnect(tvp_head_gather* g) {

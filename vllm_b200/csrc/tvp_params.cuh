@@ -53,6 +53,7 @@ struct DecodeParams {
   int32_t* const* peer_flags;       // [world] device pointers
   int32_t* done_counter;            // CTAs finished in this launch (the last resets it)
   int world, rank;
+  int32_t flag_target;              // this rank's flag once every rank signalled this launch
 };
 
 // K2c (tvp_compat.cu)
@@ -92,10 +93,6 @@ int prepare_decode(const void* q, const void* k_pool, const void* v_pool, int nu
                    int batch, float scale, int num_ctas, void* d_workspace,
                    size_t workspace_bytes, int32_t* d_error, DecodeParams* p, long long* pool_rows,
                    int* ctas);
-// The wait of a KV-head-shard gather: until *flag - target >= 0 (bounded).
-cudaError_t launch_peer_wait(const int32_t* flag, int32_t target, int32_t* err,
-                             cudaStream_t stream);
-
 // 2-D tensor map over a pool of `rows` token rows of kv_heads x 64 channels.
 bool pool_tensor_map(const void* pool, long long rows, int kv_heads, CUtensorMap* out);
 cudaError_t launch_compat_decode(const CompatParams& p, int batch, cudaStream_t stream);

@@ -85,8 +85,8 @@ class HeadShardedDecode:
 
     mode "p2p": the all-gather is fused into the decode kernel
     (``tvp_paged_decode_attention_gather``): each output group is stored
-    straight into every rank's gathered rows over NVLink and a bounded wait
-    orders the stream after all ranks' stores.  The rows live in two buffers
+    straight into every rank's gathered rows over NVLink, and the launch ends
+    once all ranks' rows have landed (bounded wait in its last CTA).  The rows live in two buffers
     used alternately, so the rows ``attend`` returns stay valid until the call
     after next.  mode "nccl": the decode writes this rank's slice and an NCCL
     all-gather plus an interleave assembles the rows.
@@ -185,8 +185,6 @@ class HeadShardedDecode:
             ops._ptr(self.workspace.buffer), self.workspace.nbytes, self._h, self.buffer,
             ops._ptr(error), st)
         N.check(rc, "tvp_paged_decode_attention_gather")
-        N.check(lib.tvp_head_gather_wait(self._h, self.buffer, ops._ptr(error), st),
-                "tvp_head_gather_wait")
         rows = self.rows[self.buffer][:batch]
         self.buffer ^= 1
         return rows
