@@ -388,6 +388,7 @@ def extras(args, dev, case, k_pool, v_pool, q_all, out, tables, seq_lens, ws):
                                 "tolerance": "1e-2 abs + 2e-2 rel"}
     res["long_context"] = bench_long_context(dev)
     res["long_context_head_shards"] = bench_long_context_heads(dev)
+    res["prefill"] = bench_prefill(dev)
     res["decode_small"] = bench_decode_small(dev)
     res["e2e_llama"] = bench_e2e_llama()
     return res
@@ -565,6 +566,80 @@ def bench_head_sharded(dev, rank, world, local_rank, iters=20):
     return res
 
 
+def tensor_peak():
+    try:
+        return float(json.loads(PEAKS_FILE.read_text())["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def bench_prefill(dev, iters=20):
+    """K3, paged causal prefill attention: 4 prompts x 1024 tokens (the
+    reference's cap) and 1 x 8192 (beyond it), 1 layer, L2 flushed between
+    launches; against the reference's contiguous cuBLAS prefill path on the
+    1024-token prompts (its per-prompt function, 4 calls)."""
+    import ctypes
+    import torch
+    import oracle
+    from vllm_b200 import ops
+    peak, kind = tensor_peak()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    res = {"roofline": "tensor (bf16 mma); flops = 256 (p + 1) per query head per token at position p",
+           "peak_source": f"{kind} bf16_tflops {peak}"}
+    ref = oracle.load_reference()
+    for name, prompts in (("4x1024", [1024] * 4), ("1x8192", [8192])):
+        case = W.decode_random(21, prompts, with_data=False, slack_pages=0)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(5)
+        shape = (1, case.num_pages, 16, W.KV_DIM)
+        kp = torch.empty(shape, dtype=torch.bfloat16, device=dev).normal_(generator=gen)
+        vp = torch.empty(shape, dtype=torch.bfloat16, device=dev).normal_(generator=gen)
+        n = sum(prompts)
+        q = torch.randn((n, W.Q_DIM), generator=gen, device=dev).to(torch.bfloat16)
+        cu = torch.tensor(np.concatenate([[0], np.cumsum(prompts)]), dtype=torch.int32, device=dev)
+        pos0 = torch.zeros(len(prompts), dtype=torch.int32, device=dev)
+        tables = torch.from_numpy(case.tables).to(dev)
+        out = torch.empty_like(q)
+        times = []
+        for i in range(iters + 3):
+            flush.fill_(i & 0xFF)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            ops.paged_prefill_attention(q, kp, vp, 0, tables, cu, pos0, max(prompts), out=out)
+            b.record()
+            torch.cuda.synchronize(dev)
+            if i >= 3:
+                times.append(a.elapsed_time(b))
+        us = statistics.median(times) * 1e3
+        flops = sum(256.0 * (L * (L + 1) / 2) * W.Q_HEADS for L in prompts)
+        entry = {"us": round(us, 2), "TFLOPs": round(flops / us / 1e6, 2),
+                 "frac_of_peak": round(flops / us / 1e6 / peak, 4)}
+        if ref is not None and max(prompts) <= 1024:
+            # the reference's prefill attention, one prompt per call, same q/k/v per prompt
+            ref_us = 0.0
+            ref_out = torch.empty((1024, W.Q_DIM), dtype=torch.bfloat16, device=dev)
+            for s, L in enumerate(prompts):
+                pages = torch.from_numpy(case.tables[s, :(L + 15) // 16].astype(np.int64)).to(dev)
+                kc = kp[0][pages].reshape(-1, W.KV_DIM)[:L].contiguous()
+                vc = vp[0][pages].reshape(-1, W.KV_DIM)[:L].contiguous()
+                qs = q[int(cu[s]):int(cu[s + 1])].contiguous()
+                ms = ctypes.c_float(0.0)
+                vptr = lambda t: ctypes.c_void_p(t.data_ptr())
+                rc = ref.ref_prefill_attention(vptr(qs), vptr(kc), vptr(vc), L, vptr(ref_out),
+                                               iters, 256 << 20, ctypes.byref(ms))
+                if rc != 0:
+                    ref_us = None
+                    break
+                ref_us += ms.value * 1e3
+            if ref_us:
+                entry["reference_cublas_us"] = round(ref_us, 2)
+                entry["speedup_vs_reference"] = round(ref_us / us, 2)
+        res[name] = entry
+        del kp, vp
+        torch.cuda.empty_cache()
+    return res
+
+
 def bench_decode_small(dev, iters=50):
     """decode_small (4 rows, L = 17..256): our fused launch vs the reference's
     gather + cuBLAS + softmax sequence, both with L2 flushed between launches."""
@@ -633,7 +708,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
-    ap.add_argument("--only", choices=["long_context", "long_context_heads", "decode_small"],
+    ap.add_argument("--only", choices=["long_context", "long_context_heads", "decode_small",
+                                       "prefill"],
                     help="run one single-GPU sub-measurement alone and print its JSON (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -649,7 +725,7 @@ def main():
         dev = torch.device("cuda", 0)
         torch.cuda.set_device(dev)
         fn = {"long_context": bench_long_context, "long_context_heads": bench_long_context_heads,
-              "decode_small": bench_decode_small}[args.only]
+              "decode_small": bench_decode_small, "prefill": bench_prefill}[args.only]
         print(json.dumps({args.only: fn(dev)}), flush=True)
         return
     import torch

@@ -148,6 +148,29 @@ int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const 
                                tvp_bf16* out, int32_t* d_error, tvp_stream_t stream);
 
 /*
+ * K3 — paged causal prefill attention, reading K and V from the pages.
+ *
+ * Replaces the prefill attention of src/model/paged_transformer.cu:37-40
+ * (computeAttentionScores, causalMask, softmaxRows, attentionScoresTimesV over
+ * the contiguous K/V, src/model/attention.cu:10-51,144-192,
+ * src/model/causalMask.cu:7-38, src/model/softmax.cu:47-72), without its
+ * 1024-token cap and without a score matrix in memory.
+ * Queries are varlen: sequence s (row s of d_block_tables) owns query tokens
+ * [d_cu_q[s], d_cu_q[s + 1]) at positions d_q_pos0[s], d_q_pos0[s] + 1, ...;
+ * each attends the keys 0..its position already in the sequence's pages
+ * (append them first with tvp_rope_append).  d_q_pos0[s] = 0 is a prompt;
+ * d_q_pos0[s] = L0 > 0 a prefill chunk after L0 cached tokens.
+ * q, out: [num_tokens][q_heads * 64] BF16, head-major as the reference;
+ * max_q_len >= the longest sequence's query count.
+ */
+int tvp_paged_prefill_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const tvp_bf16* v_pool,
+                                int num_pages, int num_layers, int layer, int kv_heads, int q_heads,
+                                const int32_t* d_block_tables, int table_stride,
+                                const int32_t* d_cu_q, const int32_t* d_q_pos0, int num_seqs,
+                                int max_q_len, float scale, tvp_bf16* out, int32_t* d_error,
+                                tvp_stream_t stream);
+
+/*
  * K2 without any allocation.  This entry point has no counterpart in the
  * reference.  It is for callers that cannot call cudaMalloc: code whose
  * device memory is owned by a host framework's pool, plug-ins running under a

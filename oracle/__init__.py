@@ -90,6 +90,9 @@ def load_reference():
                                      c_int, POINTER(c_int32), c_int, c_void_p, c_int, c_size_t,
                                      POINTER(c_float)]
     lib.ref_paged_decode.restype = c_int
+    lib.ref_prefill_attention.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int,
+                                          c_size_t, POINTER(c_float)]
+    lib.ref_prefill_attention.restype = c_int
     _ref = lib
     return lib
 
@@ -175,6 +178,26 @@ def decode_attention_f64(q, k_pool, v_pool, layer, tables, lens, scale=0.125, th
     if rc != 0:
         raise ValueError("page table entry out of range")
     return out
+
+
+def prefill_attention(q, k_pool, v_pool, layer, tables, cu_q, q_pos0, scale=0.125, threads=0):
+    """Reference-semantics causal prefill attention over the pages; bf16 bits
+    [num_tokens, q_heads*64].  Query token t of sequence s, at position p,
+    attends keys 0..p: the reference's prefill row (src/model/paged_transformer.cu:37-40:
+    BF16 scores, causal mask, softmaxRows, FP32 P.V) has -inf past p, whose
+    exp is exactly 0 in its pairwise sum, so it equals decode attention with
+    length p + 1 (src/model/paged_attention.cu:133-161)."""
+    cu_q = np.asarray(cu_q, dtype=np.int64)
+    q_pos0 = np.asarray(q_pos0, dtype=np.int64)
+    n = int(cu_q[-1])
+    rows = np.empty(n, dtype=np.int64)
+    lens = np.empty(n, dtype=np.int32)
+    for s in range(len(q_pos0)):
+        a, b = int(cu_q[s]), int(cu_q[s + 1])
+        rows[a:b] = s
+        lens[a:b] = q_pos0[s] + np.arange(b - a) + 1
+    tab = np.ascontiguousarray(np.asarray(tables, dtype=np.int32)[rows])
+    return decode_attention(q, k_pool, v_pool, layer, tab, lens, scale=scale, threads=threads)
 
 
 def max_threads() -> int:

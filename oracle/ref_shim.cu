@@ -11,6 +11,9 @@
 //                                  softmaxRows per (row, head), pagedAttentionScoresTimesV,
 //                                  freePagedBatch, in the order of
 //                                  src/model/paged_transformer.cu:65,85-94,135
+//   ref_prefill_attention       -> computeAttentionScores, causalMask, softmaxRows,
+//                                  attentionScoresTimesV over contiguous q, k, v
+//                                  (src/model/paged_transformer.cu:37-40; n <= 1024)
 // Pools are caller-owned device buffers in the reference layout; the shim
 // wraps them in the reference's PagedKVCache without taking ownership.
 #include <cublas_v2.h>
@@ -22,6 +25,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "causalMask.cuh"
 #include "paged_attention.cuh"
 #include "paged_kvcache.cuh"
 #include "rope.cuh"
@@ -160,6 +164,60 @@ int ref_paged_decode(const uint16_t* d_q, uint16_t* k_pool, uint16_t* v_pool, in
     rc = -2;
   }
   freePagedBatch(md);
+  cudaFree(scores);
+  cudaFree(flush);
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  if (rc == 0) rc = finish();
+  return rc;
+}
+
+// Prefill attention of one prompt of n tokens: q [n][2048], k, v [n][512]
+// (post-RoPE, contiguous, as the reference's prefill leaves them), out [n][2048].
+int ref_prefill_attention(const uint16_t* d_q, const uint16_t* d_k, const uint16_t* d_v, int n,
+                          uint16_t* d_out, int iters, size_t flush_bytes, float* ms_out) {
+  if (n <= 0 || n > 1024) return -1;
+  __nv_bfloat16* scores = nullptr;
+  void* flush = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  int rc = 0;
+  try {
+    if (cudaMalloc(&scores, sizeof(__nv_bfloat16) * 32 * (size_t)n * n) != cudaSuccess)
+      throw std::runtime_error("cudaMalloc scores");
+    cublasHandle_t h = cublas();
+    auto q = reinterpret_cast<__nv_bfloat16*>(const_cast<uint16_t*>(d_q));
+    auto k = reinterpret_cast<__nv_bfloat16*>(const_cast<uint16_t*>(d_k));
+    auto v = reinterpret_cast<__nv_bfloat16*>(const_cast<uint16_t*>(d_v));
+    auto out = reinterpret_cast<__nv_bfloat16*>(d_out);
+    auto step = [&]() {
+      computeAttentionScores(h, q, k, scores, n);
+      causalMask(scores, n);
+      softmaxRows(scores, 32 * n, n);
+      attentionScoresTimesV(h, scores, v, out, n);
+    };
+    step();
+    if (cudaDeviceSynchronize() != cudaSuccess) throw std::runtime_error("prefill failed");
+    if (iters > 0 && ms_out) {
+      if (flush_bytes && cudaMalloc(&flush, flush_bytes) != cudaSuccess)
+        throw std::runtime_error("cudaMalloc flush");
+      cudaEventCreate(&e0);
+      cudaEventCreate(&e1);
+      double total = 0.0;
+      for (int i = 0; i < iters; ++i) {
+        if (flush) cudaMemsetAsync(flush, i & 0xff, flush_bytes);
+        cudaEventRecord(e0);
+        step();
+        cudaEventRecord(e1);
+        cudaEventSynchronize(e1);
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        total += ms;
+      }
+      *ms_out = static_cast<float>(total / iters);
+    }
+  } catch (const std::exception&) {
+    rc = -2;
+  }
   cudaFree(scores);
   cudaFree(flush);
   if (e0) cudaEventDestroy(e0);

@@ -66,6 +66,10 @@ _SIGNATURES = {
                                                    c_int, c_int, c_int, c_void_p, c_int, c_void_p,
                                                    c_int, c_float, c_int, c_void_p, c_void_p,
                                                    c_void_p]),
+    "tvp_paged_prefill_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                            c_int, c_int, c_void_p, c_int, c_void_p, c_void_p,
+                                            c_int, c_int, ctypes.c_float, c_void_p, c_void_p,
+                                            c_void_p]),
     "tvp_head_gather_create": (c_int, [c_int, c_int, c_int, c_int, POINTER(c_void_p)]),
     "tvp_head_gather_export": (c_int, [c_void_p, c_void_p]),
     "tvp_head_gather_connect": (c_int, [c_void_p, c_void_p]),

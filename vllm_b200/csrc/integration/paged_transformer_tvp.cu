@@ -17,9 +17,12 @@
 // The layer loop around them calls the reference's functions in the
 // reference's order, because its outputs (tokens) are what must not change.
 //
-// Decode numerics: TVP_DECODE_MODE=fast selects TVP_MODE_FAST; the default is
-// TVP_MODE_COMPAT (the reference's BF16 score/probability rounding), which is
-// what greedy-token identity with the unmodified engine needs.
+// Decode numerics: TVP_DECODE_MODE=fast selects TVP_MODE_FAST, which also
+// swaps the prefill attention (paged_transformer.cu:37-40) for
+// tvp_paged_prefill_attention over the pages; the default is TVP_MODE_COMPAT
+// (the reference's BF16 score/probability rounding, and its own prefill
+// attention), which is what greedy-token identity with the unmodified engine
+// needs.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -64,7 +67,7 @@ void check_tvp(int rc) {
 
 // Device buffers that live for the process (one set per device in use).
 struct PathState {
-  int32_t* prefill = nullptr;  // [table (64) | positions (1024) | rows (1024)]
+  int32_t* prefill = nullptr;  // [table (64) | positions (1024) | rows (1024) | cu_q (2) | pos0 (1)]
   int32_t* decode = nullptr;   // [tables (4 x 64) | positions (4) | lengths (4)]
   int32_t* error = nullptr;
   void* workspace = nullptr;
@@ -83,7 +86,7 @@ PathState& path_state() {
   PathState& st = states[dev];
   if (!ready[dev]) {
     check_cuda(cudaMalloc(reinterpret_cast<void**>(&st.prefill),
-                          (kTableStride + 2 * kMaxContext) * sizeof(int32_t)));
+                          (kTableStride + 2 * kMaxContext + 4) * sizeof(int32_t)));
     check_cuda(cudaMalloc(reinterpret_cast<void**>(&st.decode),
                           (kMaxBatch * kTableStride + 2 * kMaxBatch) * sizeof(int32_t)));
     check_cuda(cudaMalloc(reinterpret_cast<void**>(&st.error), sizeof(int32_t)));
@@ -118,14 +121,17 @@ int transformerForwardPaged(cublasHandle_t cublas_handle, __nv_bfloat16* hidden_
   reserveSequenceBlocks(cache, sequence, num_tokens);
   PathState& st = path_state();
   const int pages = static_cast<int>(sequence.block_table.size());
-  std::vector<int32_t> staging(kTableStride + 2 * num_tokens, 0);
+  std::vector<int32_t> staging(kTableStride + 2 * num_tokens + 3, 0);
   std::copy(sequence.block_table.begin(), sequence.block_table.end(), staging.begin());
   for (int t = 0; t < num_tokens; ++t) staging[kTableStride + t] = t;
+  staging[kTableStride + 2 * num_tokens + 1] = num_tokens;  // cu_q = {0, n}, pos0 = {0}
   check_cuda(cudaMemcpy(st.prefill, staging.data(), staging.size() * sizeof(int32_t),
                         cudaMemcpyHostToDevice));
   const int32_t* d_table = st.prefill;
   const int32_t* d_pos = st.prefill + kTableStride;
   const int32_t* d_rows = st.prefill + kTableStride + num_tokens;
+  const int32_t* d_cu_q = st.prefill + kTableStride + 2 * num_tokens;
+  const int32_t* d_pos0 = d_cu_q + 2;
   for (int layer = 0; layer < kLayers; ++layer) {
     const LayerWeights& lw = weights.layers[layer];
     rmsNormKernel<<<num_tokens, 1024>>>(hidden_states, buffers.rms_output, lw.input_norm);
@@ -141,11 +147,22 @@ int transformerForwardPaged(cublasHandle_t cublas_handle, __nv_bfloat16* hidden_
                               reinterpret_cast<tvp_bf16*>(buffers.q), kQHeads,
                               TVP_APPEND_ROPE_K | TVP_APPEND_ROPE_Q | TVP_APPEND_WRITEBACK_K,
                               st.error, nullptr));
-    computeAttentionScores(cublas_handle, buffers.q, buffers.k, buffers.attn_scores, num_tokens);
-    causalMask(buffers.attn_scores, num_tokens);
-    softmaxRows(buffers.attn_scores, kQHeads * num_tokens, num_tokens);
-    attentionScoresTimesV(cublas_handle, buffers.attn_scores, buffers.v, buffers.attn_output,
-                          num_tokens);
+    if (st.mode == TVP_MODE_FAST) {
+      // Causal attention over the pages just written (no score matrix).
+      check_tvp(tvp_paged_prefill_attention(
+          reinterpret_cast<const tvp_bf16*>(buffers.q),
+          reinterpret_cast<const tvp_bf16*>(cache.k_blocks),
+          reinterpret_cast<const tvp_bf16*>(cache.v_blocks), cache.num_blocks, kLayers, layer,
+          kKvHeads, kQHeads, d_table, pages, d_cu_q, d_pos0, 1, num_tokens, 0.125f,
+          reinterpret_cast<tvp_bf16*>(buffers.attn_output), st.error, nullptr));
+    } else {
+      // COMPAT keeps the reference's own prefill attention (token identity).
+      computeAttentionScores(cublas_handle, buffers.q, buffers.k, buffers.attn_scores, num_tokens);
+      causalMask(buffers.attn_scores, num_tokens);
+      softmaxRows(buffers.attn_scores, kQHeads * num_tokens, num_tokens);
+      attentionScoresTimesV(cublas_handle, buffers.attn_scores, buffers.v, buffers.attn_output,
+                            num_tokens);
+    }
     outputProjection(cublas_handle, buffers.attn_output, lw.w_o, buffers.o_output, num_tokens);
     residualAdd(hidden_states, buffers.o_output, num_tokens);
     rmsNormKernel<<<num_tokens, 1024>>>(hidden_states, buffers.rms_output, lw.post_attention_norm);

@@ -238,4 +238,37 @@ int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const 
   return map_cuda(launch_paged_decode(p, pool_rows, ctas, st));
 }
 
+int tvp_paged_prefill_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const tvp_bf16* v_pool,
+                                int num_pages, int num_layers, int layer, int kv_heads, int q_heads,
+                                const int32_t* d_block_tables, int table_stride,
+                                const int32_t* d_cu_q, const int32_t* d_q_pos0, int num_seqs,
+                                int max_q_len, float scale, tvp_bf16* out, int32_t* d_error,
+                                tvp_stream_t stream) {
+  if (!q || !k_pool || !v_pool || !out || !d_block_tables || !d_cu_q || !d_q_pos0 ||
+      num_pages <= 0 || num_layers <= 0 || layer < 0 || layer >= num_layers || table_stride <= 0 ||
+      num_seqs <= 0 || num_seqs > 65535 || max_q_len < 0 || !std::isfinite(scale))
+    return TVP_ERR_INVALID_ARGUMENT;
+  if (!decode_heads_supported(kv_heads) || q_heads != kv_heads * kGroup) return TVP_ERR_UNSUPPORTED;
+  if ((long long)num_layers * num_pages * kPage > 0x7fffffffLL) return TVP_ERR_UNSUPPORTED;
+  if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(q, 4) || !aligned(out, 4))
+    return TVP_ERR_INVALID_ARGUMENT;
+  if (max_q_len == 0) return TVP_OK;
+  PrefillParams p;
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  p.k_pool = reinterpret_cast<const __nv_bfloat16*>(k_pool);
+  p.v_pool = reinterpret_cast<const __nv_bfloat16*>(v_pool);
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.tables = d_block_tables;
+  p.cu_q = d_cu_q;
+  p.q_pos0 = d_q_pos0;
+  p.layer_row_base = (long long)layer * num_pages * kPage;
+  p.num_pages = num_pages;
+  p.table_stride = table_stride;
+  p.kv_heads = kv_heads;
+  p.scale = scale;
+  p.err = d_error;
+  return map_cuda(launch_paged_prefill(p, (long long)num_layers * num_pages * kPage, max_q_len,
+                                       num_seqs, static_cast<cudaStream_t>(stream)));
+}
+
 }  // extern "C"

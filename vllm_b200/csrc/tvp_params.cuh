@@ -72,6 +72,23 @@ struct CompatParams {
   int32_t* err;
 };
 
+// K3 (tvp_prefill.cu)
+struct PrefillParams {
+  const __nv_bfloat16* q;  // [num_tokens][q_heads * 64]
+  const __nv_bfloat16* k_pool;
+  const __nv_bfloat16* v_pool;
+  __nv_bfloat16* out;      // [num_tokens][q_heads * 64]
+  const int32_t* tables;   // [num_seqs][table_stride]
+  const int32_t* cu_q;     // [num_seqs + 1] query-token offsets
+  const int32_t* q_pos0;   // [num_seqs] position of each sequence's first query token
+  long long layer_row_base;
+  int num_pages;
+  int table_stride;
+  int kv_heads;
+  float scale;
+  int32_t* err;
+};
+
 // m[4], l[4], o[4][64] of one (split-K slot, KV head).
 constexpr int kPartialFloats = 2 * kGroup + kGroup * kHeadDim;
 
@@ -96,5 +113,7 @@ int prepare_decode(const void* q, const void* k_pool, const void* v_pool, int nu
 // 2-D tensor map over a pool of `rows` token rows of kv_heads x 64 channels.
 bool pool_tensor_map(const void* pool, long long rows, int kv_heads, CUtensorMap* out);
 cudaError_t launch_compat_decode(const CompatParams& p, int batch, cudaStream_t stream);
+cudaError_t launch_paged_prefill(const PrefillParams& p, long long pool_rows, int max_q_len,
+                                 int num_seqs, cudaStream_t stream);
 
 }  // namespace tvp

@@ -170,3 +170,36 @@ def paged_decode_attention(q, k_pool, v_pool, layer, block_tables, seq_lens, wor
                                         _ptr(out), _ptr(error), _stream(stream))
     N.check(rc, "tvp_paged_decode_attention")
     return out
+
+
+def paged_prefill_attention(q, k_pool, v_pool, layer, block_tables, cu_q, q_pos0, max_q_len,
+                            out=None, scale=0.125, error=None, stream=None):
+    """K3: causal prefill attention over the pages.  Sequence s (row s of
+    ``block_tables``) owns query rows [cu_q[s], cu_q[s + 1]) of ``q`` at
+    positions q_pos0[s], q_pos0[s] + 1, ...; each attends the keys 0..its
+    position already in the sequence's pages.  ``max_q_len`` bounds the
+    longest sequence's query count (host value, sizes the grid)."""
+    lib = N.load()
+    num_layers, num_pages, kv_heads = _pool_geometry(k_pool, v_pool)
+    dev = k_pool.device
+    _need(q, "q", torch.bfloat16, dev)
+    _need(block_tables, "block_tables", torch.int32, dev)
+    _need(cu_q, "cu_q", torch.int32, dev)
+    _need(q_pos0, "q_pos0", torch.int32, dev)
+    num_seqs = q_pos0.numel()
+    if cu_q.numel() != num_seqs + 1:
+        raise ValueError("cu_q must have num_seqs + 1 entries")
+    if q.dim() != 2 or q.shape[1] != kv_heads * N.GQA_GROUP * N.HEAD_DIM:
+        raise ValueError("q must be [num_tokens, 4*kv_heads*64]")
+    if block_tables.dim() != 2 or block_tables.shape[0] < num_seqs:
+        raise ValueError("block_tables must be [>=num_seqs, table_stride]")
+    if out is None:
+        out = torch.empty_like(q)
+    _need(out, "out", torch.bfloat16, dev)
+    rc = lib.tvp_paged_prefill_attention(_ptr(q), _ptr(k_pool), _ptr(v_pool), num_pages,
+                                         num_layers, layer, kv_heads, kv_heads * N.GQA_GROUP,
+                                         _ptr(block_tables), block_tables.shape[1], _ptr(cu_q),
+                                         _ptr(q_pos0), num_seqs, int(max_q_len), float(scale),
+                                         _ptr(out), _ptr(error), _stream(stream))
+    N.check(rc, "tvp_paged_prefill_attention")
+    return out
