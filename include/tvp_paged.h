@@ -53,6 +53,11 @@ typedef void* tvp_stream_t;  /* cudaStream_t */
 #define TVP_DEVERR_BAD_PLAN 8u     /* workspace planned for another batch/grid   */
 #define TVP_DEVERR_BAD_TOKEN 16u   /* append: token's sequence row or position invalid */
 #define TVP_DEVERR_SMEM_ALIGN 32u  /* decode: shared window not 1 KiB aligned; nothing ran */
+/* With TVP_DEVERR_TIMEOUT, which wait gave up: */
+#define TVP_DEVERR_WAIT_FULL 0x100u   /* a consumer waiting for a stage's copies   */
+#define TVP_DEVERR_WAIT_EMPTY 0x200u  /* the producer waiting for a free stage     */
+#define TVP_DEVERR_WAIT_DRAIN 0x400u  /* the producer's wait for its last copies   */
+#define TVP_DEVERR_WAIT_PEERS 0x800u  /* a gather waiting for the other ranks      */
 
 /* ---- fixed geometry ---------------------------------------------------- */
 #define TVP_HEAD_DIM 64

@@ -144,10 +144,11 @@ int e2e_generate(const int* prompts, int num_requests, int prompt_len, int max_n
 // the input token of step `step` for all rows at once through decodeBatchPaged
 // (whichever paged_transformer is linked), recording per row and step the
 // engine's argmax token and the FP32 logits row (logits_out: [steps][B][VOCAB],
-// may be NULL).  first_tokens[r] is the prefill's argmax.
+// may be NULL).  first_tokens[r] is the prefill's argmax and
+// prefill_logits_out[r] (may be NULL) its FP32 logits row.
 int e2e_teacher_forced(const int* prompts, int num_requests, int prompt_len, const int* forced,
                        int steps, int max_seq_len, int* first_tokens, int* step_tokens,
-                       float* logits_out) {
+                       float* logits_out, float* prefill_logits_out) {
   if (!g_model || num_requests < 1 || num_requests > MAX_BATCH_SIZE) return -1;
   PagedKVCache cache{};
   TransformerBuffers prefill{}, decode{};
@@ -171,6 +172,10 @@ int e2e_teacher_forced(const int* prompts, int num_requests, int prompt_len, con
       embeddingGatherKernel<<<prompt_len, 1024>>>(gpu_tokens, hidden, g_model->weights.embedding);
       first_tokens[r] = transformerForwardPaged(g_model->handle, hidden, g_model->weights, cache,
                                                 states[r], prefill, logits, prompt_len);
+      if (prefill_logits_out &&
+          cudaMemcpy(prefill_logits_out + (size_t)r * VOCAB_SIZE, logits,
+                     (size_t)VOCAB_SIZE * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess)
+        throw std::runtime_error("prefill logits copy");
     }
     std::vector<SequenceKVState*> rows;
     for (auto& s : states) rows.push_back(&s);

@@ -56,11 +56,18 @@ def compare() -> dict:
         results[name] = runner([*args, "--teacher-forced", str(tmp / "forced.json"),
                                 "--logits-out", str(path)])
         logs[name] = np.load(path, mmap_mode="r")
+        logs[name + "_prefill"] = np.load(str(path) + ".prefill.npy")
     ref = logs["ref"]
     summary = {"workload": "e2e: 4 requests x 128 prompt tokens, 127 teacher-forced decode steps",
                "reference_free_running_matches_teacher_forced":
                    bool(np.array_equal(np.array(results["ref"]["step_tokens"]), gen[:, 1:]))}
     rtok = np.array(results["ref"]["step_tokens"])        # [4][127]
+
+    def gap(lr, top_tok, other_tok):
+        b = bf16_round(lr)
+        top = b[top_tok]
+        return float((top - b[other_tok]) / bf16_ulp(np.array([top]))[0])
+
     for name in ("compat", "fast"):
         ours = np.array(results[name]["step_tokens"])
         agree = ours == rtok
@@ -75,8 +82,12 @@ def compare() -> dict:
                     b = bf16_round(lr[r])
                     top = b[rtok[r, step]]
                     gaps.append(float((top - b[ours[r, step]]) / bf16_ulp(np.array([top]))[0]))
+        rfirst, ofirst = results["ref"]["first_tokens"], results[name]["first_tokens"]
+        first_gaps = [gap(np.asarray(logs["ref_prefill"][r], np.float32), rfirst[r], ofirst[r])
+                      for r in range(len(rfirst)) if rfirst[r] != ofirst[r]]
         summary[name] = {
-            "first_tokens_match": results[name]["first_tokens"] == results["ref"]["first_tokens"],
+            "first_tokens_match": rfirst == ofirst,
+            "first_token_gap_bf16_ulps": sorted(first_gaps),
             "argmax_agreement": float(agree.mean()),
             "disagreements": int((~agree).sum()),
             "gap_at_disagreement_bf16_ulps": sorted(gaps),

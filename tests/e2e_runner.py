@@ -55,18 +55,22 @@ def main():
         forced = np.ascontiguousarray(json.load(open(args.teacher_forced)), dtype=np.int32)
         steps = forced.shape[1]
         lib.e2e_teacher_forced.argtypes = [i32p, ctypes.c_int, ctypes.c_int, i32p, ctypes.c_int,
-                                           ctypes.c_int, i32p, i32p, ctypes.c_void_p]
+                                           ctypes.c_int, i32p, i32p, ctypes.c_void_p,
+                                           ctypes.c_void_p]
         first = np.zeros(args.requests, np.int32)
         step_tokens = np.zeros((steps, args.requests), np.int32)
         logits = np.zeros((steps, args.requests, 128256), np.float32) if args.logits_out else None
+        first_logits = np.zeros((args.requests, 128256), np.float32) if args.logits_out else None
         rc = lib.e2e_teacher_forced(p.ctypes.data_as(i32p), args.requests, args.prompt,
                                     forced.ctypes.data_as(i32p), steps, args.prompt + steps + 1,
                                     first.ctypes.data_as(i32p), step_tokens.ctypes.data_as(i32p),
-                                    logits.ctypes.data if logits is not None else None)
+                                    logits.ctypes.data if logits is not None else None,
+                                    first_logits.ctypes.data if first_logits is not None else None)
         if rc != 0:
             raise SystemExit(f"teacher-forced decode failed ({rc})")
         if logits is not None:
             np.save(args.logits_out, logits)
+            np.save(str(args.logits_out) + ".prefill.npy", first_logits)
         json.dump({"engine": args.engine, "mode": args.mode, "first_tokens": first.tolist(),
                    "step_tokens": step_tokens.T.tolist()}, sys.stdout)
         print()

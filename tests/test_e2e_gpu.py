@@ -34,7 +34,12 @@ def test_reference_engine_is_deterministic_under_teacher_forcing(summary):
 @pytest.mark.parametrize("mode", ["compat", "fast"])
 def test_dropped_in_path_matches_reference_up_to_bf16_ties(summary, mode):
     s = summary[mode]
-    assert s["first_tokens_match"]          # prefill: RoPE + pages are bit-exact
+    if mode == "compat":
+        assert s["first_tokens_match"]      # prefill: RoPE + pages bit-exact, reference attention
+    else:
+        # FAST prefill uses the paged prefill kernel: a first token may differ
+        # only at a near-tie of the reference's own prefill logits
+        assert max(s["first_token_gap_bf16_ulps"], default=0.0) <= 8.0
     assert s["argmax_agreement"] >= (0.90 if mode == "compat" else 0.85)
     # every disagreement is a near-tie in the reference's own BF16-rounded logits;
     # FAST keeps FP32 scores where the reference rounds them to BF16 and

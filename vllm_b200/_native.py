@@ -28,6 +28,10 @@ TVP_DEVERR_TIMEOUT = 4
 TVP_DEVERR_BAD_PLAN = 8
 TVP_DEVERR_BAD_TOKEN = 16
 TVP_DEVERR_SMEM_ALIGN = 32
+TVP_DEVERR_WAIT_FULL = 0x100
+TVP_DEVERR_WAIT_EMPTY = 0x200
+TVP_DEVERR_WAIT_DRAIN = 0x400
+TVP_DEVERR_WAIT_PEERS = 0x800
 
 TVP_MODE_FAST = 0
 TVP_MODE_COMPAT = 1

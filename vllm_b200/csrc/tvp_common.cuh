@@ -60,6 +60,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 
+// Nanoseconds since `start` by %globaltimer, as a signed difference: a timer
+// that steps back (it is re-synchronised) reads as no time passed instead of
+// wrapping to a huge unsigned interval and ending a wait at once.
+__device__ __forceinline__ long long elapsed_ns(unsigned long long start) {
+  return (long long)(global_timer_ns() - start);
+}
+
 // Bounded wait: true when the phase with `parity` completed, false when the
 // wait ran past kWaitLimitNs (the caller records the timeout and stops).
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
@@ -68,7 +75,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
   while (true) {
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - start > kWaitLimitNs) return false;
+    if (elapsed_ns(start) > (long long)kWaitLimitNs) return false;
   }
 }
 

@@ -192,14 +192,13 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
         }
         next_phys = __ldg(p.tables + (size_t)s * p.table_stride + (pg + 1 - seq_first));
       }
-      if (*abort_flag) break;  // a consumer gave up: issue nothing more
       if (kk >= STAGES) {
         int timed_out = 0;
         if (lane == 0) timed_out = !mbar_wait_bounded(smem_addr(&empty_bar[stage]), empty_parity);
         if (__shfl_sync(0xffffffffu, timed_out, 0)) {
           if (lane == 0) {
             *abort_flag = 1;
-            record_error(p.err, TVP_DEVERR_TIMEOUT);
+            record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_EMPTY);
           }
           break;
         }
@@ -284,7 +283,7 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
       ready = __all_sync(0xffffffffu, ready);
       if (!ready && lane == 0 && !*abort_flag) {
         *abort_flag = 1;
-        record_error(p.err, TVP_DEVERR_TIMEOUT);
+        record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
       }
       // Pull this head's K and V fragments of the page into registers, then
       // release the stage at once: the producer refills it while the math runs,

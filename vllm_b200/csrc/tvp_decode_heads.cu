@@ -180,14 +180,13 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
       const bool mine = lane < PS && i < n;
       i += PS;
       if (lane < PS && i < n) walk();
-      if (*abort_flag) break;  // a consumer gave up: issue nothing more
       if (kk >= STAGES) {
         int timed_out = 0;
         if (lane == 0) timed_out = !mbar_wait_bounded(smem_addr(&empty_bar[stage]), empty_parity);
         if (__shfl_sync(0xffffffffu, timed_out, 0)) {
           if (lane == 0) {
             *abort_flag = 1;
-            record_error(p.err, TVP_DEVERR_TIMEOUT);
+            record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_EMPTY);
           }
           break;
         }
@@ -275,7 +274,7 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
       ready = __all_sync(0xffffffffu, ready);
       if (!ready && lane == 0 && !*abort_flag) {
         *abort_flag = 1;
-        record_error(p.err, TVP_DEVERR_TIMEOUT);
+        record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
       }
       const bool have = ready && ((stage_mask[stage] >> o) & 1);
       bool zeroed = false;
@@ -337,8 +336,8 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
           int32_t v;
           asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
           if ((int32_t)((uint32_t)v - (uint32_t)p.flag_target) >= 0) break;
-          if (global_timer_ns() - start > kWaitLimitNs) {
-            record_error(p.err, TVP_DEVERR_TIMEOUT);
+          if (elapsed_ns(start) > (long long)kWaitLimitNs) {
+            record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_PEERS);
             break;
           }
           __nanosleep(128);

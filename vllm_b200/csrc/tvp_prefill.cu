@@ -91,14 +91,13 @@ __global__ void __launch_bounds__(kPrefillThreads)
     for (int j = 0; j < n_pages; ++j) {
       const int phys = next_phys;
       if (j + 1 < n_pages) next_phys = __ldg(p.tables + (size_t)s * p.table_stride + j + 1);
-      if (*abort_flag) break;
       if (j >= kPrefillStages) {
         int timed_out = 0;
         if (lane == 0) timed_out = !mbar_wait_bounded(smem_addr(&empty_bar[stage]), empty_parity);
         if (__shfl_sync(0xffffffffu, timed_out, 0)) {
           if (lane == 0) {
             *abort_flag = 1;
-            record_error(p.err, TVP_DEVERR_TIMEOUT);
+            record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_EMPTY);
           }
           break;
         }
@@ -170,7 +169,7 @@ __global__ void __launch_bounds__(kPrefillThreads)
     ready = __all_sync(0xffffffffu, ready);
     if (!ready && lane == 0 && !*abort_flag) {
       *abort_flag = 1;
-      record_error(p.err, TVP_DEVERR_TIMEOUT);
+      record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
     }
     const bool have = ready && stage_ok[stage];
     const uint32_t kt = smem_base + stage * kPrefillStage, vt = kt + kTileBytes;

@@ -66,18 +66,19 @@ struct TileLane {
 };
 
 // Abort-safe end of a producer: no copy into this CTA's shared memory may be in
-// flight when the CTA exits.  After a wait gave up, consumers stop releasing
-// stages and the producer stops issuing, so every slot has at most one use
-// outstanding: the last min(STAGES, issued) stages issued.  Lane 0 waits, each
-// wait bounded, for their full barriers (on the normal path these have
-// completed or are about to).
+// flight when the CTA exits.  A consumer whose wait gave up does not release
+// its stage, so the producer's next wait for that slot runs out too and it
+// stops issuing (no per-page check of the abort flag on the producer's
+// critical path); every slot then has at most one use outstanding: the last
+// min(STAGES, issued) stages issued.  Lane 0 waits, each wait bounded, for
+// their full barriers (on the normal path these have completed or are about to).
 template <int STAGES>
 __device__ __forceinline__ void drain_issued_stages(const uint64_t* full_bar, int issued, int lane,
                                                     int32_t* err) {
   if (lane == 0) {
     for (int k = issued > STAGES ? issued - STAGES : 0; k < issued; ++k)
       if (!mbar_wait_bounded(smem_addr(&full_bar[k % STAGES]), (uint32_t)((k / STAGES) & 1))) {
-        record_error(err, TVP_DEVERR_TIMEOUT);
+        record_error(err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_DRAIN);
         break;
       }
   }
