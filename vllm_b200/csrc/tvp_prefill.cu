@@ -19,7 +19,7 @@
 // fragments), S = Q K^T (16 queries x 16 keys) and O += P V (16 x 64) with
 // mma.m16n8k16 (BF16 in, FP32 accumulate), P going from the S accumulators to
 // the A operand without a shuffle, and keeps an online base-2 softmax per row
-// over BF16-rounded scores.
+// over BF16-rounded scores, with a lazy running max.
 #include "tvp_tile.cuh"
 
 namespace tvp {
@@ -57,10 +57,13 @@ __global__ void __launch_bounds__(kPrefillThreads)
 
   const int s = blockIdx.y, g = blockIdx.z;
   const int q_begin = __ldg(p.cu_q + s), q_end = __ldg(p.cu_q + s + 1);
-  const int tok0 = q_begin + blockIdx.x * kQTile;
+  // Tiles run last-first: under causality the last tiles stream the most pages,
+  // so starting them first shortens the launch's tail.
+  const int tile = gridDim.x - 1 - blockIdx.x;
+  const int tok0 = q_begin + tile * kQTile;
   if (tok0 >= q_end) return;  // this sequence has fewer tiles
   const int count = min(kQTile, q_end - tok0);
-  const int pos0 = __ldg(p.q_pos0 + s) + blockIdx.x * kQTile;  // position of the tile's row 0
+  const int pos0 = __ldg(p.q_pos0 + s) + tile * kQTile;  // position of the tile's row 0
   const int pos_last = pos0 + count - 1;
   if (pos0 < 0 || pos_last / kPage >= p.table_stride) {
     if (threadIdx.x == 0) record_error(p.err, TVP_DEVERR_BAD_TOKEN);
@@ -222,18 +225,25 @@ __global__ void __launch_bounds__(kPrefillThreads)
         }
         float mx_a = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
         float mx_b = fmaxf(fmaxf(x[4], x[5]), fmaxf(x[6], x[7]));
+        // Lazy running max (as in the decode kernels): the row maxima are
+        // reduced and O rescaled only when a score beats a row's max by more
+        // than kLazyMargin, so probabilities stay below 2^kLazyMargin.
+        float al_a = 1.f, al_b = 1.f;
+        if (__any_sync(0xffffffffu, mx_a > m[mt][0] + kLazyMargin || mx_b > m[mt][1] + kLazyMargin)) {
 #pragma unroll
-        for (int sh = 1; sh < 4; sh <<= 1) {
-          mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, sh));
-          mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, sh));
+          for (int sh = 1; sh < 4; sh <<= 1) {
+            mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, sh));
+            mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, sh));
+          }
+          const float mn_a = fmaxf(m[mt][0], mx_a), mn_b = fmaxf(m[mt][1], mx_b);
+          al_a = m[mt][0] == -INFINITY ? 0.f : fast_exp2(m[mt][0] - mn_a);
+          al_b = m[mt][1] == -INFINITY ? 0.f : fast_exp2(m[mt][1] - mn_b);
+          m[mt][0] = mn_a;
+          m[mt][1] = mn_b;
         }
-        const float mn_a = fmaxf(m[mt][0], mx_a), mn_b = fmaxf(m[mt][1], mx_b);
         // rows that have seen no key yet keep a zero base (no inf - inf)
-        const float base_a = mn_a == -INFINITY ? 0.f : mn_a;
-        const float base_b = mn_b == -INFINITY ? 0.f : mn_b;
-        const float al_a = fast_exp2(m[mt][0] - base_a), al_b = fast_exp2(m[mt][1] - base_b);
-        m[mt][0] = mn_a;
-        m[mt][1] = mn_b;
+        const float base_a = m[mt][0] == -INFINITY ? 0.f : m[mt][0];
+        const float base_b = m[mt][1] == -INFINITY ? 0.f : m[mt][1];
         // P as the A operand of O += P V (keys 0-7 then 8-15 of the page)
         uint32_t pa[4];
         pa[0] = pack_bf16x2(fast_exp2(x[0] - base_a), fast_exp2(x[1] - base_a));
@@ -244,9 +254,11 @@ __global__ void __launch_bounds__(kPrefillThreads)
                                       bf16lo_to_f32(pa[2]) + bf16hi_to_f32(pa[2]));
         l[mt][1] = l[mt][1] * al_b + (bf16lo_to_f32(pa[1]) + bf16hi_to_f32(pa[1]) +
                                       bf16lo_to_f32(pa[3]) + bf16hi_to_f32(pa[3]));
+        if (__any_sync(0xffffffffu, al_a != 1.f || al_b != 1.f)) {
 #pragma unroll
-        for (int d = 0; d < 8; ++d) {
-          o[mt][d][0] *= al_a; o[mt][d][1] *= al_a; o[mt][d][2] *= al_b; o[mt][d][3] *= al_b;
+          for (int d = 0; d < 8; ++d) {
+            o[mt][d][0] *= al_a; o[mt][d][1] *= al_a; o[mt][d][2] *= al_b; o[mt][d][3] *= al_b;
+          }
         }
 #pragma unroll
         for (int dp = 0; dp < 4; ++dp) {
