@@ -134,3 +134,43 @@ def test_two_rank_gloo_head_sharded_gather():
     full = oracle.decode_attention(case.q, case.k_pool, case.v_pool, 0, case.tables, case.lens)
     assert np.array_equal(results[0], full)
     assert np.array_equal(results[1], full)
+
+
+def _agree_worker(rank, world, port, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    from vllm_b200 import _native as N
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        # the agreement step alone: no gather group was created on any rank
+        dec = sharding.HeadShardedDecode.__new__(sharding.HeadShardedDecode)
+        dec.dist, dec.group, dec.world, dec.rank, dec._h = dist, None, world, rank, None
+        dec._agree(N.TVP_OK, "all ok", connected=False)
+        try:
+            dec._agree(N.TVP_ERR_RUNTIME if rank == 1 else N.TVP_OK, "setup", connected=False)
+            results[rank] = "returned"
+        except RuntimeError as e:
+            results[rank] = str(e)
+        dist.barrier()  # both ranks are still in step after the failure
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gloo_gather_setup_failure_is_raised_on_every_rank():
+    """A setup step that fails on one rank raises on all ranks, none of them
+    left waiting in a collective."""
+    from vllm_b200 import _native as N
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    procs = [ctx.Process(target=_agree_worker, args=(r, world, port, results))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    want = f"setup failed on ranks {{1: {N.TVP_ERR_RUNTIME}}}"
+    assert results[0] == want and results[1] == want

@@ -129,16 +129,21 @@ class HeadShardedDecode:
             return
         lib = N.load()
         with torch.cuda.device(self.device):
+            # Every fallible local step is followed by an agreement across the
+            # group, so that a failure on one rank makes every rank stop at the
+            # same point instead of leaving the others waiting in a collective.
             h = ctypes.c_void_p()
-            N.check(lib.tvp_head_gather_create(self.world, self.rank, self.kv_heads, max_batch,
-                                               ctypes.byref(h)), "tvp_head_gather_create")
-            self._h = h
             mine = (ctypes.c_char * N.TVP_IPC_HANDLE_BYTES)()
-            N.check(lib.tvp_head_gather_export(h, mine), "tvp_head_gather_export")
+            rc = lib.tvp_head_gather_create(self.world, self.rank, self.kv_heads, max_batch,
+                                            ctypes.byref(h))
+            if rc == N.TVP_OK:
+                self._h = h
+                rc = lib.tvp_head_gather_export(h, mine)
+            self._agree(rc, "tvp_head_gather_create / export", connected=False)
             handles = [None] * self.world
             dist.all_gather_object(handles, bytes(mine), group=group)
-            blob = b"".join(handles)
-            N.check(lib.tvp_head_gather_connect(h, blob), "tvp_head_gather_connect")
+            rc = lib.tvp_head_gather_connect(h, b"".join(handles))
+            self._agree(rc, "tvp_head_gather_connect", connected=True)
             self.rows = []
             for b in (0, 1):
                 ptr = ctypes.c_void_p()
@@ -148,6 +153,26 @@ class HeadShardedDecode:
                     _CudaArray(ptr.value, (max_batch, 2048), "<u2"), device=self.device
                 ).view(torch.bfloat16))
         self.buffer = 0
+
+    def _agree(self, rc: int, what: str, connected: bool):
+        """All ranks learn every rank's status; if any failed, every rank
+        tears down its group (IPC-safe order) and raises."""
+        from . import _native as N
+        statuses = [None] * self.world
+        self.dist.all_gather_object(statuses, int(rc), group=self.group)
+        if all(st == N.TVP_OK for st in statuses):
+            return
+        if self._h is not None:
+            lib = N.load()
+            if connected:
+                lib.tvp_head_gather_disconnect(self._h)
+            self.dist.barrier(group=self.group)  # no peer maps our buffer any more
+            lib.tvp_head_gather_destroy(self._h)
+            self._h = None
+        else:
+            self.dist.barrier(group=self.group)
+        bad = {r: st for r, st in enumerate(statuses) if st != N.TVP_OK}
+        raise RuntimeError(f"{what} failed on ranks {bad}")
 
     def plan(self, seq_lens, table_stride: int, error=None, stream=None):
         from . import ops
