@@ -79,6 +79,33 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
   }
 }
 
+// Bounded wait until round `round` of a pipeline stage has been issued.  The
+// producer writes the stage's tag, ((round + 1) << 1) | ok, before it issues
+// that round's copies.  A consumer that does not take every round of a stage
+// (another consumer group takes the round before) calls this before its
+// parity wait: a parity wait only tells the current phase from the one before
+// it, so on a barrier one round behind (the other group's copy still in
+// flight) it would see the round before that as complete and pass at once.
+// Once the tag shows `round`, the barrier is at that round or has just
+// completed it (the round after needs this consumer's release), so the parity
+// wait is exact.  Returns the tag, or 0 when `abort_flag` is set or the wait
+// ran past kWaitLimitNs.
+__device__ __forceinline__ int stage_tag_wait(const volatile int* tag, int round,
+                                              const volatile int* abort_flag) {
+  const int want = round + 1;
+  int t = *tag;
+  if ((t >> 1) >= want) return t;
+  const unsigned long long start = global_timer_ns();
+  while (true) {
+    for (int i = 0; i < 64; ++i) {
+      __nanosleep(32);
+      t = *tag;
+      if ((t >> 1) >= want) return t;
+    }
+    if (*abort_flag || elapsed_ns(start) > (long long)kWaitLimitNs) return 0;
+  }
+}
+
 // ---- bulk copy global -> shared (TMA, no tensor map, this CTA only) -------
 __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uint32_t bytes,
                                               uint32_t bar) {

@@ -127,8 +127,10 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
   }
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
   uint64_t* empty_bar = full_bar + STAGES;
-  int* stage_ok = reinterpret_cast<int*>(empty_bar + STAGES);
-  volatile int* abort_flag = stage_ok + STAGES;
+  // Per stage: ((round + 1) << 1) | (page id in range), written by the
+  // producer before it issues the round (see stage_tag_wait).
+  volatile int* stage_tag = reinterpret_cast<int*>(empty_bar + STAGES);
+  volatile int* abort_flag = stage_tag + STAGES;
   // Set-merge scratch (only with two consumer sets).
   float* merge = reinterpret_cast<float*>(smem + STAGES * kStageBytes + 2 * STAGES * 8 +
                                           (STAGES + 4) * 4);
@@ -140,6 +142,7 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_addr(&full_bar[s]), 1);
       mbar_init(smem_addr(&empty_bar[s]), kMaxKvHeads);
+      stage_tag[s] = 0;
     }
     *abort_flag = 0;
     mbar_fence_init();
@@ -180,7 +183,7 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
     int next_phys = p_begin < p_end
                         ? __ldg(p.tables + (size_t)s * p.table_stride + (p_begin - seq_first))
                         : 0;
-    int stage = 0, issued = 0;
+    int stage = 0, round = 0, issued = 0;
     uint32_t empty_parity = 1;  // parity of the previous round of each slot
     for (int pg = p_begin, kk = 0; pg < p_end; ++pg, ++kk) {
       const int phys = next_phys;
@@ -206,7 +209,7 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
       const bool ok = phys >= 0 && phys < p.num_pages;
       const uint32_t full = smem_addr(&full_bar[stage]);
       if (lane == 0) {
-        stage_ok[stage] = ok ? 1 : 0;
+        stage_tag[stage] = ((round + 1) << 1) | (ok ? 1 : 0);
         if (!ok) record_error(p.err, TVP_DEVERR_BAD_PAGE);
         mbar_arrive_expect_tx(full, ok ? (uint32_t)kStageBytes : 0u);
       }
@@ -222,6 +225,7 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
       issued = kk + 1;
       if (++stage == STAGES) {
         stage = 0;
+        ++round;
         empty_parity ^= 1u;
       }
     }
@@ -251,10 +255,11 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
   int s = s0;
   int pg = p_begin;
   int kbase = 0;
-  // Slot and phase of this set's current page, advanced incrementally
-  // (page kk of the CTA sits in slot kk % STAGES, phase (kk / STAGES) & 1).
-  int c_kk = 0, c_stage = 0;
-  uint32_t c_parity = 0;
+  // Slot and round of this set's current page, advanced incrementally (page
+  // kk of the CTA sits in slot kk % STAGES, round kk / STAGES).  With two sets
+  // and an odd number of stages, consecutive rounds of a slot go to different
+  // sets, so a set's wait is gated on the slot's tag (stage_tag_wait).
+  int c_kk = 0, c_stage = 0, c_round = 0;
   while (pg < p_end) {
     while (pg >= __ldg(p.cu + s + 1)) ++s;
     const int first = __ldg(p.cu + s), end = __ldg(p.cu + s + 1);
@@ -273,13 +278,17 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
       for (const int kk = kbase + i; c_kk < kk; ++c_kk) {
         if (++c_stage == STAGES) {
           c_stage = 0;
-          c_parity ^= 1u;
+          ++c_round;
         }
       }
       const int stage = c_stage;
-      const uint32_t parity = c_parity;
       bool ready = false;
-      if (!*abort_flag) ready = mbar_wait_bounded(smem_addr(&full_bar[stage]), parity);
+      int tag = 0;
+      if (!*abort_flag) {
+        tag = SETS > 1 ? stage_tag_wait(stage_tag + stage, c_round, abort_flag) : 1;
+        ready = tag != 0 &&
+                mbar_wait_bounded(smem_addr(&full_bar[stage]), (uint32_t)(c_round & 1));
+      }
       ready = __all_sync(0xffffffffu, ready);
       if (!ready && lane == 0 && !*abort_flag) {
         *abort_flag = 1;
@@ -288,7 +297,8 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
       // Pull this head's K and V fragments of the page into registers, then
       // release the stage at once: the producer refills it while the math runs,
       // so almost every stage stays in flight (a fetch takes ~4 us at full load).
-      const bool have = ready && stage_ok[stage];
+      if (SETS == 1 && ready) tag = stage_tag[stage];  // read after the copies landed
+      const bool have = ready && (tag & 1);
       bool zeroed = false;
       int valid = kPage;
       uint32_t kf[4][4], vf[4][4];
