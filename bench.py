@@ -138,55 +138,103 @@ def run_reference_arm(args, rank, world):
 
 # ---------------------------------------------------------------- clocks ---
 class ClockSampler:
+    """SM clock, maximum SM clock and clock-event reasons of one GPU, sampled
+    while the timed region runs: every 5 ms through NVML (the library
+    nvidia-smi reads these fields from), else by `nvidia-smi -lms 100`.  The
+    GPU is found by the CUDA device's UUID, so CUDA_VISIBLE_DEVICES cannot
+    point the sampler at another GPU."""
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+    def __init__(self, device):
+        import torch
+        self.device = torch.device(device)
+        self.rows = []  # (sm MHz, max sm MHz, [active reasons])
+        self.source = None
+        self._stop = threading.Event()
+        self.thread = self.proc = None
+
+    def _nvml(self):
+        import pynvml as nv
+        import torch
+        nv.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.device).uuid)
+        h = nv.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        bits = [(name, getattr(nv, attr)) for name, attr in self.REASONS]
+
+        def sample():
+            r = reasons(h)
+            self.rows.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)), max_mhz,
+                              [name for name, b in bits if r & b]))
+        return sample
 
     def start(self):
         try:
+            sample = self._nvml()
+            sample()  # fails here, not in the thread, when NVML cannot read the GPU
+            self.rows.clear()
+
+            def loop():
+                while True:
+                    sample()
+                    if self._stop.wait(0.005):
+                        return
+            self.source = "nvml, 5 ms"
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.rows.clear()
+        try:
+            import torch
+            idx = torch.cuda._get_nvml_device_index(self.device)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.gpu), "-lms", "100"], stdout=subprocess.PIPE,
+                 "-i", str(idx), "-lms", "100"], stdout=subprocess.PIPE,
                 stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.source = "nvidia-smi, 100 ms"
+            self.thread = threading.Thread(target=self._read_smi, daemon=True)
             self.thread.start()
         except Exception:
             self.proc = None
 
-    def _read(self):
+    def _read_smi(self):
+        names = [n for n, _ in self.REASONS]
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
-    def stop(self):
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        rows = []
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
+            parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
             try:
-                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+                self.rows.append((float(parts[1]), float(parts[2]),
+                                  [n for n, f in zip(names, parts[5:9]) if f.lower() == "active"]))
             except ValueError:
                 continue
+
+    def stop(self):
+        self._stop.set()
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        rows = list(self.rows)
         if not rows:
             return None
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags)
-                          if f.lower() == "active"})
         return {"sm_mhz": statistics.median(r[0] for r in rows),
-                "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
-                "samples": len(rows)}
+                "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": sorted({n for r in rows for n in r[2]}),
+                "samples": len(rows), "source": self.source}
 
 
 # ------------------------------------------------------------- our arm ---
@@ -254,7 +302,7 @@ def run_ours(args, rank, world, local_rank):
     ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(layers)]
           for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = ClockSampler(local_rank)
+    clocks = ClockSampler(dev)
     barrier()
     torch.cuda.synchronize(dev)
     clocks.start()
