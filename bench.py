@@ -452,7 +452,8 @@ def bench_e2e_llama():
     out = {"workload": "e2e: Llama-3.2-1B geometry, random N(0,0.02) weights, B=4, 128+128 tokens"}
     for name, args in (("reference", ["--engine", "ref"]),
                        ("ours_compat", ["--engine", "tvp", "--mode", "compat"]),
-                       ("ours_fast", ["--engine", "tvp", "--mode", "fast"])):
+                       ("ours_fast", ["--engine", "tvp", "--mode", "fast"]),
+                       ("ours_batched", ["--engine", "tvp", "--mode", "batched"])):
         r = subprocess.run([sys.executable, str(ROOT / "tests" / "e2e_runner.py"), *args,
                             "--runs", "2"], capture_output=True, text=True, timeout=900)
         if r.returncode != 0:
@@ -461,10 +462,11 @@ def bench_e2e_llama():
         d = json.loads(r.stdout.strip().splitlines()[-1])
         out[name] = {"tok_s": round(d["tokens_generated"] / min(d["seconds"]), 1),
                      "seconds": [round(x, 3) for x in d["seconds"]]}
-    try:
-        out["speedup_compat"] = round(out["ours_compat"]["tok_s"] / out["reference"]["tok_s"], 2)
-    except (KeyError, TypeError, ZeroDivisionError):
-        pass
+    for name in ("compat", "fast", "batched"):
+        try:
+            out[f"speedup_{name}"] = round(out[f"ours_{name}"]["tok_s"] / out["reference"]["tok_s"], 2)
+        except (KeyError, TypeError, ZeroDivisionError):
+            pass
     return out
 
 
@@ -503,9 +505,8 @@ def bench_long_context(dev, iters=20):
             "inputs": "larger than L2 (1.07 GB per launch)"}
 
 
-# Pools are freed back to torch's cache between workloads, never to the driver
-# (no torch.cuda.empty_cache()): the 8-head decode kernel has an open fault seen
-# only when it runs on fresh pools after earlier pools were returned to the driver.
+# Pools are freed back to torch's cache between workloads, not to the driver
+# (no torch.cuda.empty_cache()): later workloads reuse memory already mapped.
 
 
 def long_context_pools(dev, kv_heads, seed=99):
@@ -763,7 +764,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--only", choices=["long_context", "long_context_heads", "decode_small",
-                                       "prefill"],
+                                       "prefill", "e2e"],
                     help="run one single-GPU sub-measurement alone and print its JSON (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -779,7 +780,8 @@ def main():
         dev = torch.device("cuda", 0)
         torch.cuda.set_device(dev)
         fn = {"long_context": bench_long_context, "long_context_heads": bench_long_context_heads,
-              "decode_small": bench_decode_small, "prefill": bench_prefill}[args.only]
+              "decode_small": bench_decode_small, "prefill": bench_prefill,
+              "e2e": lambda _dev: bench_e2e_llama()}[args.only]
         print(json.dumps({args.only: fn(dev)}), flush=True)
         return
     import torch

@@ -176,6 +176,23 @@ int tvp_paged_prefill_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const
                                 tvp_stream_t stream);
 
 /*
+ * Greedy token selection for `rows` logit rows in one launch: replaces the
+ * per-row argmaxLogits of the reference (src/model/argmax.cu:83-105; two
+ * launches and a blocking copy per row) with the same selection rule
+ * (src/model/argmax.cu:16-45): logits rounded to BF16, NaNs skipped, the
+ * largest value wins with ties to the lowest index, and a row whose logit 0
+ * is NaN selects 0.  d_logits: FP32 [rows][row_stride] (row_stride >= vocab);
+ * d_tokens: int32 [rows], written on `stream`.  The workspace
+ * (tvp_greedy_argmax_workspace_bytes(rows), 8-byte aligned) must be zeroed
+ * once before its first use; every call leaves it zeroed.  Calls that share a
+ * workspace must not overlap on the GPU.
+ */
+size_t tvp_greedy_argmax_workspace_bytes(int rows);
+int tvp_greedy_argmax(const float* d_logits, int rows, int vocab, long long row_stride,
+                      int32_t* d_tokens, void* d_workspace, size_t workspace_bytes,
+                      tvp_stream_t stream);
+
+/*
  * K2 without any allocation.  This entry point has no counterpart in the
  * reference.  It is for callers that cannot call cudaMalloc: code whose
  * device memory is owned by a host framework's pool, plug-ins running under a

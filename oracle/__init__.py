@@ -200,6 +200,25 @@ def prefill_attention(q, k_pool, v_pool, layer, tables, cu_q, q_pos0, scale=0.12
     return decode_attention(q, k_pool, v_pool, layer, tab, lens, scale=scale, threads=threads)
 
 
+def greedy_argmax(logits) -> np.ndarray:
+    """Greedy token per row of FP32 logits [rows][vocab], as the reference's
+    CPU scan restated in tests/argmax_test.cu:41-45 and implemented on the GPU
+    by src/model/argmax.cu:16-45: each logit rounded to BF16; the running
+    maximum starts at logit 0 and moves only on a strictly larger value, so
+    ties keep the lowest index, NaNs never win, -0 equals +0, and a NaN logit
+    0 keeps token 0."""
+    x = np.ascontiguousarray(np.atleast_2d(logits), dtype=np.float32)
+    b = bf16_to_f32(f32_to_bf16(x))
+    out = np.zeros(x.shape[0], np.int32)
+    for r in range(x.shape[0]):
+        if np.isnan(b[r, 0]):
+            continue
+        # NaNs -> -inf cannot win: logit 0 is a number at or above -inf and
+        # comes first, so np.argmax's first-occurrence rule returns it then
+        out[r] = int(np.argmax(np.where(np.isnan(b[r]), -np.inf, b[r])))
+    return out
+
+
 def max_threads() -> int:
     return int(load().orc_max_threads())
 

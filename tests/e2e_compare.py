@@ -51,7 +51,8 @@ def compare() -> dict:
     logs = {}
     results = {}
     for name, args in {"ref": ["--engine", "ref"], "compat": ["--engine", "tvp", "--mode", "compat"],
-                       "fast": ["--engine", "tvp", "--mode", "fast"]}.items():
+                       "fast": ["--engine", "tvp", "--mode", "fast"],
+                       "batched": ["--engine", "tvp", "--mode", "batched"]}.items():
         path = tmp / f"{name}.npy"
         results[name] = runner([*args, "--teacher-forced", str(tmp / "forced.json"),
                                 "--logits-out", str(path)])
@@ -68,7 +69,7 @@ def compare() -> dict:
         top = b[top_tok]
         return float((top - b[other_tok]) / bf16_ulp(np.array([top]))[0])
 
-    for name in ("compat", "fast"):
+    for name in ("compat", "fast", "batched"):
         ours = np.array(results[name]["step_tokens"])
         agree = ours == rtok
         gaps = []

@@ -74,6 +74,9 @@ _SIGNATURES = {
                                             c_int, c_int, c_void_p, c_int, c_void_p, c_void_p,
                                             c_int, c_int, ctypes.c_float, c_void_p, c_void_p,
                                             c_void_p]),
+    "tvp_greedy_argmax_workspace_bytes": (c_size_t, [c_int]),
+    "tvp_greedy_argmax": (c_int, [c_void_p, c_int, c_int, ctypes.c_longlong, c_void_p, c_void_p,
+                                  c_size_t, c_void_p]),
     "tvp_head_gather_create": (c_int, [c_int, c_int, c_int, c_int, POINTER(c_void_p)]),
     "tvp_head_gather_export": (c_int, [c_void_p, c_void_p]),
     "tvp_head_gather_connect": (c_int, [c_void_p, c_void_p]),

@@ -17,12 +17,23 @@
 // The layer loop around them calls the reference's functions in the
 // reference's order, because its outputs (tokens) are what must not change.
 //
-// Decode numerics: TVP_DECODE_MODE=fast selects TVP_MODE_FAST, which also
-// swaps the prefill attention (paged_transformer.cu:37-40) for
-// tvp_paged_prefill_attention over the pages; the default is TVP_MODE_COMPAT
-// (the reference's BF16 score/probability rounding, and its own prefill
-// attention), which is what greedy-token identity with the unmodified engine
-// needs.
+// Modes (TVP_DECODE_MODE):
+//   compat (default)  TVP_MODE_COMPAT decode (the reference's BF16 score and
+//                     probability rounding) and the reference's own prefill
+//                     attention: greedy-token identity with the unmodified
+//                     engine.
+//   fast              TVP_MODE_FAST decode, and tvp_paged_prefill_attention
+//                     over the pages in place of the prefill attention
+//                     (paged_transformer.cu:37-40).
+//   batched           fast, plus the decode step's projections and LM head as
+//                     one GEMM over the batch (n = B) instead of B one-row
+//                     GEMMs (paged_transformer.cu:71-78,96-113,119-121), and
+//                     the B greedy tokens from one tvp_greedy_argmax launch
+//                     and one device-to-host copy instead of B argmaxLogits
+//                     calls (argmax.cu:83-105).  The batched GEMMs sum in
+//                     another order than the one-row ones, so this mode has
+//                     its own parity policy (near-ties only, as fast).
+#include <cublas_v2.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -45,6 +56,14 @@
 #include "softmax.cuh"
 #include "tvp_paged.h"
 
+// The reference's residual and SwiGLU kernels (src/model/resConnection.cu:6-10,
+// src/model/SiLU.cu:5-10), defined in its sources.  Their host wrappers
+// launch on the legacy default stream, which a stream capture cannot record;
+// the batched decode step launches the same kernels, with the wrappers'
+// launch shape, on its own stream.
+__global__ void residualKernel(__nv_bfloat16* input, __nv_bfloat16* input_embeds);
+__global__ void siluKernel(__nv_bfloat16* a, __nv_bfloat16* b);
+
 namespace {
 
 constexpr int kLayers = 16;
@@ -54,6 +73,7 @@ constexpr int kHidden = 2048;
 constexpr int kMaxContext = 1024;                     // the engine's context cap
 constexpr int kTableStride = kMaxContext / BLOCK_SIZE;  // 64, as MAX_BLOCKS_PER_SEQUENCE
 constexpr int kMaxBatch = 4;                          // MAX_BATCH_SIZE of the scheduler
+constexpr size_t kCublasWorkspace = 32u << 20;        // cuBLAS workspace of captured steps
 
 void check_cuda(cudaError_t status) {
   if (status != cudaSuccess) throw std::runtime_error(cudaGetErrorString(status));
@@ -69,10 +89,24 @@ void check_tvp(int rc) {
 struct PathState {
   int32_t* prefill = nullptr;  // [table (64) | positions (1024) | rows (1024) | cu_q (2) | pos0 (1)]
   int32_t* decode = nullptr;   // [tables (4 x 64) | positions (4) | lengths (4)]
-  int32_t* error = nullptr;
+  int32_t* error = nullptr;    // [error word | tokens (kMaxBatch)]: one read per step
   void* workspace = nullptr;
   size_t workspace_bytes = 0;
+  void* argmax_workspace = nullptr;
+  size_t argmax_workspace_bytes = 0;
   int mode = TVP_MODE_COMPAT;
+  bool batched = false;
+  // Batched mode: the decode step runs on `stream` (a blocking stream, so it
+  // is ordered after the engine's legacy-stream work) as a CUDA graph per
+  // batch size, captured on the second step that uses the same buffers.
+  cudaStream_t stream = nullptr;
+  void* cublas_workspace = nullptr;
+  int32_t* h_out = nullptr;  // pinned copy of [error word | tokens]
+  struct StepGraph {
+    std::vector<const void*> key;  // every buffer the captured launches point at
+    bool warm = false;             // one eager step ran with `key`
+    cudaGraphExec_t exec = nullptr;
+  } graphs[kMaxBatch + 1];
 };
 
 PathState& path_state() {
@@ -89,13 +123,23 @@ PathState& path_state() {
                           (kTableStride + 2 * kMaxContext + 4) * sizeof(int32_t)));
     check_cuda(cudaMalloc(reinterpret_cast<void**>(&st.decode),
                           (kMaxBatch * kTableStride + 2 * kMaxBatch) * sizeof(int32_t)));
-    check_cuda(cudaMalloc(reinterpret_cast<void**>(&st.error), sizeof(int32_t)));
-    check_cuda(cudaMemset(st.error, 0, sizeof(int32_t)));
+    check_cuda(cudaMalloc(reinterpret_cast<void**>(&st.error), (1 + kMaxBatch) * sizeof(int32_t)));
+    check_cuda(cudaMemset(st.error, 0, (1 + kMaxBatch) * sizeof(int32_t)));
+    st.argmax_workspace_bytes = tvp_greedy_argmax_workspace_bytes(kMaxBatch);
+    check_cuda(cudaMalloc(&st.argmax_workspace, st.argmax_workspace_bytes));
+    check_cuda(cudaMemset(st.argmax_workspace, 0, st.argmax_workspace_bytes));
     st.workspace_bytes = tvp_decode_workspace_bytes(kMaxBatch, kKvHeads, 0);
     if (st.workspace_bytes == 0) throw std::runtime_error("decode workspace size query failed");
     check_cuda(cudaMalloc(&st.workspace, st.workspace_bytes));
-    const char* mode = std::getenv("TVP_DECODE_MODE");
-    st.mode = (mode && std::string(mode) == "fast") ? TVP_MODE_FAST : TVP_MODE_COMPAT;
+    const std::string mode = std::getenv("TVP_DECODE_MODE") ? std::getenv("TVP_DECODE_MODE") : "";
+    st.batched = mode == "batched";
+    st.mode = (mode == "fast" || st.batched) ? TVP_MODE_FAST : TVP_MODE_COMPAT;
+    if (st.batched) {
+      check_cuda(cudaStreamCreate(&st.stream));
+      check_cuda(cudaMalloc(&st.cublas_workspace, kCublasWorkspace));
+      check_cuda(cudaMallocHost(reinterpret_cast<void**>(&st.h_out),
+                                (1 + kMaxBatch) * sizeof(int32_t)));
+    }
     ready[dev] = true;
   }
   return st;
@@ -223,55 +267,142 @@ std::vector<int> decodeBatchPaged(cublasHandle_t cublas_handle, __nv_bfloat16* h
   const int32_t* d_tables = st.decode;
   const int32_t* d_pos = st.decode + kMaxBatch * kTableStride;
   const int32_t* d_len = d_pos + kMaxBatch;
-  check_tvp(tvp_decode_plan(d_len, batch, kTableStride, kKvHeads, 0, st.workspace,
-                            st.workspace_bytes, st.error, nullptr));
-  for (int layer = 0; layer < kLayers; ++layer) {
-    const LayerWeights& lw = weights.layers[layer];
-    rmsNormKernel<<<batch, 1024>>>(hidden_states, buffers.rms_output, lw.input_norm);
-    // Row-stable one-row GEMMs, exactly as the reference (its BF16 rounding contract).
+  // A projection of the step: one GEMM over the batch (batched mode) or the
+  // reference's row-stable one-row GEMMs (its BF16 rounding contract).
+  auto project = [&](auto projection, auto* in, int in_dim, auto* w, __nv_bfloat16* out,
+                     int out_dim) {
+    if (st.batched) {
+      projection(cublas_handle, in, w, out, batch);
+      return;
+    }
     for (int row = 0; row < batch; ++row)
-      qProjection(cublas_handle, buffers.rms_output + row * kHidden, lw.w_q, buffers.q + row * kHidden, 1);
-    for (int row = 0; row < batch; ++row)
-      kProjection(cublas_handle, buffers.rms_output + row * kHidden, lw.w_k, buffers.k + row * 512, 1);
-    for (int row = 0; row < batch; ++row)
-      vProjection(cublas_handle, buffers.rms_output + row * kHidden, lw.w_v, buffers.v + row * 512, 1);
-    check_tvp(tvp_rope_append(reinterpret_cast<tvp_bf16*>(cache.k_blocks),
-                              reinterpret_cast<tvp_bf16*>(cache.v_blocks), cache.num_blocks,
-                              kLayers, layer, kKvHeads, d_tables, kTableStride, batch, nullptr,
-                              d_pos, batch, reinterpret_cast<tvp_bf16*>(buffers.k),
-                              reinterpret_cast<const tvp_bf16*>(buffers.v),
-                              reinterpret_cast<tvp_bf16*>(buffers.q), kQHeads,
-                              TVP_APPEND_ROPE_K | TVP_APPEND_ROPE_Q | TVP_APPEND_WRITEBACK_K,
-                              st.error, nullptr));
-    check_tvp(tvp_paged_decode_attention(
-        reinterpret_cast<const tvp_bf16*>(buffers.q), reinterpret_cast<const tvp_bf16*>(cache.k_blocks),
-        reinterpret_cast<const tvp_bf16*>(cache.v_blocks), cache.num_blocks, kLayers, layer, kKvHeads,
-        kQHeads, d_tables, kTableStride, d_len, batch, 0.125f, st.mode, 0, st.workspace,
-        st.workspace_bytes, reinterpret_cast<tvp_bf16*>(buffers.attn_output), st.error, nullptr));
-    for (int row = 0; row < batch; ++row)
-      outputProjection(cublas_handle, buffers.attn_output + row * kHidden, lw.w_o,
-                       buffers.o_output + row * kHidden, 1);
-    residualAdd(hidden_states, buffers.o_output, batch);
-    rmsNormKernel<<<batch, 1024>>>(hidden_states, buffers.rms_output, lw.post_attention_norm);
-    for (int row = 0; row < batch; ++row)
-      gateProjection(cublas_handle, buffers.rms_output + row * kHidden, lw.w_gate, buffers.gate + row * 8192, 1);
-    for (int row = 0; row < batch; ++row)
-      upProjection(cublas_handle, buffers.rms_output + row * kHidden, lw.w_up, buffers.up + row * 8192, 1);
-    silu(buffers.gate, buffers.up, batch);
-    for (int row = 0; row < batch; ++row)
-      downProjection(cublas_handle, buffers.gate + row * 8192, lw.w_down, buffers.down + row * kHidden, 1);
-    residualAdd(hidden_states, buffers.down, batch);
-  }
-  rmsNormKernel<<<batch, 1024>>>(hidden_states, buffers.rms_output, weights.final_norm);
-  for (int row = 0; row < batch; ++row)
-    lmHeadProjection(cublas_handle, buffers.rms_output + row * kHidden, weights.embedding,
-                     logits + static_cast<size_t>(row) * VOCAB_SIZE);
-  check_cuda(cudaGetLastError());
+      projection(cublas_handle, in + row * in_dim, w, out + row * out_dim, 1);
+  };
+  // The step's device work on `stream`; nullptr is the legacy default stream,
+  // where the reference's own op wrappers are called.
+  auto enqueue = [&](cudaStream_t stream) {
+    auto residual = [&](__nv_bfloat16* add) {
+      if (stream) residualKernel<<<batch, 1024, 0, stream>>>(hidden_states, add);
+      else residualAdd(hidden_states, add, batch);
+    };
+    check_tvp(tvp_decode_plan(d_len, batch, kTableStride, kKvHeads, 0, st.workspace,
+                              st.workspace_bytes, st.error, stream));
+    for (int layer = 0; layer < kLayers; ++layer) {
+      const LayerWeights& lw = weights.layers[layer];
+      rmsNormKernel<<<batch, 1024, 0, stream>>>(hidden_states, buffers.rms_output, lw.input_norm);
+      project(qProjection, buffers.rms_output, kHidden, lw.w_q, buffers.q, kHidden);
+      project(kProjection, buffers.rms_output, kHidden, lw.w_k, buffers.k, 512);
+      project(vProjection, buffers.rms_output, kHidden, lw.w_v, buffers.v, 512);
+      check_tvp(tvp_rope_append(reinterpret_cast<tvp_bf16*>(cache.k_blocks),
+                                reinterpret_cast<tvp_bf16*>(cache.v_blocks), cache.num_blocks,
+                                kLayers, layer, kKvHeads, d_tables, kTableStride, batch, nullptr,
+                                d_pos, batch, reinterpret_cast<tvp_bf16*>(buffers.k),
+                                reinterpret_cast<const tvp_bf16*>(buffers.v),
+                                reinterpret_cast<tvp_bf16*>(buffers.q), kQHeads,
+                                TVP_APPEND_ROPE_K | TVP_APPEND_ROPE_Q | TVP_APPEND_WRITEBACK_K,
+                                st.error, stream));
+      check_tvp(tvp_paged_decode_attention(
+          reinterpret_cast<const tvp_bf16*>(buffers.q),
+          reinterpret_cast<const tvp_bf16*>(cache.k_blocks),
+          reinterpret_cast<const tvp_bf16*>(cache.v_blocks), cache.num_blocks, kLayers, layer,
+          kKvHeads, kQHeads, d_tables, kTableStride, d_len, batch, 0.125f, st.mode, 0,
+          st.workspace, st.workspace_bytes, reinterpret_cast<tvp_bf16*>(buffers.attn_output),
+          st.error, stream));
+      project(outputProjection, buffers.attn_output, kHidden, lw.w_o, buffers.o_output, kHidden);
+      residual(buffers.o_output);
+      rmsNormKernel<<<batch, 1024, 0, stream>>>(hidden_states, buffers.rms_output,
+                                                lw.post_attention_norm);
+      project(gateProjection, buffers.rms_output, kHidden, lw.w_gate, buffers.gate, 8192);
+      project(upProjection, buffers.rms_output, kHidden, lw.w_up, buffers.up, 8192);
+      if (stream) siluKernel<<<batch, 1024, 0, stream>>>(buffers.gate, buffers.up);
+      else silu(buffers.gate, buffers.up, batch);
+      project(downProjection, buffers.gate, 8192, lw.w_down, buffers.down, kHidden);
+      residual(buffers.down);
+    }
+    rmsNormKernel<<<batch, 1024, 0, stream>>>(hidden_states, buffers.rms_output, weights.final_norm);
+    if (!st.batched) return;
+    // The LM head of lm_head.cu:8-36 over all rows: logits[row] = E h_row.
+    const float alpha = 1.0f, beta = 0.0f;
+    if (cublasGemmEx(cublas_handle, CUBLAS_OP_T, CUBLAS_OP_N, VOCAB_SIZE, batch, kHidden, &alpha,
+                     weights.embedding, CUDA_R_16BF, kHidden, buffers.rms_output, CUDA_R_16BF,
+                     kHidden, &beta, logits, CUDA_R_32F, VOCAB_SIZE, CUBLAS_COMPUTE_32F,
+                     CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
+      throw std::runtime_error("LM head projection failed");
+    check_tvp(tvp_greedy_argmax(logits, batch, VOCAB_SIZE, VOCAB_SIZE, st.error + 1,
+                                st.argmax_workspace, st.argmax_workspace_bytes, stream));
+  };
+
   std::vector<int> tokens;
   tokens.reserve(batch);
-  for (int row = 0; row < batch; ++row)
-    tokens.push_back(argmaxLogits(logits + static_cast<size_t>(row) * VOCAB_SIZE));
-  raise_device_errors(st);
+  if (!st.batched) {
+    enqueue(nullptr);
+    for (int row = 0; row < batch; ++row)
+      lmHeadProjection(cublas_handle, buffers.rms_output + row * kHidden, weights.embedding,
+                       logits + static_cast<size_t>(row) * VOCAB_SIZE);
+    check_cuda(cudaGetLastError());
+    for (int row = 0; row < batch; ++row)
+      tokens.push_back(argmaxLogits(logits + static_cast<size_t>(row) * VOCAB_SIZE));
+    raise_device_errors(st);
+  } else {
+    // cuBLAS works on the step's stream while this call runs; the caller's
+    // stream (and with it cuBLAS's default workspace) is restored on return.
+    cudaStream_t caller_stream = nullptr;
+    if (cublasGetStream(cublas_handle, &caller_stream) != CUBLAS_STATUS_SUCCESS ||
+        cublasSetStream(cublas_handle, st.stream) != CUBLAS_STATUS_SUCCESS)
+      throw std::runtime_error("cuBLAS stream setup failed");
+    struct RestoreStream {
+      cublasHandle_t handle;
+      cudaStream_t stream;
+      ~RestoreStream() { cublasSetStream(handle, stream); }
+    } restore{cublas_handle, caller_stream};
+    PathState::StepGraph& g = st.graphs[batch];
+    const std::vector<const void*> key = {
+        hidden_states, buffers.rms_output, buffers.q, buffers.k, buffers.v, buffers.attn_output,
+        buffers.o_output, buffers.gate, buffers.up, buffers.down, logits, cache.k_blocks,
+        cache.v_blocks, reinterpret_cast<const void*>(static_cast<intptr_t>(cache.num_blocks)),
+        weights.embedding, weights.final_norm, weights.layers[0].w_q, cublas_handle};
+    if (g.exec && g.key == key) {
+      check_cuda(cudaGraphLaunch(g.exec, st.stream));
+    } else if (g.warm && g.key == key) {
+      // Second step on these buffers: record it once, then replay it.
+      if (cublasSetWorkspace(cublas_handle, st.cublas_workspace, kCublasWorkspace) !=
+          CUBLAS_STATUS_SUCCESS)
+        throw std::runtime_error("cuBLAS workspace setup failed");
+      check_cuda(cudaStreamBeginCapture(st.stream, cudaStreamCaptureModeThreadLocal));
+      cudaGraph_t graph = nullptr;
+      try {
+        enqueue(st.stream);
+      } catch (...) {
+        cudaStreamEndCapture(st.stream, &graph);
+        if (graph) cudaGraphDestroy(graph);
+        throw;
+      }
+      check_cuda(cudaStreamEndCapture(st.stream, &graph));
+      cudaGraphExec_t exec = nullptr;
+      const cudaError_t made = cudaGraphInstantiate(&exec, graph, 0);
+      cudaGraphDestroy(graph);
+      check_cuda(made);
+      if (g.exec) cudaGraphExecDestroy(g.exec);
+      g.exec = exec;
+      check_cuda(cudaGraphLaunch(g.exec, st.stream));
+    } else {
+      // First step on these buffers: eager, which also loads every kernel.
+      if (g.exec) cudaGraphExecDestroy(g.exec);
+      g.exec = nullptr;
+      enqueue(st.stream);
+      g.key = key;
+      g.warm = true;
+    }
+    check_cuda(cudaMemcpyAsync(st.h_out, st.error, (1 + batch) * sizeof(int32_t),
+                               cudaMemcpyDeviceToHost, st.stream));
+    check_cuda(cudaStreamSynchronize(st.stream));
+    if (st.h_out[0]) {
+      check_cuda(cudaMemset(st.error, 0, sizeof(int32_t)));
+      throw std::runtime_error("paged-KV kernels reported device error bits " +
+                               std::to_string(st.h_out[0]));
+    }
+    tokens.assign(st.h_out + 1, st.h_out + 1 + batch);
+  }
   for (auto* sequence : sequences) sequence->current_seq_len += 1;
   return tokens;
 }

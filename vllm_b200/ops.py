@@ -203,3 +203,30 @@ def paged_prefill_attention(q, k_pool, v_pool, layer, block_tables, cu_q, q_pos0
                                          _ptr(out), _ptr(error), _stream(stream))
     N.check(rc, "tvp_paged_prefill_attention")
     return out
+
+
+def greedy_argmax(logits, out=None, workspace=None, stream=None):
+    """Greedy token per row of FP32 logits [rows, vocab] (rows may be strided:
+    logits.stride(1) must be 1), with the reference engine's selection rule
+    (BF16-rounded logits, NaNs skipped, ties to the lowest index, a NaN logit 0
+    selects 0), one launch for all rows.  ``workspace``: a zeroed uint8 tensor
+    of tvp_greedy_argmax_workspace_bytes(rows) bytes, reusable across calls
+    (each call leaves it zeroed); allocated per call when omitted."""
+    lib = N.load()
+    if not (logits.is_cuda and logits.dtype == torch.float32):
+        raise ValueError("logits must be a CUDA float32 tensor")
+    if logits.dim() != 2 or logits.stride(1) != 1 or logits.stride(0) < logits.shape[1]:
+        raise ValueError("logits must be [rows, vocab] with unit stride along vocab")
+    rows, vocab = logits.shape
+    dev = logits.device
+    nbytes = lib.tvp_greedy_argmax_workspace_bytes(rows)
+    if workspace is None:
+        workspace = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int32, device=dev)
+    _need(out, "out", torch.int32, dev)
+    rc = lib.tvp_greedy_argmax(_ptr(logits), rows, vocab, logits.stride(0), _ptr(out),
+                               _ptr(workspace), workspace.numel() * workspace.element_size(),
+                               _stream(stream))
+    N.check(rc, "tvp_greedy_argmax")
+    return out
