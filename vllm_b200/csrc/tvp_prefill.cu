@@ -1,4 +1,5 @@
-// K3 — paged causal prefill attention, reading K and V from the pages.
+// K3 — paged causal prefill attention, reading K and V from the pages, on the
+// 5th-generation tensor cores (tcgen05, accumulators in Tensor Memory).
 //
 // Replaces the reference's prefill attention (src/model/paged_transformer.cu:37-40):
 // computeAttentionScores (32 cuBLAS GEMMs over the contiguous K,
@@ -10,93 +11,126 @@
 // context: chunked prefill), with no length cap and no score matrix in HBM.
 //
 // Queries are varlen: sequence s owns query tokens [cu_q[s], cu_q[s + 1]) at
-// positions q_pos0[s], q_pos0[s] + 1, ...  A CTA takes one (16-query tile,
-// sequence, KV head): a producer warp streams the sequence's pages 0 .. the
-// tile's last position (one 2 KiB K box and one V box of this KV head per
-// page, the decode kernels' tensor maps and 128-byte swizzle), and 4 consumer
-// warps, one per query head of the GQA group, share every page.  Per page a
-// warp forms, for each of its 16-query m-tiles (sharing the page's K and V
-// fragments), S = Q K^T (16 queries x 16 keys) and O += P V (16 x 64) with
-// mma.m16n8k16 (BF16 in, FP32 accumulate), P going from the S accumulators to
-// the A operand without a shuffle, and keeps an online base-2 softmax per row
-// over BF16-rounded scores, with a lazy running max.
+// positions q_pos0[s], q_pos0[s] + 1, ...  A CTA takes one (32-token tile,
+// sequence, KV head); its 128 MMA rows are the tile's (token, query head)
+// pairs of the GQA group, row 4 t + h, so every K/V byte serves 4 heads.
+// Keys go in chunks of 4 pages (64 keys):
+//   * warp 0 streams each chunk's K and V boxes (the decode kernels' tensor
+//     maps, 128-byte swizzle) into a 4-stage ring with TMA; page slots past
+//     the tile's last position are filled with zeros by an out-of-range box;
+//   * warp 1 allocates Tensor Memory and one of its threads issues the MMAs:
+//     S = Q K^T (M 128, N 64, K 64: Q and K both K-major in shared memory,
+//     S in TMEM) and O += P V (M 128, N 64, K 64: P K-major, V MN-major as it
+//     lands from TMA, O in TMEM), each followed by tcgen05.commit to an
+//     mbarrier;
+//   * warps 2-5 (one thread per row, TMEM lane quarter = warp % 4) load Q into
+//     shared memory, then per chunk read their S row from TMEM, mask it
+//     causally, round scores to BF16 where the reference rounds them, keep an
+//     online base-2 softmax with a lazy running max (O in TMEM rescaled only
+//     when the max grows by more than kLazyMargin), and write P as BF16 into
+//     the 128-byte-swizzled A tile of the P V MMA.
+// Order per chunk c: S(c) -> softmax(c) -> [P V(c), S(c + 1)] -> ...; with 96
+// KiB of shared memory and 128 TMEM columns per CTA, two CTAs share an SM, so
+// one CTA's softmax overlaps the other's MMAs.
 #include "tvp_tile.cuh"
+#include "tvp_umma.cuh"
 
 namespace tvp {
 
 namespace {
 
-constexpr int kPrefillStages = 6;
-constexpr int kPrefillStage = 2 * kTileBytes;  // K tile, then V tile (4 KiB)
-// 16-row m-tiles per warp.  Two (each page's K/V fragments serving 32 queries)
-// measured slower on B200 than one: 188 vs 150 us for 4 x 1024 prompts, with
-// half the CTAs and two instead of three CTAs per SM.
-constexpr int kPrefillMTiles = 1;
-constexpr int kQTile = 16 * kPrefillMTiles;    // query tokens per CTA
-constexpr int kPrefillThreads = (kGroup + 1) * 32;
+constexpr int kTcTokens = 32;                       // query tokens per CTA
+constexpr int kTcRows = kTcTokens * kGroup;         // 128 MMA rows
+constexpr int kTcChunkPages = 4;                    // pages per key chunk
+constexpr int kTcChunk = kTcChunkPages * kPage;     // 64 keys
+constexpr int kTcStages = 4;
+constexpr int kTcKvBytes = kTcChunkPages * kTileBytes;  // 8 KiB of K (or of V) per stage
+constexpr int kTcStageBytes = 2 * kTcKvBytes;           // K, then V
+constexpr int kTcQBytes = kTcRows * 128;                // 64 BF16 per row
+constexpr int kTcPBytes = kTcRows * 128;                // 64 keys per row
+constexpr int kTcThreads = 6 * 32;
+constexpr uint32_t kTcTmemCols = 128;                   // S: columns 0-63, O: 64-127
+constexpr int kOffQ = 0;
+constexpr int kOffP = kOffQ + kTcQBytes;
+constexpr int kOffStages = kOffP + kTcPBytes;
+constexpr int kOffBars = kOffStages + kTcStages * kTcStageBytes;
+// q_full, s_full, p_full, o_full, drain, kv_full[stages], kv_empty[stages]
+constexpr int kBarKvFull = 5;
+constexpr int kBarKvEmpty = kBarKvFull + kTcStages;
+constexpr int kNumBars = kBarKvEmpty + kTcStages;
 
 constexpr size_t prefill_smem_bytes() {
-  return 1024 /* alignment slack */ + (size_t)kPrefillStages * kPrefillStage +
-         2 * kPrefillStages * 8 + (kPrefillStages + 4) * 4;
+  return 1024 /* alignment slack */ + kOffBars + kNumBars * 8 + 16;
 }
 
-// MT: 16-row m-tiles per warp; every K/V fragment loaded from a page serves MT.
-template <int MT>
-__global__ void __launch_bounds__(kPrefillThreads)
+__global__ void __launch_bounds__(kTcThreads, 2)
     paged_prefill_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap k_map,
                          const __grid_constant__ CUtensorMap v_map) {
   extern __shared__ unsigned char smem_raw[];
   // 128-byte swizzled tiles need 1 KiB alignment: round the window up.
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t smem_base = smem_addr(smem);
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + kPrefillStages * kPrefillStage);
-  uint64_t* empty_bar = full_bar + kPrefillStages;
-  int* stage_ok = reinterpret_cast<int*>(empty_bar + kPrefillStages);
-  volatile int* abort_flag = stage_ok + kPrefillStages;
+  const uint32_t sbase = smem_addr(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
+  auto bar = [&](int i) { return smem_addr(&bars[i]); };
+  const uint32_t q_full = bar(0), s_full = bar(1), p_full = bar(2), o_full = bar(3),
+                 drain = bar(4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int s = blockIdx.y, g = blockIdx.z;
   const int q_begin = __ldg(p.cu_q + s), q_end = __ldg(p.cu_q + s + 1);
   // Tiles run last-first: under causality the last tiles stream the most pages,
   // so starting them first shortens the launch's tail.
   const int tile = gridDim.x - 1 - blockIdx.x;
-  const int tok0 = q_begin + tile * kQTile;
+  const int tok0 = q_begin + tile * kTcTokens;
   if (tok0 >= q_end) return;  // this sequence has fewer tiles
-  const int count = min(kQTile, q_end - tok0);
-  const int pos0 = __ldg(p.q_pos0 + s) + tile * kQTile;  // position of the tile's row 0
+  const int count = min(kTcTokens, q_end - tok0);
+  const int pos0 = __ldg(p.q_pos0 + s) + tile * kTcTokens;  // position of the tile's token 0
   const int pos_last = pos0 + count - 1;
   if (pos0 < 0 || pos_last / kPage >= p.table_stride) {
     if (threadIdx.x == 0) record_error(p.err, TVP_DEVERR_BAD_TOKEN);
     return;
   }
-  const int n_pages = pos_last / kPage + 1;
+  const int last_page = pos_last / kPage;
+  const int n_chunks = pos_last / kTcChunk + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kPrefillStages; ++i) {
-      mbar_init(smem_addr(&full_bar[i]), 1);
-      mbar_init(smem_addr(&empty_bar[i]), kGroup);
+    mbar_init(q_full, 4);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(o_full, 1);
+    mbar_init(drain, 1);
+    for (int i = 0; i < kTcStages; ++i) {
+      mbar_init(bar(kBarKvFull + i), 1);
+      mbar_init(bar(kBarKvEmpty + i), 1);
     }
     *abort_flag = 0;
     mbar_fence_init();
   }
+  if (warp == 1) {
+    tmem_alloc(smem_addr(tmem_slot), kTcTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
   __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_s = *tmem_slot, tmem_o = tmem_s + 64;
 
-  if (warp == kGroup) {
+  if (warp == 0) {
     // ------------------------------ producer ------------------------------
     if (lane == 0) {
       prefetch_tensor_map(&k_map);
       prefetch_tensor_map(&v_map);
     }
-    int stage = 0, issued = 0;
-    uint32_t empty_parity = 1;
-    int next_phys = __ldg(p.tables + (size_t)s * p.table_stride);
-    for (int j = 0; j < n_pages; ++j) {
-      const int phys = next_phys;
-      if (j + 1 < n_pages) next_phys = __ldg(p.tables + (size_t)s * p.table_stride + j + 1);
-      if (j >= kPrefillStages) {
+    int issued = 0;
+    for (int c = 0; c < n_chunks; ++c) {
+      const int st = c % kTcStages;
+      if (c >= kTcStages) {
         int timed_out = 0;
-        if (lane == 0) timed_out = !mbar_wait_bounded(smem_addr(&empty_bar[stage]), empty_parity);
+        if (lane == 0)
+          timed_out = !mbar_wait_bounded(bar(kBarKvEmpty + st), ((c / kTcStages) - 1) & 1);
         if (__shfl_sync(0xffffffffu, timed_out, 0)) {
           if (lane == 0) {
             *abort_flag = 1;
@@ -105,198 +139,220 @@ __global__ void __launch_bounds__(kPrefillThreads)
           break;
         }
       }
-      const bool ok = phys >= 0 && phys < p.num_pages;
-      const uint32_t full = smem_addr(&full_bar[stage]);
-      if (lane == 0) {
-        stage_ok[stage] = ok ? 1 : 0;
-        if (!ok) record_error(p.err, TVP_DEVERR_BAD_PAGE);
-        mbar_arrive_expect_tx(full, ok ? (uint32_t)kPrefillStage : 0u);
-      }
+      // lanes 0-3: K box of page slot `lane`, lanes 4-7: V box of slot lane - 4
+      const int pg = c * kTcChunkPages + (lane & 3);
+      const bool real = lane < 8 && pg <= last_page;
+      const int phys = real ? __ldg(p.tables + (size_t)s * p.table_stride + pg) : -1;
+      const bool ok = real && phys >= 0 && phys < p.num_pages;
+      if (real && !ok && lane < 4) record_error(p.err, TVP_DEVERR_BAD_PAGE);
+      if (lane == 0) mbar_arrive_expect_tx(bar(kBarKvFull + st), kTcStageBytes);
       __syncwarp();
-      if (ok && lane < 2) {
-        const int y = (int)(p.layer_row_base + (long long)phys * kPage);
-        tma_load_2d(smem_base + stage * kPrefillStage + lane * kTileBytes,
-                    lane == 0 ? &k_map : &v_map, g * kHeadDim, y, full);
+      if (lane < 8) {
+        const uint32_t dst = sbase + kOffStages + st * kTcStageBytes +
+                             (lane < 4 ? 0 : kTcKvBytes) + (lane & 3) * kTileBytes;
+        // A box wholly outside the pool (rows -16 .. -1) arrives as zeros.
+        const int y = ok ? (int)(p.layer_row_base + (long long)phys * kPage) : -kPage;
+        tma_load_2d(dst, lane < 4 ? &k_map : &v_map, g * kHeadDim, y, bar(kBarKvFull + st));
       }
-      issued = j + 1;
-      if (++stage == kPrefillStages) {
-        stage = 0;
-        empty_parity ^= 1u;
+      issued = c + 1;
+    }
+    drain_issued_stages<kTcStages>(bars + kBarKvFull, issued, lane, p.err);
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ----------------------------
+    if (lane == 0) {
+      constexpr uint32_t kIdS = umma_idesc_bf16_f32(kTcRows, kTcChunk, false, false);
+      constexpr uint32_t kIdO = umma_idesc_bf16_f32(kTcRows, kHeadDim, false, true);
+      const uint32_t q_tile = sbase + kOffQ, p_tile = sbase + kOffP;
+      auto stage_k = [&](int c) { return sbase + kOffStages + (c % kTcStages) * kTcStageBytes; };
+      // O += P V(c): K = the chunk's 64 keys, 16 (one page of V) per MMA.
+      auto issue_pv = [&](int c) {
+        const uint32_t v_tile = stage_k(c) + kTcKvBytes;
+#pragma unroll
+        for (int kk = 0; kk < kTcChunkPages; ++kk)
+          umma_bf16(tmem_o, umma_desc_sw128(p_tile + 32 * kk, 16, 1024),
+                    umma_desc_sw128(v_tile + kk * kTileBytes, 0, 1024), kIdO, (c > 0 || kk > 0));
+      };
+      bool ok = mbar_wait_bounded(q_full, 0);
+      if (!ok) record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
+      for (int c = 0; ok && c < n_chunks; ++c) {
+        if (!mbar_wait_bounded(bar(kBarKvFull + c % kTcStages), (c / kTcStages) & 1)) {
+          record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
+          ok = false;
+          break;
+        }
+        if (c > 0) {
+          if (!mbar_wait_bounded(p_full, (c - 1) & 1)) {
+            record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          issue_pv(c - 1);
+          umma_commit(bar(kBarKvEmpty + (c - 1) % kTcStages));
+        }
+        tc_fence_after_sync();
+        // S = Q K(c)^T: K = the 64 channels, 16 per MMA.
+        const uint32_t k_tile = stage_k(c);
+#pragma unroll
+        for (int k = 0; k < kHeadDim / 16; ++k)
+          umma_bf16(tmem_s, umma_desc_sw128(q_tile + 32 * k, 16, 1024),
+                    umma_desc_sw128(k_tile + 32 * k, 16, 1024), kIdS, k > 0);
+        umma_commit(s_full);
       }
+      if (ok) {
+        if (mbar_wait_bounded(p_full, (n_chunks - 1) & 1)) {
+          tc_fence_after_sync();
+          issue_pv(n_chunks - 1);
+          umma_commit(o_full);
+        } else {
+          record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
+          ok = false;
+        }
+      }
+      if (!ok) *abort_flag = 1;
+      // Every MMA issued has completed before Tensor Memory is released.
+      umma_commit(drain);
+      if (!mbar_wait_bounded(drain, 0))
+        record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_DRAIN);
     }
-    drain_issued_stages<kPrefillStages>(full_bar, issued, lane, p.err);
-    return;
-  }
-
-  // ------------------------------ consumers -------------------------------
-  const int hq = g * kGroup + warp;  // query head of this warp
-  const int qdim = p.kv_heads * kGroup * kHeadDim;
-  const int r = lane >> 2, c = lane & 3;  // accumulator rows r, r + 8; column pair 2c
-  const int mrow = lane & 7, mat = lane >> 3;
-
-  // Per m-tile mt (query rows 16 mt .. 16 mt + 15 of the CTA's tile):
-  // Q A-operand fragments, O accumulators, running max and normaliser of rows
-  // 16 mt + r (index 0) and 16 mt + r + 8 (index 1).
-  uint32_t qa[MT][4][4];
-  float o[MT][8][4];
-  float m[MT][2], l[MT][2];
+    __syncwarp();
+  } else {
+    // ------------------------------ softmax -------------------------------
+    const int quarter = warp & 3;  // TMEM lanes 32 quarter .. + 31
+    const int row = quarter * 32 + lane;
+    const int t = row >> 2, h = row & 3;
+    const bool valid = t < count;
+    const int qpos = pos0 + t;
+    const int qdim = p.kv_heads * kGroup * kHeadDim;
+    const int hq = g * kGroup + h;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    {
+      // Q row (token t, head hq) into the swizzled A tile of S = Q K^T.
+      const uint4* src =
+          reinterpret_cast<const uint4*>(p.q + (size_t)(tok0 + t) * qdim + hq * kHeadDim);
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt) {
-    const int ra = 16 * mt + r, rb = ra + 8;
-    const __nv_bfloat16* qr = p.q + (size_t)(tok0 + ra) * qdim + hq * kHeadDim + 2 * c;
-    const __nv_bfloat16* qr8 = qr + (size_t)8 * qdim;
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-      qa[mt][ks][0] = ra < count ? __ldg(reinterpret_cast<const uint32_t*>(qr + ks * 16)) : 0u;
-      qa[mt][ks][1] = rb < count ? __ldg(reinterpret_cast<const uint32_t*>(qr8 + ks * 16)) : 0u;
-      qa[mt][ks][2] = ra < count ? __ldg(reinterpret_cast<const uint32_t*>(qr + ks * 16 + 8)) : 0u;
-      qa[mt][ks][3] = rb < count ? __ldg(reinterpret_cast<const uint32_t*>(qr8 + ks * 16 + 8)) : 0u;
+      for (int cc = 0; cc < 8; ++cc)
+        *reinterpret_cast<uint4*>(smem + kOffQ + sw128_offset(row, cc)) =
+            valid ? __ldg(src + cc) : make_uint4(0, 0, 0, 0);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_full);
     }
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int c = 0; c < n_chunks; ++c) {
+      bool ready = !*abort_flag && mbar_wait_bounded(s_full, c & 1);
+      ready = __all_sync(0xffffffffu, ready);
+      if (!ready) {
+        if (lane == 0 && !*abort_flag) {
+          *abort_flag = 1;
+          record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
+        }
+        ok = false;
+        break;
+      }
+      tc_fence_after_sync();
+      uint32_t sr[2][32];
+      tmem_ld32(tmem_s + lane_base, sr[0]);
+      tmem_ld32(tmem_s + lane_base + 32, sr[1]);
+      tmem_wait_ld();
+      // Scores rounded to BF16 where the reference rounds them (its score GEMM
+      // writes BF16, src/model/attention.cu:10-51), taken to base 2, masked.
+      const int key0 = c * kTcChunk;
+      float x[kTcChunk];
+      float mx = -INFINITY;
 #pragma unroll
-    for (int d = 0; d < 8; ++d) o[mt][d][0] = o[mt][d][1] = o[mt][d][2] = o[mt][d][3] = 0.f;
-    m[mt][0] = m[mt][1] = -INFINITY;
-    l[mt][0] = l[mt][1] = 0.f;
-  }
-
-  // ldmatrix row addresses: K (non-transposed, B operand of S = Q K^T):
-  // matrix i = keys 8 (i >> 1) .., chunk 2 ks + (i & 1); V (transposed, B
-  // operand of O = P V): matrix i = keys 8 (i & 1) .., chunk 2 dp + (i >> 1).
-  const int k_key = (mat >> 1) * 8 + mrow, k_chunk = mat & 1;
-  const int v_key = (mat & 1) * 8 + mrow, v_chunk = mat >> 1;
-
-  int stage = 0;
-  uint32_t parity = 0;
-  for (int j = 0; j < n_pages; ++j) {
-    bool ready = false;
-    if (!*abort_flag) ready = mbar_wait_bounded(smem_addr(&full_bar[stage]), parity);
-    ready = __all_sync(0xffffffffu, ready);
-    if (!ready && lane == 0 && !*abort_flag) {
+      for (int j = 0; j < kTcChunk; ++j) {
+        const float v = __uint_as_float(sr[j >> 5][j & 31]);
+        x[j] = key0 + j <= qpos
+                   ? __bfloat162float(__float2bfloat16_rn(v * p.scale)) * 1.4426950408889634f
+                   : -INFINITY;
+        mx = fmaxf(mx, x[j]);
+      }
+      // Lazy running max: rescale only when a score beats the row's max by
+      // more than kLazyMargin (probabilities stay below 2^kLazyMargin).
+      float alpha = 1.f;
+      if (mx > m + kLazyMargin) {
+        const float mn = fmaxf(m, mx);
+        alpha = m == -INFINITY ? 0.f : fast_exp2(m - mn);
+        m = mn;
+      }
+      if (c > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        // O holds chunks 0 .. c - 1 (their P V completed before s_full(c)).
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t o[32];
+          tmem_ld32(tmem_o + lane_base + 32 * half, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+          tmem_st32(tmem_o + lane_base + 32 * half, o);
+        }
+        tmem_wait_st();
+      }
+      l *= alpha;
+      const float base = m == -INFINITY ? 0.f : m;
+      // P row into the swizzled A tile of O += P V; l sums the BF16 values the
+      // MMA multiplies.
+      float lsum = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          w[e] = pack_bf16x2(fast_exp2(x[8 * cc + 2 * e] - base),
+                             fast_exp2(x[8 * cc + 2 * e + 1] - base));
+          lsum += bf16lo_to_f32(w[e]) + bf16hi_to_f32(w[e]);
+        }
+        *reinterpret_cast<uint4*>(smem + kOffP + sw128_offset(row, cc)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      l += lsum;
+      // The last page's rows past pos_last hold stale data (possibly NaN): zero
+      // them in the V tile before P V reads it (P is 0 there, but 0 x NaN is not).
+      if (c == n_chunks - 1 && warp == 2)
+        zero_stale_v_rows(smem + kOffStages + (c % kTcStages) * kTcStageBytes + kTcKvBytes +
+                              (last_page - c * kTcChunkPages) * kTileBytes,
+                          pos_last % kPage + 1, lane);
+      fence_proxy_async_smem();
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    bool fin = ok && !*abort_flag && mbar_wait_bounded(o_full, 0);
+    fin = __all_sync(0xffffffffu, fin);
+    if (!fin && ok && lane == 0 && !*abort_flag) {
       *abort_flag = 1;
       record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
     }
-    const bool have = ready && stage_ok[stage];
-    const uint32_t kt = smem_base + stage * kPrefillStage, vt = kt + kTileBytes;
-    // Rows of the last page past pos_last hold stale data: warp 0 zeroes them in
-    // the V tile before any warp reads it (all 4 warps meet at the barrier).
-    if (j == n_pages - 1) {
-      if (have && warp == 0) {
-        zero_stale_v_rows(smem + stage * kPrefillStage + kTileBytes, pos_last % kPage + 1, lane);
-        fence_proxy_async_smem();
-      }
-      named_barrier_sync(1, kGroup * 32);
-    }
-    uint32_t kb[4][4], vb[4][4];
-    if (have) {
+    if (fin) {
+      tc_fence_after_sync();
+      uint32_t o[2][32];
+      tmem_ld32(tmem_o + lane_base, o[0]);
+      tmem_ld32(tmem_o + lane_base + 32, o[1]);
+      tmem_wait_ld();
+      if (valid) {
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)(tok0 + t) * qdim + hq * kHeadDim);
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        ldmatrix_x4(kt + k_key * 128 + (((2 * ks + k_chunk) ^ (k_key & 7)) << 4), kb[ks][0],
-                    kb[ks][1], kb[ks][2], kb[ks][3]);
+        for (int cc = 0; cc < 8; ++cc) {
+          uint32_t w[4];
 #pragma unroll
-      for (int dp = 0; dp < 4; ++dp)
-        ldmatrix_x4_trans(vt + v_key * 128 + (((2 * dp + v_chunk) ^ (v_key & 7)) << 4),
-                          vb[dp][0], vb[dp][1], vb[dp][2], vb[dp][3]);
-    }
-    __syncwarp();
-    if (ready && lane == 0) mbar_arrive(smem_addr(&empty_bar[stage]));
-    if (have) {
-      const int key0 = j * kPage + 2 * c;  // keys key0, key0 + 1, key0 + 8, key0 + 9
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        // S = Q K^T: n-tile 0 = keys 0-7, n-tile 1 = keys 8-15 of the page.
-        float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          mma_bf16_16816(s0[0], s0[1], s0[2], s0[3], qa[mt][ks][0], qa[mt][ks][1], qa[mt][ks][2],
-                         qa[mt][ks][3], kb[ks][0], kb[ks][1]);
-          mma_bf16_16816(s1[0], s1[1], s1[2], s1[3], qa[mt][ks][0], qa[mt][ks][1], qa[mt][ks][2],
-                         qa[mt][ks][3], kb[ks][2], kb[ks][3]);
-        }
-        float x[8] = {s0[0], s0[1], s1[0], s1[1], s0[2], s0[3], s1[2], s1[3]};
-        const int qpos_a = pos0 + 16 * mt + r, qpos_b = qpos_a + 8;
-        // Scores are rounded to BF16 where the reference rounds them (its score
-        // GEMM writes BF16, src/model/attention.cu:10-51), then taken to base 2.
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int key = key0 + (e & 1) + ((e >> 1) & 1) * 8;
-          const int qpos = e < 4 ? qpos_a : qpos_b;
-          x[e] = key <= qpos
-                     ? __bfloat162float(__float2bfloat16_rn(x[e] * p.scale)) * 1.4426950408889634f
-                     : -INFINITY;
-        }
-        float mx_a = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
-        float mx_b = fmaxf(fmaxf(x[4], x[5]), fmaxf(x[6], x[7]));
-        // Lazy running max (as in the decode kernels): the row maxima are
-        // reduced and O rescaled only when a score beats a row's max by more
-        // than kLazyMargin, so probabilities stay below 2^kLazyMargin.
-        float al_a = 1.f, al_b = 1.f;
-        if (__any_sync(0xffffffffu, mx_a > m[mt][0] + kLazyMargin || mx_b > m[mt][1] + kLazyMargin)) {
-#pragma unroll
-          for (int sh = 1; sh < 4; sh <<= 1) {
-            mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, sh));
-            mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, sh));
+          for (int e = 0; e < 4; ++e) {
+            const int d = 8 * cc + 2 * e;
+            w[e] = pack_bf16x2(__uint_as_float(o[d >> 5][d & 31]) * inv,
+                               __uint_as_float(o[(d + 1) >> 5][(d + 1) & 31]) * inv);
           }
-          const float mn_a = fmaxf(m[mt][0], mx_a), mn_b = fmaxf(m[mt][1], mx_b);
-          al_a = m[mt][0] == -INFINITY ? 0.f : fast_exp2(m[mt][0] - mn_a);
-          al_b = m[mt][1] == -INFINITY ? 0.f : fast_exp2(m[mt][1] - mn_b);
-          m[mt][0] = mn_a;
-          m[mt][1] = mn_b;
-        }
-        // rows that have seen no key yet keep a zero base (no inf - inf)
-        const float base_a = m[mt][0] == -INFINITY ? 0.f : m[mt][0];
-        const float base_b = m[mt][1] == -INFINITY ? 0.f : m[mt][1];
-        // P as the A operand of O += P V (keys 0-7 then 8-15 of the page)
-        uint32_t pa[4];
-        pa[0] = pack_bf16x2(fast_exp2(x[0] - base_a), fast_exp2(x[1] - base_a));
-        pa[1] = pack_bf16x2(fast_exp2(x[4] - base_b), fast_exp2(x[5] - base_b));
-        pa[2] = pack_bf16x2(fast_exp2(x[2] - base_a), fast_exp2(x[3] - base_a));
-        pa[3] = pack_bf16x2(fast_exp2(x[6] - base_b), fast_exp2(x[7] - base_b));
-        l[mt][0] = l[mt][0] * al_a + (bf16lo_to_f32(pa[0]) + bf16hi_to_f32(pa[0]) +
-                                      bf16lo_to_f32(pa[2]) + bf16hi_to_f32(pa[2]));
-        l[mt][1] = l[mt][1] * al_b + (bf16lo_to_f32(pa[1]) + bf16hi_to_f32(pa[1]) +
-                                      bf16lo_to_f32(pa[3]) + bf16hi_to_f32(pa[3]));
-        if (__any_sync(0xffffffffu, al_a != 1.f || al_b != 1.f)) {
-#pragma unroll
-          for (int d = 0; d < 8; ++d) {
-            o[mt][d][0] *= al_a; o[mt][d][1] *= al_a; o[mt][d][2] *= al_b; o[mt][d][3] *= al_b;
-          }
-        }
-#pragma unroll
-        for (int dp = 0; dp < 4; ++dp) {
-          mma_bf16_16816(o[mt][2 * dp][0], o[mt][2 * dp][1], o[mt][2 * dp][2], o[mt][2 * dp][3],
-                         pa[0], pa[1], pa[2], pa[3], vb[dp][0], vb[dp][1]);
-          mma_bf16_16816(o[mt][2 * dp + 1][0], o[mt][2 * dp + 1][1], o[mt][2 * dp + 1][2],
-                         o[mt][2 * dp + 1][3], pa[0], pa[1], pa[2], pa[3], vb[dp][2], vb[dp][3]);
+          dst[cc] = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
-    }
-    if (++stage == kPrefillStages) {
-      stage = 0;
-      parity ^= 1u;
     }
   }
-
-  // Normalise and store rows 16 mt + r, + 8 (channels 8 d + 2 c, + 1).
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt) {
-    float la = l[mt][0], lb = l[mt][1];
-#pragma unroll
-    for (int sh = 1; sh < 4; sh <<= 1) {
-      la += __shfl_xor_sync(0xffffffffu, la, sh);
-      lb += __shfl_xor_sync(0xffffffffu, lb, sh);
-    }
-    const float inv_a = la > 0.f ? 1.f / la : 0.f, inv_b = lb > 0.f ? 1.f / lb : 0.f;
-    const int ra = 16 * mt + r;
-    __nv_bfloat16* out_a = p.out + (size_t)(tok0 + ra) * qdim + hq * kHeadDim + 2 * c;
-    __nv_bfloat16* out_b = out_a + (size_t)8 * qdim;
-#pragma unroll
-    for (int d = 0; d < 8; ++d) {
-      if (ra < count)
-        *reinterpret_cast<uint32_t*>(out_a + 8 * d) =
-            pack_bf16x2(o[mt][d][0] * inv_a, o[mt][d][1] * inv_a);
-      if (ra + 8 < count)
-        *reinterpret_cast<uint32_t*>(out_b + 8 * d) =
-            pack_bf16x2(o[mt][d][2] * inv_b, o[mt][d][3] * inv_b);
-    }
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_s, kTcTmemCols);
   }
 }
 
@@ -309,8 +365,7 @@ cudaError_t launch_paged_prefill(const PrefillParams& p, long long pool_rows, in
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64 || !configured[dev]) {
-    e = cudaFuncSetAttribute(paged_prefill_kernel<kPrefillMTiles>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(paged_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)prefill_smem_bytes());
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev] = true;
@@ -319,9 +374,8 @@ cudaError_t launch_paged_prefill(const PrefillParams& p, long long pool_rows, in
   if (!pool_tensor_map(p.k_pool, pool_rows, p.kv_heads, &k_map) ||
       !pool_tensor_map(p.v_pool, pool_rows, p.kv_heads, &v_map))
     return cudaErrorInvalidValue;
-  const dim3 grid((max_q_len + kQTile - 1) / kQTile, num_seqs, p.kv_heads);
-  paged_prefill_kernel<kPrefillMTiles>
-      <<<grid, kPrefillThreads, prefill_smem_bytes(), stream>>>(p, k_map, v_map);
+  const dim3 grid((max_q_len + kTcTokens - 1) / kTcTokens, num_seqs, p.kv_heads);
+  paged_prefill_kernel<<<grid, kTcThreads, prefill_smem_bytes(), stream>>>(p, k_map, v_map);
   return cudaGetLastError();
 }
 
