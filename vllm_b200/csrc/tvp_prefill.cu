@@ -28,10 +28,16 @@
 //     causally, round scores to BF16 where the reference rounds them, keep an
 //     online base-2 softmax with a lazy running max (O in TMEM rescaled only
 //     when the max grows by more than kLazyMargin), and write P as BF16 into
-//     the 128-byte-swizzled A tile of the P V MMA.
-// Order per chunk c: S(c) -> softmax(c) -> [P V(c), S(c + 1)] -> ...; with 96
-// KiB of shared memory and 128 TMEM columns per CTA, two CTAs share an SM, so
-// one CTA's softmax overlaps the other's MMAs.
+//     a 128-byte-swizzled A tile of the P V MMA.
+// S (two TMEM buffers) and P (two shared tiles) are double-buffered, so the
+// tensor core computes S(c + 1) while the softmax works on chunk c, and
+// P V(c) while it works on chunk c + 1: the MMA thread issues S(0), S(1),
+// then per chunk c: [wait P(c)] P V(c), S(c + 2).  Each buffer has its own
+// full barrier, so no waiter is ever two phases behind (a parity wait tells
+// only the current phase from the one before it).  An O rescale waits for
+// P V(c - 1) on pv_done; S(c)'s commit already covers P V(c - 2), so that
+// wait, too, is at most one phase behind.  96 KiB of pipeline state and 256
+// TMEM columns per CTA let two CTAs share an SM.
 #include "tvp_tile.cuh"
 #include "tvp_umma.cuh"
 
@@ -49,32 +55,35 @@ constexpr int kTcStageBytes = 2 * kTcKvBytes;           // K, then V
 constexpr int kTcQBytes = kTcRows * 128;                // 64 BF16 per row
 constexpr int kTcPBytes = kTcRows * 128;                // 64 keys per row
 constexpr int kTcThreads = 6 * 32;
-constexpr uint32_t kTcTmemCols = 128;                   // S: columns 0-63, O: 64-127
+constexpr uint32_t kTcTmemCols = 256;  // S(even chunks) 0-63, S(odd) 64-127, O 128-191
 constexpr int kOffQ = 0;
-constexpr int kOffP = kOffQ + kTcQBytes;
-constexpr int kOffStages = kOffP + kTcPBytes;
+constexpr int kOffP = kOffQ + kTcQBytes;                // P(even), then P(odd)
+constexpr int kOffStages = kOffP + 2 * kTcPBytes;
 constexpr int kOffBars = kOffStages + kTcStages * kTcStageBytes;
-// q_full, s_full, p_full, o_full, drain, kv_full[stages], kv_empty[stages]
-constexpr int kBarKvFull = 5;
+// q_full, o_full, drain, pv_done, s_full[2], p_full[2], kv_full[stages], kv_empty[stages]
+constexpr int kBarSFull = 4;
+constexpr int kBarPFull = 6;
+constexpr int kBarKvFull = 8;
 constexpr int kBarKvEmpty = kBarKvFull + kTcStages;
 constexpr int kNumBars = kBarKvEmpty + kTcStages;
 
-constexpr size_t prefill_smem_bytes() {
-  return 1024 /* alignment slack */ + kOffBars + kNumBars * 8 + 16;
-}
+constexpr size_t prefill_smem_bytes() { return kOffBars + kNumBars * 8 + 16; }
 
 __global__ void __launch_bounds__(kTcThreads, 2)
     paged_prefill_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap k_map,
                          const __grid_constant__ CUtensorMap v_map) {
-  extern __shared__ unsigned char smem_raw[];
-  // 128-byte swizzled tiles need 1 KiB alignment: round the window up.
-  unsigned char* smem = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 128-byte swizzled tiles need 1 KiB alignment.  The dynamic shared window of
+  // this kernel (no static shared memory) starts 1 KiB aligned; a launch where
+  // it does not reports an error instead of running.
+  extern __shared__ __align__(1024) unsigned char smem[];
   const uint32_t sbase = smem_addr(smem);
+  if (sbase & 1023u) {
+    if (threadIdx.x == 0) record_error(p.err, TVP_DEVERR_SMEM_ALIGN);
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
   auto bar = [&](int i) { return smem_addr(&bars[i]); };
-  const uint32_t q_full = bar(0), s_full = bar(1), p_full = bar(2), o_full = bar(3),
-                 drain = bar(4);
+  const uint32_t q_full = bar(0), o_full = bar(1), drain = bar(2), pv_done = bar(3);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -98,10 +107,13 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     mbar_init(q_full, 4);
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
     mbar_init(o_full, 1);
     mbar_init(drain, 1);
+    mbar_init(pv_done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar(kBarSFull + b), 1);
+      mbar_init(bar(kBarPFull + b), 4);
+    }
     for (int i = 0; i < kTcStages; ++i) {
       mbar_init(bar(kBarKvFull + i), 1);
       mbar_init(bar(kBarKvEmpty + i), 1);
@@ -116,7 +128,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
-  const uint32_t tmem_s = *tmem_slot, tmem_o = tmem_s + 64;
+  const uint32_t tmem = *tmem_slot, tmem_o = tmem + 128;
 
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
@@ -162,53 +174,45 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     if (lane == 0) {
       constexpr uint32_t kIdS = umma_idesc_bf16_f32(kTcRows, kTcChunk, false, false);
       constexpr uint32_t kIdO = umma_idesc_bf16_f32(kTcRows, kHeadDim, false, true);
-      const uint32_t q_tile = sbase + kOffQ, p_tile = sbase + kOffP;
+      const uint32_t q_tile = sbase + kOffQ;
       auto stage_k = [&](int c) { return sbase + kOffStages + (c % kTcStages) * kTcStageBytes; };
-      // O += P V(c): K = the chunk's 64 keys, 16 (one page of V) per MMA.
-      auto issue_pv = [&](int c) {
+      bool ok = true;
+      auto wait = [&](uint32_t b, uint32_t parity) {
+        if (ok && !mbar_wait_bounded(b, parity)) {
+          record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
+          ok = false;
+        }
+        return ok;
+      };
+      // S(c) = Q K(c)^T into S buffer c % 2: K = the 64 channels, 16 per MMA.
+      auto issue_s = [&](int c) {
+        if (!wait(bar(kBarKvFull + c % kTcStages), (c / kTcStages) & 1)) return;
+        tc_fence_after_sync();
+        const uint32_t k_tile = stage_k(c);
+#pragma unroll
+        for (int k = 0; k < kHeadDim / 16; ++k)
+          umma_bf16(tmem + 64 * (c & 1), umma_desc_sw128(q_tile + 32 * k, 16, 1024),
+                    umma_desc_sw128(k_tile + 32 * k, 16, 1024), kIdS, k > 0);
+        umma_commit(bar(kBarSFull + (c & 1)));
+      };
+      wait(q_full, 0);
+      issue_s(0);
+      if (n_chunks > 1) issue_s(1);
+      for (int c = 0; ok && c < n_chunks; ++c) {
+        // O += P(c) V(c): K = the chunk's 64 keys, 16 (one page of V) per MMA.
+        if (!wait(bar(kBarPFull + (c & 1)), (c >> 1) & 1)) break;
+        tc_fence_after_sync();
+        const uint32_t p_tile = sbase + kOffP + (c & 1) * kTcPBytes;
         const uint32_t v_tile = stage_k(c) + kTcKvBytes;
 #pragma unroll
         for (int kk = 0; kk < kTcChunkPages; ++kk)
           umma_bf16(tmem_o, umma_desc_sw128(p_tile + 32 * kk, 16, 1024),
                     umma_desc_sw128(v_tile + kk * kTileBytes, 0, 1024), kIdO, (c > 0 || kk > 0));
-      };
-      bool ok = mbar_wait_bounded(q_full, 0);
-      if (!ok) record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
-      for (int c = 0; ok && c < n_chunks; ++c) {
-        if (!mbar_wait_bounded(bar(kBarKvFull + c % kTcStages), (c / kTcStages) & 1)) {
-          record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
-          ok = false;
-          break;
-        }
-        if (c > 0) {
-          if (!mbar_wait_bounded(p_full, (c - 1) & 1)) {
-            record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
-            ok = false;
-            break;
-          }
-          tc_fence_after_sync();
-          issue_pv(c - 1);
-          umma_commit(bar(kBarKvEmpty + (c - 1) % kTcStages));
-        }
-        tc_fence_after_sync();
-        // S = Q K(c)^T: K = the 64 channels, 16 per MMA.
-        const uint32_t k_tile = stage_k(c);
-#pragma unroll
-        for (int k = 0; k < kHeadDim / 16; ++k)
-          umma_bf16(tmem_s, umma_desc_sw128(q_tile + 32 * k, 16, 1024),
-                    umma_desc_sw128(k_tile + 32 * k, 16, 1024), kIdS, k > 0);
-        umma_commit(s_full);
+        umma_commit(pv_done);
+        umma_commit(bar(kBarKvEmpty + c % kTcStages));
+        if (c + 2 < n_chunks) issue_s(c + 2);
       }
-      if (ok) {
-        if (mbar_wait_bounded(p_full, (n_chunks - 1) & 1)) {
-          tc_fence_after_sync();
-          issue_pv(n_chunks - 1);
-          umma_commit(o_full);
-        } else {
-          record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
-          ok = false;
-        }
-      }
+      if (ok) umma_commit(o_full);
       if (!ok) *abort_flag = 1;
       // Every MMA issued has completed before Tensor Memory is released.
       umma_commit(drain);
@@ -238,10 +242,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       __syncwarp();
       if (lane == 0) mbar_arrive(q_full);
     }
-    float m = -INFINITY, l = 0.f;
+    float m = -INFINITY, l = 0.f;  // running max of the base-2 scores, normaliser
     bool ok = true;
+    constexpr float kLog2e = 1.4426950408889634f;
     for (int c = 0; c < n_chunks; ++c) {
-      bool ready = !*abort_flag && mbar_wait_bounded(s_full, c & 1);
+      bool ready = !*abort_flag && mbar_wait_bounded(bar(kBarSFull + (c & 1)), (c >> 1) & 1);
       ready = __all_sync(0xffffffffu, ready);
       if (!ready) {
         if (lane == 0 && !*abort_flag) {
@@ -253,22 +258,30 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       }
       tc_fence_after_sync();
       uint32_t sr[2][32];
-      tmem_ld32(tmem_s + lane_base, sr[0]);
-      tmem_ld32(tmem_s + lane_base + 32, sr[1]);
+      tmem_ld32(tmem + 64 * (c & 1) + lane_base, sr[0]);
+      tmem_ld32(tmem + 64 * (c & 1) + lane_base + 32, sr[1]);
       tmem_wait_ld();
       // Scores rounded to BF16 where the reference rounds them (its score GEMM
-      // writes BF16, src/model/attention.cu:10-51), taken to base 2, masked.
+      // writes BF16, src/model/attention.cu:10-51), two per conversion; keys
+      // past the row's position masked (only chunks that reach the tile's
+      // first position need the test).
       const int key0 = c * kTcChunk;
-      float x[kTcChunk];
+      const bool diagonal = key0 + kTcChunk - 1 > pos0;
+      float r[kTcChunk];
       float mx = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < kTcChunk; ++j) {
-        const float v = __uint_as_float(sr[j >> 5][j & 31]);
-        x[j] = key0 + j <= qpos
-                   ? __bfloat162float(__float2bfloat16_rn(v * p.scale)) * 1.4426950408889634f
-                   : -INFINITY;
-        mx = fmaxf(mx, x[j]);
+      for (int j = 0; j < kTcChunk; j += 2) {
+        const uint32_t pr = pack_bf16x2(__uint_as_float(sr[j >> 5][j & 31]) * p.scale,
+                                        __uint_as_float(sr[j >> 5][(j & 31) + 1]) * p.scale);
+        r[j] = bf16lo_to_f32(pr);
+        r[j + 1] = bf16hi_to_f32(pr);
+        if (diagonal) {
+          if (key0 + j > qpos) r[j] = -INFINITY;
+          if (key0 + j + 1 > qpos) r[j + 1] = -INFINITY;
+        }
+        mx = fmaxf(mx, fmaxf(r[j], r[j + 1]));
       }
+      mx *= kLog2e;
       // Lazy running max: rescale only when a score beats the row's max by
       // more than kLazyMargin (probabilities stay below 2^kLazyMargin).
       float alpha = 1.f;
@@ -278,7 +291,18 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         m = mn;
       }
       if (c > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-        // O holds chunks 0 .. c - 1 (their P V completed before s_full(c)).
+        // O holds chunks 0 .. c - 1 once P V(c - 1) completes.
+        bool done = !*abort_flag && mbar_wait_bounded(pv_done, (c - 1) & 1);
+        done = __all_sync(0xffffffffu, done);
+        if (!done) {
+          if (lane == 0 && !*abort_flag) {
+            *abort_flag = 1;
+            record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
+          }
+          ok = false;
+          break;
+        }
+        tc_fence_after_sync();
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           uint32_t o[32];
@@ -290,24 +314,23 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         }
         tmem_wait_st();
       }
-      l *= alpha;
-      const float base = m == -INFINITY ? 0.f : m;
-      // P row into the swizzled A tile of O += P V; l sums the BF16 values the
-      // MMA multiplies.
+      const float nbase = m == -INFINITY ? 0.f : -m;
+      // P row into this chunk's swizzled A tile of O += P V.
+      unsigned char* p_tile = smem + kOffP + (c & 1) * kTcPBytes;
       float lsum = 0.f;
 #pragma unroll
       for (int cc = 0; cc < 8; ++cc) {
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          w[e] = pack_bf16x2(fast_exp2(x[8 * cc + 2 * e] - base),
-                             fast_exp2(x[8 * cc + 2 * e + 1] - base));
-          lsum += bf16lo_to_f32(w[e]) + bf16hi_to_f32(w[e]);
+          const float p0 = fast_exp2(fmaf(r[8 * cc + 2 * e], kLog2e, nbase));
+          const float p1 = fast_exp2(fmaf(r[8 * cc + 2 * e + 1], kLog2e, nbase));
+          lsum += p0 + p1;
+          w[e] = pack_bf16x2(p0, p1);
         }
-        *reinterpret_cast<uint4*>(smem + kOffP + sw128_offset(row, cc)) =
-            make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(p_tile + sw128_offset(row, cc)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      l += lsum;
+      l = l * alpha + lsum;
       // The last page's rows past pos_last hold stale data (possibly NaN): zero
       // them in the V tile before P V reads it (P is 0 there, but 0 x NaN is not).
       if (c == n_chunks - 1 && warp == 2)
@@ -317,7 +340,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       fence_proxy_async_smem();
       tc_fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(bar(kBarPFull + (c & 1)));
     }
     bool fin = ok && !*abort_flag && mbar_wait_bounded(o_full, 0);
     fin = __all_sync(0xffffffffu, fin);
@@ -352,7 +375,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after_sync();
-    tmem_dealloc(tmem_s, kTcTmemCols);
+    tmem_dealloc(tmem, kTcTmemCols);
   }
 }
 
