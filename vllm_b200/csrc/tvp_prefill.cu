@@ -268,19 +268,25 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       const int key0 = c * kTcChunk;
       const bool diagonal = key0 + kTcChunk - 1 > pos0;
       float r[kTcChunk];
-      float mx = -INFINITY;
+      float mxs[8];  // eight independent max chains, merged by a tree
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mxs[i] = -INFINITY;
+      const uint64_t scale2 = f2_pack(p.scale, p.scale);
 #pragma unroll
       for (int j = 0; j < kTcChunk; j += 2) {
-        const uint32_t pr = pack_bf16x2(__uint_as_float(sr[j >> 5][j & 31]) * p.scale,
-                                        __uint_as_float(sr[j >> 5][(j & 31) + 1]) * p.scale);
+        float a, b;
+        f2_unpack(f2_mul(f2_pack(__uint_as_float(sr[j >> 5][j & 31]),
+                                 __uint_as_float(sr[j >> 5][(j & 31) + 1])), scale2), a, b);
+        const uint32_t pr = pack_bf16x2(a, b);
         r[j] = bf16lo_to_f32(pr);
         r[j + 1] = bf16hi_to_f32(pr);
         if (diagonal) {
           if (key0 + j > qpos) r[j] = -INFINITY;
           if (key0 + j + 1 > qpos) r[j + 1] = -INFINITY;
         }
-        mx = fmaxf(mx, fmaxf(r[j], r[j + 1]));
+        mxs[(j >> 1) & 7] = max3(mxs[(j >> 1) & 7], r[j], r[j + 1]);
       }
+      float mx = fmaxf(max3(mxs[0], mxs[1], mxs[2]), max3(mxs[3], mxs[4], max3(mxs[5], mxs[6], mxs[7])));
       mx *= kLog2e;
       // Lazy running max: rescale only when a score beats the row's max by
       // more than kLazyMargin (probabilities stay below 2^kLazyMargin).
@@ -317,19 +323,27 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       const float nbase = m == -INFINITY ? 0.f : -m;
       // P row into this chunk's swizzled A tile of O += P V.
       unsigned char* p_tile = smem + kOffP + (c & 1) * kTcPBytes;
-      float lsum = 0.f;
+      const uint64_t l2e2 = f2_pack(kLog2e, kLog2e), nb2 = f2_pack(nbase, nbase);
+      uint64_t ls2[4];  // four independent paired sums
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ls2[i] = f2_pack(0.f, 0.f);
 #pragma unroll
       for (int cc = 0; cc < 8; ++cc) {
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = fast_exp2(fmaf(r[8 * cc + 2 * e], kLog2e, nbase));
-          const float p1 = fast_exp2(fmaf(r[8 * cc + 2 * e + 1], kLog2e, nbase));
-          lsum += p0 + p1;
+          const int j0 = 8 * cc + 2 * e;
+          float a0, a1;
+          f2_unpack(f2_fma(f2_pack(r[j0], r[j0 + 1]), l2e2, nb2), a0, a1);
+          const float p0 = fast_exp2(a0), p1 = fast_exp2(a1);
+          ls2[e] = f2_add(ls2[e], f2_pack(p0, p1));
           w[e] = pack_bf16x2(p0, p1);
         }
         *reinterpret_cast<uint4*>(p_tile + sw128_offset(row, cc)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
+      float la, lb;
+      f2_unpack(f2_add(f2_add(ls2[0], ls2[1]), f2_add(ls2[2], ls2[3])), la, lb);
+      const float lsum = la + lb;
       l = l * alpha + lsum;
       // The last page's rows past pos_last hold stale data (possibly NaN): zero
       // them in the V tile before P V reads it (P is 0 there, but 0 x NaN is not).
