@@ -124,10 +124,15 @@ def run_reference_arm(args, rank, world):
         samples.append(cb["value"])
     value = statistics.median(samples)
     cb["value"] = round(value, 3)
+    # Each timed step is a bounded sample; ms_per_step is one full step of the
+    # workload (256 rows, 16 layers) at the measured rate.
+    step_bytes = algorithmic_bytes(W.sweep_lengths(4, 256))["kv"] * 16
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(step_bytes / (value * 1e9) * 1e3, 1),
+        "ms_per_step_basis": "one full decode_sweep step (256 rows x 16 layers) at the sample rate",
+        "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": config_block(world, 256), "cpu_baseline": cb,
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
