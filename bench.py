@@ -541,7 +541,8 @@ def bench_long_context_heads(dev, iters=20):
     from vllm_b200 import ops
     peak, kind = hbm_peak()
     res = {"workload": "long_context 16 x 32768, 1 layer, pools of kv_heads of the 8 heads",
-           "peak_source": kind}
+           "peak_source": kind, "l2": "flushed between timed launches (256 MB written)"}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     for kv_heads in (4, 2, 1):
         case, kp, vp, q = long_context_pools(dev, kv_heads)
         tables = torch.from_numpy(case.tables).to(dev)
@@ -554,7 +555,8 @@ def bench_long_context_heads(dev, iters=20):
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(iters)]
         torch.cuda.synchronize(dev)
-        for a, b in ev:
+        for i, (a, b) in enumerate(ev):
+            flush.fill_(i & 0xFF)
             a.record()
             ops.paged_decode_attention(q, kp, vp, 0, tables, lens, ws, out=out)
             b.record()
@@ -585,7 +587,9 @@ def bench_head_sharded(dev, rank, world, local_rank, iters=20):
     lens = torch.from_numpy(case.lens).to(dev)
     stream = torch.cuda.current_stream(dev)
     res = {"workload": f"long_context 16 x 32768, 1 layer, {kv_heads} KV head(s) per GPU",
-           "all_gather_bytes_per_rank": 16 * kv_heads * W.GROUP * W.HEAD_DIM * 2}
+           "all_gather_bytes_per_rank": 16 * kv_heads * W.GROUP * W.HEAD_DIM * 2,
+           "l2": "flushed between timed layers (256 MB written)"}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
     def timed(fn):
         for _ in range(3):
@@ -594,7 +598,8 @@ def bench_head_sharded(dev, rank, world, local_rank, iters=20):
               for _ in range(iters)]
         dist.barrier(device_ids=[local_rank])
         torch.cuda.synchronize(dev)
-        for a, b in ev:
+        for i, (a, b) in enumerate(ev):
+            flush.fill_(i & 0xFF)
             a.record(stream)
             fn()
             b.record(stream)
