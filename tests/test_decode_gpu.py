@@ -162,6 +162,23 @@ def test_plan_mismatch_is_reported():
     assert int(err.item()) & N.TVP_DEVERR_BAD_PLAN
 
 
+@pytest.mark.parametrize("kv_heads", [8, 1])
+def test_batch_beyond_one_plan_block(kv_heads):
+    """3000 ragged rows (empty, one-page and multi-page rows, a few long ones):
+    the plan's prefix scan runs over three 1024-row blocks with a carry, most
+    CTAs hold many whole sequences and the split-K slots and counters are
+    indexed far past the first block."""
+    rng = np.random.default_rng(5)
+    lens = rng.integers(0, 120, size=3000).astype(np.int32)
+    lens[rng.choice(3000, 6, replace=False)] = [5000, 3000, 2048, 1025, 16, 17]
+    lens[::97] = 0
+    case = W.decode_random(23, lens, kv_heads=kv_heads)
+    out, err = run_decode(case)
+    assert err == 0
+    assert_close_bf16(out, exact_out(case), ATOL, RTOL, f"3000 rows, kv_heads={kv_heads}")
+    assert (out[lens == 0] == 0).all()
+
+
 def test_long_context_rows():
     case = W.decode_random(81, [32768, 20000, 5])
     out, err = run_decode(case)
