@@ -27,7 +27,10 @@
 // box is the largest unit that is contiguous in a page *and* swizzlable;
 // one bulk copy per 1 KiB token row streamed at only ~4.4 TB/s on B200,
 // these boxes stream at the copy roofline.
-// Consumer warp g of set s owns KV head g on the pages k with k % SETS == s.
+// Consumer warp g of set s owns KV head g on the pages i of each sequence
+// piece with i % SETS == s (the sets' states are merged at the piece's end).
+// With an odd number of stages consecutive rounds of a stage go to different
+// sets, so each set gates its stage waits on the stage's round tag.
 // Per page it forms S^T = K_g Q_g^T (16 tokens x 8 query columns, 4 real) and
 // O^T += V_g^T P^T with mma.m16n8k16 (BF16 in, FP32 accumulate), running an
 // online softmax in base 2 on the accumulator fragments; P^T is turned from
@@ -119,9 +122,9 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
     if (threadIdx.x == 0) record_error(p.err, TVP_DEVERR_SMEM_ALIGN);
     return;
   }
-  const int T_header_ok = (p.header[0] == kPlanMagic && p.header[1] == p.batch &&
-                           p.header[2] == (int)gridDim.x && p.header[3] == kMaxKvHeads);
-  if (!T_header_ok) {
+  const bool plan_ok = (p.header[0] == kPlanMagic && p.header[1] == p.batch &&
+                        p.header[2] == (int)gridDim.x && p.header[3] == kMaxKvHeads);
+  if (!plan_ok) {
     if (threadIdx.x == 0 && blockIdx.x == 0) record_error(p.err, TVP_DEVERR_BAD_PLAN);
     return;
   }
@@ -131,11 +134,10 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
   // producer before it issues the round (see stage_tag_wait).
   volatile int* stage_tag = reinterpret_cast<int*>(empty_bar + STAGES);
   volatile int* abort_flag = stage_tag + STAGES;
-  // Set-merge scratch (only with two consumer sets).
-  float* merge = reinterpret_cast<float*>(smem + STAGES * kStageBytes + 2 * STAGES * 8 +
-                                          (STAGES + 4) * 4);
-  merge = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(merge) + 15) & ~uintptr_t(15));
-  (void)merge;
+  // Set-merge scratch (used with two consumer sets only), 16-byte aligned.
+  [[maybe_unused]] float* const merge = reinterpret_cast<float*>(
+      (reinterpret_cast<uintptr_t>(smem + STAGES * kStageBytes + 2 * STAGES * 8 +
+                                   (STAGES + 4) * 4) + 15) & ~uintptr_t(15));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
