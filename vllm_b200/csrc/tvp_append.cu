@@ -27,13 +27,19 @@ __device__ __forceinline__ float llama3_theta(int pair) {
   return theta;
 }
 
-// Rotation of one (x, y) = (d, d + 32) pair, as src/model/RoPe.cu:23-27.
-__device__ __forceinline__ void rope_rotate(__nv_bfloat16 x_i, __nv_bfloat16 y_i, int position,
-                                            float theta, __nv_bfloat16& x_o,
-                                            __nv_bfloat16& y_o) {
-  float angle = position * theta;
-  x_o = (__nv_bfloat16)((float)x_i * cosf(angle) - (float)y_i * sinf(angle));
-  y_o = (__nv_bfloat16)((float)x_i * sinf(angle) + (float)y_i * cosf(angle));
+// Rotation of one (x, y) = (d, d + 32) pair by cos/sin of angle = position *
+// theta, src/model/RoPe.cu:23-27: x' = x cos - y sin, y' = x sin + y cos.
+// cos and sin depend on the position and the pair only, so they are evaluated
+// once per token row.  The products are fused as nvcc fuses the reference's
+// expression (x' = fma(x, cos, -(y sin)), y' = fma(y, cos, x sin): all 2^20
+// (position, pair) rotations of positions 0..32767 compared bit for bit with
+// the reference kernel's output), written out so that the rounding does not
+// depend on where the compiler finds cos and sin.
+__device__ __forceinline__ void rope_rotate(__nv_bfloat16 x_i, __nv_bfloat16 y_i, float c, float s,
+                                            __nv_bfloat16& x_o, __nv_bfloat16& y_o) {
+  const float x = (float)x_i, y = (float)y_i;
+  x_o = (__nv_bfloat16)__fmaf_rn(x, c, -__fmul_rn(y, s));
+  y_o = (__nv_bfloat16)__fmaf_rn(y, c, __fmul_rn(x, s));
 }
 
 
@@ -43,6 +49,18 @@ __global__ void __launch_bounds__(256) rope_append_kernel(AppendParams p) {
   const int seq = p.token_seq ? p.token_seq[t] : t;
   const int kv_dim = p.kv_heads * kHeadDim;
 
+  // cos and sin of angle = pos * theta(pair) for the 32 pairs, shared by all
+  // of the row's q and K heads.
+  __shared__ float cos_pair[kHeadDim / 2], sin_pair[kHeadDim / 2];
+  if (p.flags & (TVP_APPEND_ROPE_Q | TVP_APPEND_ROPE_K)) {
+    if (threadIdx.x < kHeadDim / 2) {
+      const float angle = pos * llama3_theta(threadIdx.x);
+      cos_pair[threadIdx.x] = cosf(angle);
+      sin_pair[threadIdx.x] = sinf(angle);
+    }
+    __syncthreads();
+  }
+
   if (p.flags & TVP_APPEND_ROPE_Q) {
     __nv_bfloat16* qrow = p.q + (size_t)t * p.q_heads * kHeadDim;
     const int pairs = p.q_heads * (kHeadDim / 2);
@@ -51,7 +69,7 @@ __global__ void __launch_bounds__(256) rope_append_kernel(AppendParams p) {
       const int x_index = (i / (kHeadDim / 2)) * kHeadDim + pair;
       const int y_index = x_index + kHeadDim / 2;
       __nv_bfloat16 xo, yo;
-      rope_rotate(qrow[x_index], qrow[y_index], pos, llama3_theta(pair), xo, yo);
+      rope_rotate(qrow[x_index], qrow[y_index], cos_pair[pair], sin_pair[pair], xo, yo);
       qrow[x_index] = xo;
       qrow[y_index] = yo;
     }
@@ -76,7 +94,7 @@ __global__ void __launch_bounds__(256) rope_append_kernel(AppendParams p) {
     const int x_index = (i / (kHeadDim / 2)) * kHeadDim + pair;
     const int y_index = x_index + kHeadDim / 2;
     __nv_bfloat16 xo = krow[x_index], yo = krow[y_index];
-    if (p.flags & TVP_APPEND_ROPE_K) rope_rotate(xo, yo, pos, llama3_theta(pair), xo, yo);
+    if (p.flags & TVP_APPEND_ROPE_K) rope_rotate(xo, yo, cos_pair[pair], sin_pair[pair], xo, yo);
     p.k_pool[dst + x_index] = xo;
     p.k_pool[dst + y_index] = yo;
     if (p.flags & TVP_APPEND_WRITEBACK_K) {
