@@ -12,17 +12,17 @@ namespace {
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct WorkspaceLayout {
-  size_t header, cu, cta_seq, counters, partials, total;
+  size_t header, cu, cta_start, counters, partials, total;
 };
 
-// header | cu[batch + 1] | cta_seq[num_ctas] | counters[batch][kv_heads] |
+// header | cu[batch + 1] | cta_start[num_ctas] (int4) | counters[batch][kv_heads] |
 // partials[2 num_ctas][kv_heads]
 WorkspaceLayout workspace_layout(int batch, int kv_heads, int num_ctas) {
   WorkspaceLayout w;
   w.header = 0;
   w.cu = 256;
-  w.cta_seq = align_up(w.cu + (size_t)(batch + 1) * 4, 256);
-  w.counters = align_up(w.cta_seq + (size_t)num_ctas * 4, 256);
+  w.cta_start = align_up(w.cu + (size_t)(batch + 1) * 4, 256);
+  w.counters = align_up(w.cta_start + (size_t)num_ctas * 16, 256);
   w.partials = align_up(w.counters + (size_t)batch * kv_heads * 4, 256);
   w.total = align_up(w.partials + (size_t)num_ctas * 2 * kv_heads * kPartialFloats * 4, 256);
   return w;
@@ -92,7 +92,7 @@ int prepare_decode(const void* q, const void* k_pool, const void* v_pool, int nu
   p->seq_lens = d_seq_lens;
   p->header = reinterpret_cast<const int32_t*>(base + w.header);
   p->cu = reinterpret_cast<const int32_t*>(base + w.cu);
-  p->cta_seq = reinterpret_cast<const int32_t*>(base + w.cta_seq);
+  p->cta_start = reinterpret_cast<const int4*>(base + w.cta_start);
   p->counters = reinterpret_cast<int32_t*>(base + w.counters);
   p->partials = reinterpret_cast<float*>(base + w.partials);
   p->layer_row_base = (long long)layer * num_pages * kPage;
@@ -189,7 +189,7 @@ int tvp_decode_plan(const int32_t* d_seq_lens, int batch, int table_stride, int 
   return map_cuda(launch_decode_plan(d_seq_lens, batch, table_stride, ctas, kv_heads,
                                      reinterpret_cast<int32_t*>(base + w.header),
                                      reinterpret_cast<int32_t*>(base + w.cu),
-                                     reinterpret_cast<int32_t*>(base + w.cta_seq),
+                                     reinterpret_cast<int4*>(base + w.cta_start),
                                      reinterpret_cast<int32_t*>(base + w.counters), d_error,
                                      static_cast<cudaStream_t>(stream)));
 }

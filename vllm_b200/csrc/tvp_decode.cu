@@ -45,12 +45,12 @@ constexpr int kMergeFields = 2;  // per-lane values exchanged per merge round (s
 
 
 // ---------------------------------------------------------------------------
-// Plan: cu[b] = sum_{i<b} ceil(L_i / 16), cta_seq[c] = the sequence holding
-// CTA c's first page, header, counters = 0.
+// Plan: cu[b] = sum_{i<b} ceil(L_i / 16), cta_start[c] = {s, cu[s], cu[s + 1]}
+// for the sequence s holding CTA c's first page, header, counters = 0.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024)
     decode_plan_kernel(const int32_t* __restrict__ lens, int batch, int table_stride,
-                       int num_ctas, int groups, int32_t* header, int32_t* cu, int32_t* cta_seq,
+                       int num_ctas, int groups, int32_t* header, int32_t* cu, int4* cta_start,
                        int32_t* counters, int32_t* err) {
   __shared__ int warp_sums[32];
   __shared__ int carry;
@@ -97,7 +97,8 @@ __global__ void __launch_bounds__(1024)
   for (int s = tid; s < batch && C > 0; s += blockDim.x) {
     const long long a = cu[s];
     const long long b = s + 1 < batch ? (long long)cu[s + 1] : T;
-    for (long long c = (a * C + T - 1) / T; c < (b * C + T - 1) / T; ++c) cta_seq[c] = s;
+    for (long long c = (a * C + T - 1) / T; c < (b * C + T - 1) / T; ++c)
+      cta_start[c] = make_int4(s, (int)a, (int)b, 0);
   }
   if (tid == 0) {
     cu[batch] = carry;
@@ -118,12 +119,19 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
   // memory) starts 1 KiB aligned; a launch where it does not reports an error
   // instead of running the copies.
   extern __shared__ __align__(1024) unsigned char smem[];
+  // The plan's header, the step's page count and this CTA's start record,
+  // loaded together (one round trip) before anything depends on them.  The
+  // record is read only when the header matches this launch and the CTA
+  // takes pages; the workspace holds one record per CTA of the grid.
+  const int4 hdr = __ldg(reinterpret_cast<const int4*>(p.header));
+  const int total_pages = __ldg(p.cu + p.batch);
+  const int4 start = __ldg(p.cta_start + blockIdx.x);
   if (smem_addr(smem) & 1023u) {
     if (threadIdx.x == 0) record_error(p.err, TVP_DEVERR_SMEM_ALIGN);
     return;
   }
-  const bool plan_ok = (p.header[0] == kPlanMagic && p.header[1] == p.batch &&
-                        p.header[2] == (int)gridDim.x && p.header[3] == kMaxKvHeads);
+  const bool plan_ok = (hdr.x == kPlanMagic && hdr.y == p.batch && hdr.z == (int)gridDim.x &&
+                        hdr.w == kMaxKvHeads);
   if (!plan_ok) {
     if (threadIdx.x == 0 && blockIdx.x == 0) record_error(p.err, TVP_DEVERR_BAD_PLAN);
     return;
@@ -153,15 +161,16 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
 
   // Only min(grid, T) CTAs take pages, so that every range holds at least one
   // page and the pieces of a sequence are exactly the CTAs c0..c1 it spans.
-  const long long T = p.cu[p.batch];
+  const long long T = total_pages;
   const long long C = T < (long long)gridDim.x ? T : (long long)gridDim.x;
   const long long c = blockIdx.x;
   const int p_begin = c < C ? (int)(c * T / C) : 0;
   const int p_end = c < C ? (int)((c + 1) * T / C) : 0;
   const uint32_t smem_base = smem_addr(smem);
 
-  // First sequence of the range (the s with cu[s] <= p_begin < cu[s + 1]), from the plan.
-  const int s0 = p_begin < p_end ? __ldg(p.cta_seq + c) : 0;
+  // First sequence of the range (the s with cu[s] <= p_begin < cu[s + 1]) and
+  // its page span, from the plan.
+  const int s0 = p_begin < p_end ? start.x : 0;
 
   if (warp >= SETS * kMaxKvHeads) {
     // ------------------------------ producer ------------------------------
@@ -177,11 +186,7 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
     // and the next page id is loaded one iteration ahead, so nothing but the
     // empty-slot wait sits between a slot being freed and its refill.
     int s = s0;
-    int seq_first = 0, seq_end = 0;
-    if (p_begin < p_end) {
-      seq_first = __ldg(p.cu + s);
-      seq_end = __ldg(p.cu + s + 1);
-    }
+    int seq_first = start.y, seq_end = start.z;  // used only when the CTA takes pages
     int next_phys = p_begin < p_end
                         ? __ldg(p.tables + (size_t)s * p.table_stride + (p_begin - seq_first))
                         : 0;
@@ -255,6 +260,7 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
   }
 
   int s = s0;
+  int first = start.y, end = start.z;  // page span of sequence s
   int pg = p_begin;
   int kbase = 0;
   // Slot and round of this set's current page, advanced incrementally (page
@@ -263,8 +269,11 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
   // sets, so a set's wait is gated on the slot's tag (stage_tag_wait).
   int c_kk = 0, c_stage = 0, c_round = 0;
   while (pg < p_end) {
-    while (pg >= __ldg(p.cu + s + 1)) ++s;
-    const int first = __ldg(p.cu + s), end = __ldg(p.cu + s + 1);
+    while (pg >= end) {  // next non-empty sequence
+      ++s;
+      first = end;
+      end = __ldg(p.cu + s + 1);
+    }
     const int piece_end = min(p_end, end);
     const int n = piece_end - pg;
     const bool complete = (pg == first) && (piece_end == end);
@@ -399,10 +408,10 @@ constexpr size_t decode_smem_bytes() {
 }
 
 cudaError_t launch_decode_plan(const int32_t* lens, int batch, int table_stride, int num_ctas,
-                               int kv_heads, int32_t* header, int32_t* cu, int32_t* cta_seq,
+                               int kv_heads, int32_t* header, int32_t* cu, int4* cta_start,
                                int32_t* counters, int32_t* err, cudaStream_t stream) {
   decode_plan_kernel<<<1, 1024, 0, stream>>>(lens, batch, table_stride, num_ctas, kv_heads,
-                                             header, cu, cta_seq, counters, err);
+                                             header, cu, cta_start, counters, err);
   return cudaGetLastError();
 }
 

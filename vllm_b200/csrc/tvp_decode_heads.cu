@@ -106,12 +106,15 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
   constexpr int STAGES = kHeadsStages;
   // 1 KiB alignment of the stage tiles (128-byte swizzle); checked, as in K2.
   extern __shared__ __align__(1024) unsigned char smem[];
+  // Plan header, page count and this CTA's start record in one round trip (K2).
+  const int4 hdr = __ldg(reinterpret_cast<const int4*>(p.header));
+  const int total_pages = __ldg(p.cu + p.batch);
+  const int4 start = __ldg(p.cta_start + blockIdx.x);
   if (smem_addr(smem) & 1023u) {
     if (threadIdx.x == 0) record_error(p.err, TVP_DEVERR_SMEM_ALIGN);
     return;
   }
-  if (!(p.header[0] == kPlanMagic && p.header[1] == p.batch &&
-        p.header[2] == (int)gridDim.x && p.header[3] == KVH)) {
+  if (!(hdr.x == kPlanMagic && hdr.y == p.batch && hdr.z == (int)gridDim.x && hdr.w == KVH)) {
     if (threadIdx.x == 0 && blockIdx.x == 0) record_error(p.err, TVP_DEVERR_BAD_PLAN);
     return;
   }
@@ -134,7 +137,7 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
   }
   __syncthreads();
 
-  const long long T = p.cu[p.batch];
+  const long long T = total_pages;
   const long long C = T < (long long)gridDim.x ? T : (long long)gridDim.x;
   const long long c = blockIdx.x;
   const int p_begin = c < C ? (int)(c * T / C) : 0;
@@ -142,7 +145,7 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
   const int n = p_end - p_begin;
   const uint32_t smem_base = smem_addr(smem);
 
-  const int s0 = n > 0 ? __ldg(p.cta_seq + c) : 0;  // sequence of the range's first page
+  const int s0 = n > 0 ? start.x : 0;  // sequence of the range's first page
 
   if (warp >= 2 * kStageTiles) {
     // ------------------------------ producer ------------------------------
@@ -168,8 +171,8 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
       phys = __ldg(p.tables + (size_t)s * p.table_stride + (pg - seq_first));
     };
     if (lane < PS && i < n) {
-      seq_first = __ldg(p.cu + s);
-      seq_end = __ldg(p.cu + s + 1);
+      seq_first = start.y;
+      seq_end = start.z;
       walk();
     }
     const int n_stages = (n + PS - 1) / PS;
@@ -244,13 +247,17 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
   }
 
   int s = s0;
+  int first = start.y, end = start.z;  // page span of sequence s
   int pg = p_begin;
   int kbase = 0;  // range-local index of the piece's first page
   int c_kk = 0, c_stage = 0;
   uint32_t c_parity = 0;
   while (pg < p_end) {
-    while (pg >= __ldg(p.cu + s + 1)) ++s;
-    const int first = __ldg(p.cu + s), end = __ldg(p.cu + s + 1);
+    while (pg >= end) {  // next non-empty sequence
+      ++s;
+      first = end;
+      end = __ldg(p.cu + s + 1);
+    }
     const int piece_end = min(p_end, end);
     const int np = piece_end - pg;
     const bool complete = (pg == first) && (piece_end == end);

@@ -36,7 +36,9 @@ struct DecodeParams {
   const int32_t* seq_lens;
   const int32_t* header;
   const int32_t* cu;
-  const int32_t* cta_seq;  // per CTA: the sequence holding its first page
+  // Per CTA taking pages: {s0, cu[s0], cu[s0 + 1], 0}, s0 the sequence holding
+  // its first page (so the CTA starts without walking the prefix sums).
+  const int4* cta_start;
   int32_t* counters;
   float* partials;
   long long layer_row_base;  // layer * num_pages * 16
@@ -94,7 +96,7 @@ constexpr int kPartialFloats = 2 * kGroup + kGroup * kHeadDim;
 
 cudaError_t launch_rope_append(const AppendParams& p, int num_tokens, cudaStream_t stream);
 cudaError_t launch_decode_plan(const int32_t* lens, int batch, int table_stride, int num_ctas,
-                               int kv_heads, int32_t* header, int32_t* cu, int32_t* cta_seq,
+                               int kv_heads, int32_t* header, int32_t* cu, int4* cta_start,
                                int32_t* counters, int32_t* err, cudaStream_t stream);
 // Dispatches on p.kv_heads: 8 -> tvp_decode.cu, 1, 2, 4 -> tvp_decode_heads.cu.
 cudaError_t launch_paged_decode(const DecodeParams& p, long long pool_rows, int num_ctas,
