@@ -165,8 +165,8 @@ int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const 
  * each attends the keys 0..its position already in the sequence's pages
  * (append them first with tvp_rope_append).  d_q_pos0[s] = 0 is a prompt;
  * d_q_pos0[s] = L0 > 0 a prefill chunk after L0 cached tokens.
- * q, out: [num_tokens][q_heads * 64] BF16, head-major as the reference;
- * max_q_len >= the longest sequence's query count.
+ * q, out: [num_tokens][q_heads * 64] BF16, head-major as the reference,
+ * 16-byte aligned; max_q_len >= the longest sequence's query count.
  */
 int tvp_paged_prefill_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const tvp_bf16* v_pool,
                                 int num_pages, int num_layers, int layer, int kv_heads, int q_heads,

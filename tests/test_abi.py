@@ -81,6 +81,36 @@ def test_decode_rejects_bad_arguments_on_host(native):
     assert call(out=ctypes.c_void_p(0x10008)) == N.TVP_ERR_INVALID_ARGUMENT
 
 
+def test_prefill_rejects_bad_arguments_on_host(native):
+    fake = ctypes.c_void_p(0x10000)
+    args = dict(q=fake, k=fake, v=fake, pages=8, layers=16, layer=0, kvh=8, qh=32, tables=fake,
+                stride=4, cu=fake, pos0=fake, seqs=2, maxq=64, scale=0.125, out=fake, err=None,
+                stream=None)
+
+    def call(**over):
+        a = dict(args, **over)
+        return native.tvp_paged_prefill_attention(a["q"], a["k"], a["v"], a["pages"], a["layers"],
+                                                  a["layer"], a["kvh"], a["qh"], a["tables"],
+                                                  a["stride"], a["cu"], a["pos0"], a["seqs"],
+                                                  a["maxq"], a["scale"], a["out"], a["err"],
+                                                  a["stream"])
+
+    assert call(q=None) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(cu=None) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(layer=16) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(seqs=0) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(seqs=65536) == N.TVP_ERR_INVALID_ARGUMENT    # one grid row per sequence
+    assert call(maxq=-1) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(scale=float("inf")) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(kvh=3, qh=12) == N.TVP_ERR_UNSUPPORTED
+    assert call(qh=16) == N.TVP_ERR_UNSUPPORTED
+    # q and output rows move as 16-byte vectors
+    assert call(q=ctypes.c_void_p(0x10004)) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(out=ctypes.c_void_p(0x10008)) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(k=ctypes.c_void_p(0x10008)) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(maxq=0) == N.TVP_OK                         # nothing to attend: no launch
+
+
 def test_workspace_size_grows_with_batch_and_grid(native):
     a = native.tvp_decode_workspace_bytes(4, 8, 148)
     b = native.tvp_decode_workspace_bytes(256, 8, 148)
@@ -90,8 +120,9 @@ def test_workspace_size_grows_with_batch_and_grid(native):
     assert native.tvp_decode_workspace_bytes(0, 8, 148) == 0
     assert native.tvp_decode_workspace_bytes(4, 3, 148) == 0
     assert native.tvp_decode_workspace_bytes(4, 16, 148) == 0
-    # partials: 2 slots x 8 KV heads x (4 + 4 + 256) floats per CTA
-    assert c - b >= 148 * 2 * 8 * 264 * 4
+    # per CTA: a 16-byte start record and 2 partial slots x 8 KV heads x (4 + 4 + 256) floats
+    # (regions are rounded up to 256 bytes)
+    assert c - b >= 148 * (16 + 2 * 8 * 264 * 4) - 256
     # a head shard's workspace holds counters and partials for its heads only
     sizes = [native.tvp_decode_workspace_bytes(256, h, 148) for h in (1, 2, 4, 8)]
     assert 0 < sizes[0] < sizes[1] < sizes[2] < sizes[3] == b

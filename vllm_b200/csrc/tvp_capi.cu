@@ -250,7 +250,8 @@ int tvp_paged_prefill_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const
     return TVP_ERR_INVALID_ARGUMENT;
   if (!decode_heads_supported(kv_heads) || q_heads != kv_heads * kGroup) return TVP_ERR_UNSUPPORTED;
   if ((long long)num_layers * num_pages * kPage > 0x7fffffffLL) return TVP_ERR_UNSUPPORTED;
-  if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(q, 4) || !aligned(out, 4))
+  // q rows are read and output rows written as 16-byte vectors.
+  if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(q, 16) || !aligned(out, 16))
     return TVP_ERR_INVALID_ARGUMENT;
   if (max_q_len == 0) return TVP_OK;
   PrefillParams p;
