@@ -204,7 +204,7 @@ int tvp_greedy_argmax(const float* d_logits, int rows, int vocab, long long row_
  * caller's, exactly as for tvp_paged_decode_attention.
  *   - Returns TVP_ERR_WORKSPACE when batch and grid (num_ctas, 0 = one CTA per
  *     SM) need more than 4 MiB of workspace (with one CTA per SM of a B200:
- *     batches beyond about 40,000 rows).
+ *     batches beyond 46,968 rows with 8 KV heads).
  *   - The first call on a device resolves the array's device address on that
  *     device (cudaGetSymbolAddress); make that first call before any stream
  *     capture.

@@ -17,7 +17,7 @@ namespace {
 
 // Largest workspace the no-allocation entry point can serve.  4 MiB covers a
 // one-CTA-per-SM B200 grid (~2.5 MB of split-K partials) plus page prefix sums
-// and counters for batches of up to about 40,000 rows.  Every GPU that loads
+// and counters for batches of up to 46,968 rows (8 KV heads, 148 CTAs).  Every GPU that loads
 // this library keeps these 4 MiB resident until the process exits.
 constexpr size_t kStaticWorkspaceBytes = size_t(4) << 20;
 
