@@ -334,17 +334,42 @@ def run_ours(args, rank, world, local_rank):
     out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
     q_d, k_d, v_d = torch.empty_like(q_all), torch.empty_like(k_new), torch.empty_like(v_new)
 
+    # Copies overlap the layers as in a serving loop: layer l's inputs come in
+    # on an H2D stream and layer l waits only for them; layer l's output goes
+    # out on a D2H stream as soon as the layer is done.  The step ends on the
+    # compute stream after the last output copy, so every byte of every step
+    # is copied inside the timed region.
+    h2d_stream = torch.cuda.Stream(dev)
+    d2h_stream = torch.cuda.Stream(dev)
+    step_done = torch.cuda.Event()
+    step_done.record(stream)
+
     def e2e_step():
-        q_d.copy_(q_h, non_blocking=True)
-        k_d.copy_(k_h, non_blocking=True)
-        v_d.copy_(v_h, non_blocking=True)
+        h2d_stream.wait_event(step_done)  # the previous step no longer reads q_d, k_d, v_d
+        arrived = []
+        with torch.cuda.stream(h2d_stream):
+            for l in range(layers):
+                q_d[l].copy_(q_h[l], non_blocking=True)
+                k_d[l].copy_(k_h[l], non_blocking=True)
+                v_d[l].copy_(v_h[l], non_blocking=True)
+                arrived.append(torch.cuda.Event())
+                arrived[-1].record(h2d_stream)
         ops.decode_plan(seq_lens, stride, ws, error=err, stream=stream)
         for l in range(layers):
+            stream.wait_event(arrived[l])
             ops.rope_append(k_pool, v_pool, l, tables, positions, k_d[l], v_d[l], q=q_d[l],
                             writeback_k=False, error=err, stream=stream)
             ops.paged_decode_attention(q_d[l], k_pool, v_pool, l, tables, seq_lens, ws,
                                        out=out[l], error=err, stream=stream)
-        out_h.copy_(out, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(stream)
+            d2h_stream.wait_event(done)
+            with torch.cuda.stream(d2h_stream):
+                out_h[l].copy_(out[l], non_blocking=True)
+        sent = torch.cuda.Event()
+        sent.record(d2h_stream)
+        stream.wait_event(sent)
+        step_done.record(stream)
 
     for _ in range(2):
         e2e_step()
