@@ -246,7 +246,6 @@ class ClockSampler:
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
-    from vllm_b200 import _native as N
     from vllm_b200 import ops
 
     dev = torch.device("cuda", local_rank)

@@ -9,9 +9,8 @@ The allocator itself is the native C++ one (vllm_b200/csrc/tvp_host.cpp).
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, c_int, c_int32, c_void_p
+from ctypes import c_int, c_int32, c_void_p
 
-import numpy as np
 import torch
 
 from . import _native as N
