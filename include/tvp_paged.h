@@ -166,7 +166,8 @@ int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const 
  * (append them first with tvp_rope_append).  d_q_pos0[s] = 0 is a prompt;
  * d_q_pos0[s] = L0 > 0 a prefill chunk after L0 cached tokens.
  * q, out: [num_tokens][q_heads * 64] BF16, head-major as the reference,
- * 16-byte aligned; max_q_len >= the longest sequence's query count.
+ * 16-byte aligned; max_q_len >= the longest sequence's query count (at most
+ * 65535 x 32 tokens: TVP_ERR_UNSUPPORTED beyond).
  */
 int tvp_paged_prefill_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const tvp_bf16* v_pool,
                                 int num_pages, int num_layers, int layer, int kv_heads, int q_heads,

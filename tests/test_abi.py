@@ -101,6 +101,7 @@ def test_prefill_rejects_bad_arguments_on_host(native):
     assert call(seqs=0) == N.TVP_ERR_INVALID_ARGUMENT
     assert call(seqs=65536) == N.TVP_ERR_INVALID_ARGUMENT    # one grid row per sequence
     assert call(maxq=-1) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(maxq=65535 * 32 + 1) == N.TVP_ERR_UNSUPPORTED  # 32-token tiles beyond the grid
     assert call(scale=float("inf")) == N.TVP_ERR_INVALID_ARGUMENT
     assert call(kvh=3, qh=12) == N.TVP_ERR_UNSUPPORTED
     assert call(qh=16) == N.TVP_ERR_UNSUPPORTED

@@ -248,6 +248,7 @@ int tvp_paged_prefill_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const
       num_pages <= 0 || num_layers <= 0 || layer < 0 || layer >= num_layers || table_stride <= 0 ||
       num_seqs <= 0 || num_seqs > 65535 || max_q_len < 0 || !std::isfinite(scale))
     return TVP_ERR_INVALID_ARGUMENT;
+  if (max_q_len > 65535 * 32) return TVP_ERR_UNSUPPORTED;  // one grid row per 32-token tile
   if (!decode_heads_supported(kv_heads) || q_heads != kv_heads * kGroup) return TVP_ERR_UNSUPPORTED;
   if ((long long)num_layers * num_pages * kPage > 0x7fffffffLL) return TVP_ERR_UNSUPPORTED;
   // q rows are read and output rows written as 16-byte vectors.

@@ -87,11 +87,12 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  const int s = blockIdx.y, g = blockIdx.z;
+  const int s = blockIdx.x, g = blockIdx.y;
   const int q_begin = __ldg(p.cu_q + s), q_end = __ldg(p.cu_q + s + 1);
-  // Tiles run last-first: under causality the last tiles stream the most pages,
-  // so starting them first shortens the launch's tail.
-  const int tile = gridDim.x - 1 - blockIdx.x;
+  // Tiles run last-first: under causality the last tiles stream the most pages.
+  // The tile is the slowest grid dimension, so the longest tiles of every
+  // sequence and head start in the first wave and the short ones fill the tail.
+  const int tile = gridDim.z - 1 - blockIdx.z;
   const int tok0 = q_begin + tile * kTcTokens;
   if (tok0 >= q_end) return;  // this sequence has fewer tiles
   const int count = min(kTcTokens, q_end - tok0);
@@ -411,7 +412,7 @@ cudaError_t launch_paged_prefill(const PrefillParams& p, long long pool_rows, in
   if (!pool_tensor_map(p.k_pool, pool_rows, p.kv_heads, &k_map) ||
       !pool_tensor_map(p.v_pool, pool_rows, p.kv_heads, &v_map))
     return cudaErrorInvalidValue;
-  const dim3 grid((max_q_len + kTcTokens - 1) / kTcTokens, num_seqs, p.kv_heads);
+  const dim3 grid(num_seqs, p.kv_heads, (max_q_len + kTcTokens - 1) / kTcTokens);
   paged_prefill_kernel<<<grid, kTcThreads, prefill_smem_bytes(), stream>>>(p, k_map, v_map);
   return cudaGetLastError();
 }
