@@ -466,6 +466,7 @@ def extras(args, dev, case, k_pool, v_pool, q_all, out, tables, seq_lens, ws):
     res["long_context_head_shards"] = bench_long_context_heads(dev)
     res["prefill"] = bench_prefill(dev)
     res["decode_small"] = bench_decode_small(dev)
+    res["decode_projections"] = bench_projections(dev)
     res["e2e_llama"] = bench_e2e_llama()
     return res
 
@@ -482,7 +483,8 @@ def bench_e2e_llama():
     for name, args in (("reference", ["--engine", "ref"]),
                        ("ours_compat", ["--engine", "tvp", "--mode", "compat"]),
                        ("ours_fast", ["--engine", "tvp", "--mode", "fast"]),
-                       ("ours_batched", ["--engine", "tvp", "--mode", "batched"])):
+                       ("ours_batched", ["--engine", "tvp", "--mode", "batched"]),
+                       ("ours_native", ["--engine", "tvp", "--mode", "native"])):
         r = subprocess.run([sys.executable, str(ROOT / "tests" / "e2e_runner.py"), *args,
                             "--runs", "2"], capture_output=True, text=True, timeout=900)
         if r.returncode != 0:
@@ -491,7 +493,7 @@ def bench_e2e_llama():
         d = json.loads(r.stdout.strip().splitlines()[-1])
         out[name] = {"tok_s": round(d["tokens_generated"] / min(d["seconds"]), 1),
                      "seconds": [round(x, 3) for x in d["seconds"]]}
-    for name in ("compat", "fast", "batched"):
+    for name in ("compat", "fast", "batched", "native"):
         try:
             out[f"speedup_{name}"] = round(out[f"ours_{name}"]["tok_s"] / out["reference"]["tok_s"], 2)
         except (KeyError, TypeError, ZeroDivisionError):
@@ -786,6 +788,83 @@ def bench_decode_small(dev, iters=50):
     return res
 
 
+def bench_projections(dev, iters=20):
+    """K5 (tvp_decode_projections): one decode layer's projections of the
+    Llama-3.2-1B geometry over 4 rows (Q+K+V, O, gate+up, down: 121.6 MB of
+    BF16 weights, 4 launches) and its LM head (128256 x 2048, 525 MB, FP32
+    logits), each launch timed alone with L2 flushed before it; against torch's
+    cuBLAS BF16 GEMMs of the same shapes (the batched engine's 7 projection
+    GEMMs and its LM head GEMM).  Roofline: HBM, bytes = the weights."""
+    import torch
+    from vllm_b200 import ops
+    peak, kind = hbm_peak()
+    g = torch.Generator(device=dev).manual_seed(3)
+    H, I, KV, VOC, B = 2048, 8192, 512, 128256, 4
+
+    def w(n, k):
+        return (torch.randn(n, k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+
+    x = torch.randn(B, H, generator=g, device=dev).to(torch.bfloat16)
+    xi = torch.randn(B, I, generator=g, device=dev).to(torch.bfloat16)
+    wq, wk, wv, wo, wg, wu, wd = w(H, H), w(KV, H), w(KV, H), w(H, H), w(I, H), w(I, H), w(H, I)
+    emb = w(VOC, H)
+    o = lambda n, dt=torch.bfloat16: torch.empty(B, n, dtype=dt, device=dev)
+    oq, ok, ov, oo, og, ou, od, ol = o(H), o(KV), o(KV), o(H), o(I), o(I), o(H), o(VOC, torch.float32)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def timed(fn):
+        times = []
+        for i in range(iters + 3):
+            flush.fill_(i & 0xFF)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize(dev)
+            if i >= 3:
+                times.append(a.elapsed_time(b))
+        return statistics.median(times) * 1e3  # us
+
+    layer = {
+        "qkv": (lambda: ops.decode_projections(x, [wq, wk, wv], outs=[oq, ok, ov]), [wq, wk, wv]),
+        "o": (lambda: ops.decode_projections(x, [wo], outs=[oo]), [wo]),
+        "gate_up": (lambda: ops.decode_projections(x, [wg, wu], outs=[og, ou]), [wg, wu]),
+        "down": (lambda: ops.decode_projections(xi, [wd], outs=[od]), [wd]),
+    }
+    cublas = {
+        "qkv": lambda: (torch.mm(x, wq.t(), out=oq), torch.mm(x, wk.t(), out=ok),
+                        torch.mm(x, wv.t(), out=ov)),
+        "o": lambda: torch.mm(x, wo.t(), out=oo),
+        "gate_up": lambda: (torch.mm(x, wg.t(), out=og), torch.mm(x, wu.t(), out=ou)),
+        "down": lambda: torch.mm(xi, wd.t(), out=od),
+    }
+    res = {"workload": "Llama-3.2-1B decode projections, 4 rows, BF16 weights, L2 flushed",
+           "roofline": "hbm; bytes = weights read", "peak_source": kind}
+    tot_ours = tot_lib = tot_bytes = 0.0
+    for name, (fn, ws) in layer.items():
+        nbytes = sum(t.numel() * 2 for t in ws)
+        us, lib_us = timed(fn), timed(cublas[name])
+        tot_ours += us
+        tot_lib += lib_us
+        tot_bytes += nbytes
+        res[name] = {"us": round(us, 2), "GBps": round(nbytes / us / 1e3, 1),
+                     "frac_of_peak": round(nbytes / us / 1e3 / peak, 4),
+                     "cublas_us": round(lib_us, 2)}
+    res["layer"] = {"us": round(tot_ours, 2), "bytes": int(tot_bytes),
+                    "GBps": round(tot_bytes / tot_ours / 1e3, 1),
+                    "frac_of_peak": round(tot_bytes / tot_ours / 1e3 / peak, 4),
+                    "cublas_us": round(tot_lib, 2),
+                    "speedup_vs_cublas": round(tot_lib / tot_ours, 2)}
+    nb = emb.numel() * 2
+    us = timed(lambda: ops.decode_projections(x, [emb], outs=[ol], out_f32=True))
+    olb = o(VOC)
+    lib_us = timed(lambda: torch.mm(x, emb.t(), out=olb))
+    res["lm_head"] = {"us": round(us, 2), "GBps": round(nb / us / 1e3, 1),
+                      "frac_of_peak": round(nb / us / 1e3 / peak, 4),
+                      "cublas_bf16_out_us": round(lib_us, 2)}
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -798,7 +877,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--only", choices=["long_context", "long_context_heads", "decode_small",
-                                       "prefill", "e2e"],
+                                       "prefill", "e2e", "projections"],
                     help="run one single-GPU sub-measurement alone and print its JSON (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -815,7 +894,7 @@ def main():
         torch.cuda.set_device(dev)
         fn = {"long_context": bench_long_context, "long_context_heads": bench_long_context_heads,
               "decode_small": bench_decode_small, "prefill": bench_prefill,
-              "e2e": lambda _dev: bench_e2e_llama()}[args.only]
+              "e2e": lambda _dev: bench_e2e_llama(), "projections": bench_projections}[args.only]
         print(json.dumps({args.only: fn(dev)}), flush=True)
         return
     import torch

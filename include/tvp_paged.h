@@ -194,6 +194,29 @@ int tvp_greedy_argmax(const float* d_logits, int rows, int vocab, long long row_
                       tvp_stream_t stream);
 
 /*
+ * K5 — the decode step's weight projections over 1-8 rows, several matrices
+ * that share the input rows in one launch.
+ *
+ * Replaces the cublasGemmEx projections of the reference's decode step:
+ * outputProjection / qProjection / kProjection / vProjection
+ * (src/model/attention.cu:194-323), gateProjection / upProjection /
+ * downProjection (src/model/mlp.cu:8-102) and lmHeadProjection
+ * (src/model/lm_head.cu:8-36), called there once per row in decode.  Same
+ * operands and math: for i < count,
+ *     out[i][t][n] = sum_k w[i][n][k] x[t][k],   t < rows, n < n[i],
+ * x: [rows][k] BF16; w[i]: [n[i]][k] BF16 (the reference's weight layout);
+ * out[i]: [rows][n[i]] BF16 (out_f32 = 0) or FP32 (out_f32 = 1); FP32
+ * accumulation, the sum over k in a fixed order (results do not vary from run
+ * to run), rounded once.  w, n and out are HOST arrays of `count` (1..3)
+ * entries.  rows 1..8; k a multiple of 256; every n[i] a multiple of 16; x and
+ * w[i] 16-byte aligned, out[i] aligned to its element.  No workspace, no
+ * synchronisation: the launch goes on `stream`.
+ */
+#define TVP_PROJ_MAX 3
+int tvp_decode_projections(const tvp_bf16* x, int rows, int k, int count, const tvp_bf16* const* w,
+                           const int* n, void* const* out, int out_f32, tvp_stream_t stream);
+
+/*
  * K2 without any allocation.  This entry point has no counterpart in the
  * reference.  It is for callers that cannot call cudaMalloc: code whose
  * device memory is owned by a host framework's pool, plug-ins running under a

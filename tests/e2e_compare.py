@@ -52,7 +52,8 @@ def compare() -> dict:
     results = {}
     for name, args in {"ref": ["--engine", "ref"], "compat": ["--engine", "tvp", "--mode", "compat"],
                        "fast": ["--engine", "tvp", "--mode", "fast"],
-                       "batched": ["--engine", "tvp", "--mode", "batched"]}.items():
+                       "batched": ["--engine", "tvp", "--mode", "batched"],
+                       "native": ["--engine", "tvp", "--mode", "native"]}.items():
         path = tmp / f"{name}.npy"
         results[name] = runner([*args, "--teacher-forced", str(tmp / "forced.json"),
                                 "--logits-out", str(path)])
@@ -69,7 +70,7 @@ def compare() -> dict:
         top = b[top_tok]
         return float((top - b[other_tok]) / bf16_ulp(np.array([top]))[0])
 
-    for name in ("compat", "fast", "batched"):
+    for name in ("compat", "fast", "batched", "native"):
         ours = np.array(results[name]["step_tokens"])
         agree = ours == rtok
         gaps = []

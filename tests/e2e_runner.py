@@ -32,7 +32,7 @@ def prompts(requests: int, length: int, seed: int) -> np.ndarray:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--engine", choices=sorted(LIBS), required=True)
-    ap.add_argument("--mode", choices=["compat", "fast", "batched"], default="compat")
+    ap.add_argument("--mode", choices=["compat", "fast", "batched", "native"], default="compat")
     ap.add_argument("--requests", type=int, default=4)
     ap.add_argument("--prompt", type=int, default=128)
     ap.add_argument("--new", type=int, default=128)

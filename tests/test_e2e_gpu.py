@@ -31,13 +31,14 @@ def test_reference_engine_is_deterministic_under_teacher_forcing(summary):
     assert summary["reference_free_running_matches_teacher_forced"]
 
 
-@pytest.mark.parametrize("mode", ["compat", "fast", "batched"])
+@pytest.mark.parametrize("mode", ["compat", "fast", "batched", "native"])
 def test_dropped_in_path_matches_reference_up_to_bf16_ties(summary, mode):
     """batched: fast's attention and prefill, plus the decode projections and
     LM head as one GEMM over the batch, the greedy tokens from one batched
     argmax launch, and the step replayed as a CUDA graph.  Its GEMMs may sum in
     another order than the one-row GEMMs, so it is held to fast's near-tie
-    policy."""
+    policy.  native: batched with the projections and the LM head on
+    tvp_decode_projections, another summation order again: the same policy."""
     s = summary[mode]
     if mode == "compat":
         assert s["first_tokens_match"]      # prefill: RoPE + pages bit-exact, reference attention

@@ -77,6 +77,8 @@ _SIGNATURES = {
     "tvp_greedy_argmax_workspace_bytes": (c_size_t, [c_int]),
     "tvp_greedy_argmax": (c_int, [c_void_p, c_int, c_int, ctypes.c_longlong, c_void_p, c_void_p,
                                   c_size_t, c_void_p]),
+    "tvp_decode_projections": (c_int, [c_void_p, c_int, c_int, c_int, POINTER(c_void_p),
+                                       POINTER(c_int), POINTER(c_void_p), c_int, c_void_p]),
     "tvp_head_gather_create": (c_int, [c_int, c_int, c_int, c_int, POINTER(c_void_p)]),
     "tvp_head_gather_export": (c_int, [c_void_p, c_void_p]),
     "tvp_head_gather_connect": (c_int, [c_void_p, c_void_p]),

@@ -26,7 +26,8 @@ LIB = LIB_DIR / "libtvp_paged.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 SOURCES = ["tvp_append.cu", "tvp_decode.cu", "tvp_decode_heads.cu", "tvp_compat.cu", "tvp_capi.cu", "tvp_host.cpp",
-           "tvp_noalloc.cu", "tvp_gather.cu", "tvp_prefill.cu", "tvp_argmax.cu"]
+           "tvp_noalloc.cu", "tvp_gather.cu", "tvp_prefill.cu", "tvp_argmax.cu",
+           "tvp_project.cu"]
 
 
 def nvcc() -> str:

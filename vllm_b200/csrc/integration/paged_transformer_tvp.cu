@@ -33,12 +33,18 @@
 //                     calls (argmax.cu:83-105).  The batched GEMMs sum in
 //                     another order than the one-row ones, so this mode has
 //                     its own parity policy (near-ties only, as fast).
+//   native            batched, with every projection and the LM head on
+//                     tvp_decode_projections (Q, K and V in one launch, gate
+//                     and up in one launch) instead of cuBLAS: the same
+//                     operands and FP32 accumulation, another summation order,
+//                     so fast's parity policy again.
 #include <cublas_v2.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
+#include <initializer_list>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -96,6 +102,7 @@ struct PathState {
   size_t argmax_workspace_bytes = 0;
   int mode = TVP_MODE_COMPAT;
   bool batched = false;
+  bool native_proj = false;  // native mode: projections on tvp_decode_projections
   // Batched mode: the decode step runs on `stream` (a blocking stream, so it
   // is ordered after the engine's legacy-stream work) as a CUDA graph per
   // batch size, captured on the second step that uses the same buffers.
@@ -132,7 +139,8 @@ PathState& path_state() {
     if (st.workspace_bytes == 0) throw std::runtime_error("decode workspace size query failed");
     check_cuda(cudaMalloc(&st.workspace, st.workspace_bytes));
     const std::string mode = std::getenv("TVP_DECODE_MODE") ? std::getenv("TVP_DECODE_MODE") : "";
-    st.batched = mode == "batched";
+    st.native_proj = mode == "native";
+    st.batched = mode == "batched" || st.native_proj;
     st.mode = (mode == "fast" || st.batched) ? TVP_MODE_FAST : TVP_MODE_COMPAT;
     if (st.batched) {
       check_cuda(cudaStreamCreate(&st.stream));
@@ -278,6 +286,22 @@ std::vector<int> decodeBatchPaged(cublasHandle_t cublas_handle, __nv_bfloat16* h
     for (int row = 0; row < batch; ++row)
       projection(cublas_handle, in + row * in_dim, w, out + row * out_dim, 1);
   };
+  // Native mode: up to three projections of the same rows in one launch.
+  auto native = [&](const __nv_bfloat16* in, int in_dim,
+                    std::initializer_list<const __nv_bfloat16*> ws, std::initializer_list<int> ns,
+                    std::initializer_list<__nv_bfloat16*> outs) {
+    const tvp_bf16* w[TVP_PROJ_MAX];
+    int n[TVP_PROJ_MAX];
+    void* out[TVP_PROJ_MAX];
+    int count = 0;
+    for (auto* p : ws) w[count++] = reinterpret_cast<const tvp_bf16*>(p);
+    count = 0;
+    for (int v : ns) n[count++] = v;
+    count = 0;
+    for (auto* p : outs) out[count++] = p;
+    check_tvp(tvp_decode_projections(reinterpret_cast<const tvp_bf16*>(in), batch, in_dim, count,
+                                     w, n, out, 0, st.stream));
+  };
   // The step's device work on `stream`; nullptr is the legacy default stream,
   // where the reference's own op wrappers are called.
   auto enqueue = [&](cudaStream_t stream) {
@@ -290,9 +314,14 @@ std::vector<int> decodeBatchPaged(cublasHandle_t cublas_handle, __nv_bfloat16* h
     for (int layer = 0; layer < kLayers; ++layer) {
       const LayerWeights& lw = weights.layers[layer];
       rmsNormKernel<<<batch, 1024, 0, stream>>>(hidden_states, buffers.rms_output, lw.input_norm);
-      project(qProjection, buffers.rms_output, kHidden, lw.w_q, buffers.q, kHidden);
-      project(kProjection, buffers.rms_output, kHidden, lw.w_k, buffers.k, 512);
-      project(vProjection, buffers.rms_output, kHidden, lw.w_v, buffers.v, 512);
+      if (st.native_proj) {
+        native(buffers.rms_output, kHidden, {lw.w_q, lw.w_k, lw.w_v}, {kHidden, 512, 512},
+               {buffers.q, buffers.k, buffers.v});
+      } else {
+        project(qProjection, buffers.rms_output, kHidden, lw.w_q, buffers.q, kHidden);
+        project(kProjection, buffers.rms_output, kHidden, lw.w_k, buffers.k, 512);
+        project(vProjection, buffers.rms_output, kHidden, lw.w_v, buffers.v, 512);
+      }
       check_tvp(tvp_rope_append(reinterpret_cast<tvp_bf16*>(cache.k_blocks),
                                 reinterpret_cast<tvp_bf16*>(cache.v_blocks), cache.num_blocks,
                                 kLayers, layer, kKvHeads, d_tables, kTableStride, batch, nullptr,
@@ -308,22 +337,39 @@ std::vector<int> decodeBatchPaged(cublasHandle_t cublas_handle, __nv_bfloat16* h
           kKvHeads, kQHeads, d_tables, kTableStride, d_len, batch, 0.125f, st.mode, 0,
           st.workspace, st.workspace_bytes, reinterpret_cast<tvp_bf16*>(buffers.attn_output),
           st.error, stream));
-      project(outputProjection, buffers.attn_output, kHidden, lw.w_o, buffers.o_output, kHidden);
+      if (st.native_proj)
+        native(buffers.attn_output, kHidden, {lw.w_o}, {kHidden}, {buffers.o_output});
+      else
+        project(outputProjection, buffers.attn_output, kHidden, lw.w_o, buffers.o_output, kHidden);
       residual(buffers.o_output);
       rmsNormKernel<<<batch, 1024, 0, stream>>>(hidden_states, buffers.rms_output,
                                                 lw.post_attention_norm);
-      project(gateProjection, buffers.rms_output, kHidden, lw.w_gate, buffers.gate, 8192);
-      project(upProjection, buffers.rms_output, kHidden, lw.w_up, buffers.up, 8192);
+      if (st.native_proj) {
+        native(buffers.rms_output, kHidden, {lw.w_gate, lw.w_up}, {8192, 8192},
+               {buffers.gate, buffers.up});
+      } else {
+        project(gateProjection, buffers.rms_output, kHidden, lw.w_gate, buffers.gate, 8192);
+        project(upProjection, buffers.rms_output, kHidden, lw.w_up, buffers.up, 8192);
+      }
       if (stream) siluKernel<<<batch, 1024, 0, stream>>>(buffers.gate, buffers.up);
       else silu(buffers.gate, buffers.up, batch);
-      project(downProjection, buffers.gate, 8192, lw.w_down, buffers.down, kHidden);
+      if (st.native_proj)
+        native(buffers.gate, 8192, {lw.w_down}, {kHidden}, {buffers.down});
+      else
+        project(downProjection, buffers.gate, 8192, lw.w_down, buffers.down, kHidden);
       residual(buffers.down);
     }
     rmsNormKernel<<<batch, 1024, 0, stream>>>(hidden_states, buffers.rms_output, weights.final_norm);
     if (!st.batched) return;
     // The LM head of lm_head.cu:8-36 over all rows: logits[row] = E h_row.
     const float alpha = 1.0f, beta = 0.0f;
-    if (cublasGemmEx(cublas_handle, CUBLAS_OP_T, CUBLAS_OP_N, VOCAB_SIZE, batch, kHidden, &alpha,
+    if (st.native_proj) {
+      const tvp_bf16* w = reinterpret_cast<const tvp_bf16*>(weights.embedding);
+      const int n = VOCAB_SIZE;
+      void* out = logits;
+      check_tvp(tvp_decode_projections(reinterpret_cast<const tvp_bf16*>(buffers.rms_output),
+                                       batch, kHidden, 1, &w, &n, &out, 1, stream));
+    } else if (cublasGemmEx(cublas_handle, CUBLAS_OP_T, CUBLAS_OP_N, VOCAB_SIZE, batch, kHidden, &alpha,
                      weights.embedding, CUDA_R_16BF, kHidden, buffers.rms_output, CUDA_R_16BF,
                      kHidden, &beta, logits, CUDA_R_32F, VOCAB_SIZE, CUBLAS_COMPUTE_32F,
                      CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)

@@ -1,0 +1,170 @@
+// K5 — the decode step's weight projections over a small batch of rows.
+//
+// Replaces the projection GEMMs of a decode step: outputProjection, qProjection,
+// kProjection, vProjection (src/model/attention.cu:194-323), gateProjection,
+// upProjection, downProjection (src/model/mlp.cu:8-102) and lmHeadProjection
+// (src/model/lm_head.cu:8-36).
+// Each is a cublasGemmEx with W in the reference's layout, [n_out][k] BF16
+// (k contiguous, op T), the rows [rows][k] BF16 (op N), FP32 accumulation and
+// a BF16 (FP32 for the LM head) result [rows][n_out]:
+//     out[t][n] = sum_k W[n][k] x[t][k].
+// With 1-8 rows the work is a stream over the weights (121.6 MB per layer of a
+// Llama-3.2-1B geometry, 525 MB for its LM head), so the roofline is HBM.
+//
+// Design:
+//  * One CTA per 16 weight rows; its warps split k into equal slices.  Several
+//    matrices that share the input rows (Q, K and V; gate and up) run in one
+//    launch: the CTAs of matrix i follow those of matrix i - 1.
+//  * A lane loads 16 B of weight row r and of row r + 8 and 16 B of input row
+//    t = lane / 4 per 32-column block, straight from global memory (weights
+//    bypass L1: they are read once), and feeds them to two m16n8k16 BF16
+//    tensor-core MMAs.  The dot product does not depend on which k goes to
+//    which MMA slot as long as the weight and the input use the same slot, so
+//    the lane's 8 contiguous k fill its 4 k-slots of two MMAs: no shared-memory
+//    staging and no shuffles.  Input rows t >= rows are zero columns.
+//  * The warps' 16 x 8 FP32 partial tiles are summed in shared memory in warp
+//    order, so the result does not depend on timing (deterministic), then
+//    rounded once to the output type.
+#include <cuda_bf16.h>
+
+#include "tvp_common.cuh"
+
+namespace tvp {
+namespace {
+
+constexpr int kProjRows = 16;      // weight rows per CTA (the MMA's M)
+constexpr int kProjMaxTokens = 8;  // input rows (the MMA's N)
+constexpr int kProjBlock = 32;     // k columns per lane step (two MMAs)
+constexpr int kProjUnroll = 8;     // blocks whose loads are in flight together
+
+struct ProjParams {
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* w[TVP_PROJ_MAX];
+  void* out[TVP_PROJ_MAX];
+  int n[TVP_PROJ_MAX];
+  int cta_end[TVP_PROJ_MAX];  // prefix sums of n / 16
+  int count, rows, k, out_f32;
+};
+
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+template <int kWarps>
+__global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
+    decode_projection_kernel(const ProjParams p) {
+  __shared__ float red[kWarps][4][32];
+  // This CTA's matrix, selected with constant indices (a runtime index into
+  // the parameter arrays would copy them to local memory).
+  const __nv_bfloat16* w = p.w[0];
+  void* out = p.out[0];
+  int n_out = p.n[0], first = 0;
+#pragma unroll
+  for (int i = 1; i < TVP_PROJ_MAX; ++i)
+    if (i < p.count && (int)blockIdx.x >= p.cta_end[i - 1]) {
+      w = p.w[i];
+      out = p.out[i];
+      n_out = p.n[i];
+      first = p.cta_end[i - 1];
+    }
+  const int group = blockIdx.x - first;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int slice = p.k / kWarps;  // a multiple of kProjBlock
+  const int k0 = warp * slice + 8 * q;
+  const __nv_bfloat16* wa = w + (size_t)(group * kProjRows + g) * p.k + k0;
+  const __nv_bfloat16* wb = wa + (size_t)8 * p.k;
+  const bool has_x = g < p.rows;
+  const __nv_bfloat16* xr = p.x + (size_t)(has_x ? g : 0) * p.k + k0;
+
+  float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
+  const int blocks = slice / kProjBlock;
+  for (int b0 = 0; b0 < blocks; b0 += kProjUnroll) {
+    uint4 va[kProjUnroll], vb[kProjUnroll], vx[kProjUnroll];
+#pragma unroll
+    for (int i = 0; i < kProjUnroll; ++i) {
+      if (b0 + i < blocks) {
+        const int off = (b0 + i) * kProjBlock;
+        va[i] = ld_stream_v4(wa + off);
+        vb[i] = ld_stream_v4(wb + off);
+        vx[i] = has_x ? __ldg(reinterpret_cast<const uint4*>(xr + off)) : make_uint4(0, 0, 0, 0);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kProjUnroll; ++i) {
+      if (b0 + i < blocks) {
+        // k 8q + 0..3 of the block in the first MMA, 8q + 4..7 in the second
+        mma_bf16_16816(c0, c1, c2, c3, va[i].x, vb[i].x, va[i].y, vb[i].y, vx[i].x, vx[i].y);
+        mma_bf16_16816(c0, c1, c2, c3, va[i].z, vb[i].z, va[i].w, vb[i].w, vx[i].z, vx[i].w);
+      }
+    }
+  }
+  red[warp][0][lane] = c0;
+  red[warp][1][lane] = c1;
+  red[warp][2][lane] = c2;
+  red[warp][3][lane] = c3;
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    const int r = threadIdx.x >> 5, ln = threadIdx.x & 31;
+    float s = 0.f;
+#pragma unroll
+    for (int wi = 0; wi < kWarps; ++wi) s += red[wi][r][ln];
+    // accumulator r of lane ln: weight row (ln / 4) + 8 (r / 2), input row 2 (ln % 4) + r % 2
+    const int row = group * kProjRows + (ln >> 2) + ((r & 2) ? 8 : 0);
+    const int t = 2 * (ln & 3) + (r & 1);
+    if (t < p.rows) {
+      if (p.out_f32)
+        static_cast<float*>(out)[(size_t)t * n_out + row] = s;
+      else
+        static_cast<__nv_bfloat16*>(out)[(size_t)t * n_out + row] = __float2bfloat16_rn(s);
+    }
+  }
+}
+
+}  // namespace
+}  // namespace tvp
+
+using namespace tvp;
+
+extern "C" {
+
+int tvp_decode_projections(const tvp_bf16* x, int rows, int k, int count, const tvp_bf16* const* w,
+                           const int* n, void* const* out, int out_f32, tvp_stream_t stream) {
+  if (!x || !w || !n || !out || rows < 1 || rows > kProjMaxTokens || count < 1 ||
+      count > TVP_PROJ_MAX || k < 256 || k % 256 != 0 || (out_f32 != 0 && out_f32 != 1) ||
+      (reinterpret_cast<uintptr_t>(x) & 15u))
+    return TVP_ERR_INVALID_ARGUMENT;
+  ProjParams p{};
+  p.x = reinterpret_cast<const __nv_bfloat16*>(x);
+  p.count = count;
+  p.rows = rows;
+  p.k = k;
+  p.out_f32 = out_f32;
+  long long ctas = 0;
+  for (int i = 0; i < count; ++i) {
+    if (!w[i] || !out[i] || n[i] < kProjRows || n[i] % kProjRows != 0 ||
+        (reinterpret_cast<uintptr_t>(w[i]) & 15u) ||
+        (reinterpret_cast<uintptr_t>(out[i]) & (out_f32 ? 3u : 1u)))
+      return TVP_ERR_INVALID_ARGUMENT;
+    ctas += n[i] / kProjRows;
+    if (ctas > 0x7fffffffLL) return TVP_ERR_UNSUPPORTED;
+    p.w[i] = reinterpret_cast<const __nv_bfloat16*>(w[i]);
+    p.out[i] = out[i];
+    p.n[i] = n[i];
+    p.cta_end[i] = (int)ctas;
+  }
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // 16 warps (one CTA per SM) when each of 8 warps would stream more than
+  // 512 columns, so that long rows keep enough loads in flight per SM.
+  if (k > 4096 && k % 512 == 0)
+    decode_projection_kernel<16><<<(unsigned)ctas, 16 * 32, 0, s>>>(p);
+  else
+    decode_projection_kernel<8><<<(unsigned)ctas, 8 * 32, 0, s>>>(p);
+  return cudaGetLastError() == cudaSuccess ? TVP_OK : TVP_ERR_RUNTIME;
+}
+
+}  // extern "C"

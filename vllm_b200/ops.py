@@ -230,3 +230,41 @@ def greedy_argmax(logits, out=None, workspace=None, stream=None):
                                _stream(stream))
     N.check(rc, "tvp_greedy_argmax")
     return out
+
+
+def decode_projections(x, weights, outs=None, out_f32=False, stream=None):
+    """The decode step's projections of 1-8 rows by up to three weight matrices
+    that share them, in one launch: outs[i][t] = weights[i] @ x[t].
+
+    x: BF16 [rows, k] (k a multiple of 256); weights[i]: BF16 [n_i, k] (n_i a
+    multiple of 16), the reference's weight layout; outs[i]: [rows, n_i], BF16,
+    or FP32 when ``out_f32`` (the LM head).  FP32 accumulation in a fixed
+    order, one rounding.  Returns the list of outputs."""
+    lib = N.load()
+    weights = list(weights)
+    dev = x.device
+    _need(x, "x", torch.bfloat16, dev)
+    if x.dim() != 2:
+        raise ValueError("x must be [rows, k]")
+    rows, k = x.shape
+    if not 1 <= len(weights) <= 3:
+        raise ValueError("one to three weight matrices")
+    odt = torch.float32 if out_f32 else torch.bfloat16
+    for i, w in enumerate(weights):
+        _need(w, f"weights[{i}]", torch.bfloat16, dev)
+        if w.dim() != 2 or w.shape[1] != k:
+            raise ValueError(f"weights[{i}] must be [n, {k}]")
+    if outs is None:
+        outs = [torch.empty(rows, w.shape[0], dtype=odt, device=dev) for w in weights]
+    for i, (o, w) in enumerate(zip(outs, weights)):
+        _need(o, f"outs[{i}]", odt, dev)
+        if tuple(o.shape) != (rows, w.shape[0]):
+            raise ValueError(f"outs[{i}] must be [{rows}, {w.shape[0]}]")
+    cnt = len(weights)
+    wp = (ctypes.c_void_p * cnt)(*[w.data_ptr() for w in weights])
+    op = (ctypes.c_void_p * cnt)(*[o.data_ptr() for o in outs])
+    ns = (ctypes.c_int * cnt)(*[w.shape[0] for w in weights])
+    rc = lib.tvp_decode_projections(_ptr(x), rows, k, cnt, wp, ns, op, int(bool(out_f32)),
+                                    _stream(stream))
+    N.check(rc, "tvp_decode_projections")
+    return outs
