@@ -813,17 +813,19 @@ def bench_projections(dev, iters=20):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
     def timed(fn):
-        times = []
+        # Every iteration is enqueued before one synchronisation, so the host's
+        # launch overhead never leaves the GPU idle between the events (the
+        # 256 MB flush before each launch keeps the host ahead).
+        ev = []
         for i in range(iters + 3):
             flush.fill_(i & 0xFF)
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
             fn()
             b.record()
-            torch.cuda.synchronize(dev)
-            if i >= 3:
-                times.append(a.elapsed_time(b))
-        return statistics.median(times) * 1e3  # us
+            ev.append((a, b))
+        torch.cuda.synchronize(dev)
+        return statistics.median(a.elapsed_time(b) for a, b in ev[3:]) * 1e3  # us
 
     layer = {
         "qkv": (lambda: ops.decode_projections(x, [wq, wk, wv], outs=[oq, ok, ov]), [wq, wk, wv]),
@@ -856,7 +858,7 @@ def bench_projections(dev, iters=20):
                     "cublas_us": round(tot_lib, 2),
                     "speedup_vs_cublas": round(tot_lib / tot_ours, 2)}
     nb = emb.numel() * 2
-    us = timed(lambda: ops.decode_projections(x, [emb], outs=[ol], out_f32=True))
+    us = timed(lambda: ops.decode_projections(x, [emb], outs=[ol], epilogue="f32"))
     olb = o(VOC)
     lib_us = timed(lambda: torch.mm(x, emb.t(), out=olb))
     res["lm_head"] = {"us": round(us, 2), "GBps": round(nb / us / 1e3, 1),

@@ -203,18 +203,32 @@ int tvp_greedy_argmax(const float* d_logits, int rows, int vocab, long long row_
  * downProjection (src/model/mlp.cu:8-102) and lmHeadProjection
  * (src/model/lm_head.cu:8-36), called there once per row in decode.  Same
  * operands and math: for i < count,
- *     out[i][t][n] = sum_k w[i][n][k] x[t][k],   t < rows, n < n[i],
+ *     y[i][t][n] = sum_k w[i][n][k] x[t][k],   t < rows, n < n[i],
  * x: [rows][k] BF16; w[i]: [n[i]][k] BF16 (the reference's weight layout);
- * out[i]: [rows][n[i]] BF16 (out_f32 = 0) or FP32 (out_f32 = 1); FP32
- * accumulation, the sum over k in a fixed order (results do not vary from run
- * to run), rounded once.  w, n and out are HOST arrays of `count` (1..3)
- * entries.  rows 1..8; k a multiple of 256; every n[i] a multiple of 16; x and
- * w[i] 16-byte aligned, out[i] aligned to its element.  No workspace, no
+ * FP32 accumulation, the sum over k in a fixed order (results do not vary
+ * from run to run).  `epilogue` says what is stored:
+ *   TVP_PROJ_BF16      out[i] = bf16(y[i])                    [rows][n[i]] BF16
+ *   TVP_PROJ_F32       out[i] = y[i]  (the LM head's logits)   [rows][n[i]] FP32
+ *   TVP_PROJ_RESIDUAL  out[i] = out[i] + bf16(y[i]) as one BF16 add: the
+ *                      projection followed by residualAdd
+ *                      (src/model/resConnection.cu:6-17), bit for bit
+ *   TVP_PROJ_SWIGLU    count = 2, n[0] = n[1]: out[0] =
+ *                      bf16(g (1 / (1 + expf(-g))) u), g = bf16(y[0]),
+ *                      u = bf16(y[1]): gate and up projections followed by
+ *                      silu (src/model/SiLU.cu:5-16), bit for bit; out[1] is
+ *                      not used (may be null)
+ * w, n and out are HOST arrays of `count` (1..3) entries.  rows 1..8; k a
+ * multiple of 256; every n[i] a multiple of 16; x and w[i] 16-byte aligned,
+ * out[i] aligned to its element and not overlapping x.  No workspace, no
  * synchronisation: the launch goes on `stream`.
  */
 #define TVP_PROJ_MAX 3
+#define TVP_PROJ_BF16 0
+#define TVP_PROJ_F32 1
+#define TVP_PROJ_RESIDUAL 2
+#define TVP_PROJ_SWIGLU 3
 int tvp_decode_projections(const tvp_bf16* x, int rows, int k, int count, const tvp_bf16* const* w,
-                           const int* n, void* const* out, int out_f32, tvp_stream_t stream);
+                           const int* n, void* const* out, int epilogue, tvp_stream_t stream);
 
 /*
  * K2 without any allocation.  This entry point has no counterpart in the

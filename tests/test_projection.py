@@ -40,7 +40,15 @@ def test_projection_entry_point_checks_arguments(lib):
     assert call(lib, outs=(0,)) == bad
     assert call(lib, outs=(0x3001,)) == bad                 # BF16 output misaligned
     assert call(lib, outs=(0x3002,), f32=1) == bad          # FP32 output misaligned
-    assert call(lib, f32=2) == bad
+    assert call(lib, f32=4) == bad                          # epilogue 0..3
+    assert call(lib, f32=-1) == bad
+    # SwiGLU: exactly two matrices of one shape
+    assert call(lib, f32=3) == bad
+    assert call(lib, ws=(0x2000, 0x4000), ns=(2048, 1024), outs=(0x3000, 0), f32=3) == bad
+    assert call(lib, ws=(0x2000, 0x4000, 0x5000), ns=(16,) * 3, outs=(0x3000,) * 3, f32=3) == bad
+    # an output overlapping the input rows
+    assert call(lib, x=0x100000, outs=(0x100000 + 2 * 4 * 2048 - 16,)) == bad
+    assert call(lib, x=0x100000, outs=(0x100000 - 2 * 4 * 2048 + 2,)) == bad
     assert call(lib, ws=(0x2000, 0x2008), ns=(16, 16), outs=(0x3000, 0x4000)) == bad
 
 

@@ -6,11 +6,21 @@ src/model/mlp.cu:8-102, src/model/lm_head.cu:8-36).
 Tolerance: the exact sum rounded once, so the FP32 result may differ from
 the FP32 reference by the accumulation error, bounded here by 1e-4 of the
 sum of |products|, and a BF16 result additionally by one BF16 rounding
-(2^-8 relative).  Results must be bitwise identical from call to call."""
+(2^-8 relative).  Results must be bitwise identical from call to call.
+
+The fused epilogues must equal, bit for bit, the reference's own residualAdd
+and silu kernels (src/model/resConnection.cu:6-17, src/model/SiLU.cu:5-16, run
+from the reference engine compiled under oracle/_ref) applied to the
+projection's BF16 result."""
+import ctypes
+from pathlib import Path
+
 import pytest
 import torch
 
 from vllm_b200 import ops
+
+ROOT = Path(__file__).resolve().parents[1]
 
 pytestmark = pytest.mark.gpu
 
@@ -48,8 +58,8 @@ def test_projection_matches_fp32_reference(rows, k, ns):
 
 def test_lm_head_form_fp32_output_and_determinism():
     x, (w,) = make(4, 2048, [4096], seed=7)
-    a = ops.decode_projections(x, [w], out_f32=True)[0]
-    b = ops.decode_projections(x, [w], out_f32=True)[0]
+    a = ops.decode_projections(x, [w], epilogue="f32")[0]
+    b = ops.decode_projections(x, [w], epilogue="f32")[0]
     torch.cuda.synchronize()
     check(x, w, a, f32=True)
     assert torch.equal(a, b)
@@ -71,3 +81,49 @@ def test_matches_cublas_bf16_gemm_closely():
     lib = (x @ ws[0].t()).float()  # torch's cuBLAS BF16 GEMM, FP32 accumulation
     torch.cuda.synchronize()
     assert float((ours - lib).abs().max()) <= 2.0 ** -7 * float(lib.abs().max())
+
+
+@pytest.fixture(scope="module")
+def reference_engine():
+    path = ROOT / "oracle" / "_ref" / "libtvp_e2e_ref.so"
+    if not path.exists():
+        pytest.skip("reference engine not built (make -C oracle e2e)")
+    lib = ctypes.CDLL(str(path))
+    for name in ("_Z4siluP13__nv_bfloat16S0_i", "_Z11residualAddP13__nv_bfloat16S0_i"):
+        getattr(lib, name).argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+        getattr(lib, name).restype = None
+    return lib
+
+
+@pytest.mark.parametrize("rows", [1, 4, 8])
+@pytest.mark.parametrize("k", [2048, 8192])  # O projection, down projection
+def test_residual_epilogue_is_the_reference_residual_add(reference_engine, rows, k):
+    x, (w,) = make(rows, k, [2048], seed=40 + rows + k)
+    g = torch.Generator(device="cuda").manual_seed(rows)
+    hidden = torch.randn(rows, 2048, generator=g, device="cuda").to(torch.bfloat16)
+    y = ops.decode_projections(x, [w])[0]
+    expect = hidden.clone()
+    torch.cuda.synchronize()
+    # residualAdd(hidden, y, rows) launches on the legacy default stream
+    reference_engine._Z11residualAddP13__nv_bfloat16S0_i(expect.data_ptr(), y.data_ptr(), rows)
+    torch.cuda.synchronize()
+    got = hidden.clone()
+    ops.decode_projections(x, [w], outs=[got], epilogue="residual")
+    torch.cuda.synchronize()
+    assert torch.equal(got, expect)
+    assert not torch.equal(got, hidden)
+
+
+@pytest.mark.parametrize("rows", [1, 4, 8])
+def test_swiglu_epilogue_is_the_reference_silu(reference_engine, rows):
+    x, (wg, wu) = make(rows, 2048, [8192, 8192], seed=60 + rows)
+    gate, up = ops.decode_projections(x, [wg, wu])
+    expect = gate.clone()
+    torch.cuda.synchronize()
+    reference_engine._Z4siluP13__nv_bfloat16S0_i(expect.data_ptr(), up.data_ptr(), rows)
+    torch.cuda.synchronize()
+    got = ops.decode_projections(x, [wg, wu], epilogue="swiglu")[0]
+    again = ops.decode_projections(x, [wg, wu], epilogue="swiglu")[0]
+    torch.cuda.synchronize()
+    assert torch.equal(got, expect)
+    assert torch.equal(got, again)

@@ -34,10 +34,13 @@
 //                     another order than the one-row ones, so this mode has
 //                     its own parity policy (near-ties only, as fast).
 //   native            batched, with every projection and the LM head on
-//                     tvp_decode_projections (Q, K and V in one launch, gate
-//                     and up in one launch) instead of cuBLAS: the same
-//                     operands and FP32 accumulation, another summation order,
-//                     so fast's parity policy again.
+//                     tvp_decode_projections instead of cuBLAS: Q, K and V in
+//                     one launch; O with the residual add in its epilogue;
+//                     gate and up with silu in their epilogue; down with the
+//                     residual add.  The same operands and FP32 accumulation
+//                     in another summation order (the fused residual and silu
+//                     keep the reference's rounding points), so fast's parity
+//                     policy again.
 #include <cublas_v2.h>
 #include <cuda_runtime.h>
 
@@ -289,18 +292,18 @@ std::vector<int> decodeBatchPaged(cublasHandle_t cublas_handle, __nv_bfloat16* h
   // Native mode: up to three projections of the same rows in one launch.
   auto native = [&](const __nv_bfloat16* in, int in_dim,
                     std::initializer_list<const __nv_bfloat16*> ws, std::initializer_list<int> ns,
-                    std::initializer_list<__nv_bfloat16*> outs) {
+                    std::initializer_list<__nv_bfloat16*> outs, int epilogue) {
     const tvp_bf16* w[TVP_PROJ_MAX];
     int n[TVP_PROJ_MAX];
-    void* out[TVP_PROJ_MAX];
+    void* out[TVP_PROJ_MAX] = {};
     int count = 0;
     for (auto* p : ws) w[count++] = reinterpret_cast<const tvp_bf16*>(p);
     count = 0;
     for (int v : ns) n[count++] = v;
-    count = 0;
-    for (auto* p : outs) out[count++] = p;
+    int stored = 0;
+    for (auto* p : outs) out[stored++] = p;
     check_tvp(tvp_decode_projections(reinterpret_cast<const tvp_bf16*>(in), batch, in_dim, count,
-                                     w, n, out, 0, st.stream));
+                                     w, n, out, epilogue, st.stream));
   };
   // The step's device work on `stream`; nullptr is the legacy default stream,
   // where the reference's own op wrappers are called.
@@ -316,7 +319,7 @@ std::vector<int> decodeBatchPaged(cublasHandle_t cublas_handle, __nv_bfloat16* h
       rmsNormKernel<<<batch, 1024, 0, stream>>>(hidden_states, buffers.rms_output, lw.input_norm);
       if (st.native_proj) {
         native(buffers.rms_output, kHidden, {lw.w_q, lw.w_k, lw.w_v}, {kHidden, 512, 512},
-               {buffers.q, buffers.k, buffers.v});
+               {buffers.q, buffers.k, buffers.v}, TVP_PROJ_BF16);
       } else {
         project(qProjection, buffers.rms_output, kHidden, lw.w_q, buffers.q, kHidden);
         project(kProjection, buffers.rms_output, kHidden, lw.w_k, buffers.k, 512);
@@ -337,27 +340,30 @@ std::vector<int> decodeBatchPaged(cublasHandle_t cublas_handle, __nv_bfloat16* h
           kKvHeads, kQHeads, d_tables, kTableStride, d_len, batch, 0.125f, st.mode, 0,
           st.workspace, st.workspace_bytes, reinterpret_cast<tvp_bf16*>(buffers.attn_output),
           st.error, stream));
-      if (st.native_proj)
-        native(buffers.attn_output, kHidden, {lw.w_o}, {kHidden}, {buffers.o_output});
-      else
+      if (st.native_proj) {  // hidden += O attn, one launch
+        native(buffers.attn_output, kHidden, {lw.w_o}, {kHidden}, {hidden_states},
+               TVP_PROJ_RESIDUAL);
+      } else {
         project(outputProjection, buffers.attn_output, kHidden, lw.w_o, buffers.o_output, kHidden);
-      residual(buffers.o_output);
+        residual(buffers.o_output);
+      }
       rmsNormKernel<<<batch, 1024, 0, stream>>>(hidden_states, buffers.rms_output,
                                                 lw.post_attention_norm);
-      if (st.native_proj) {
-        native(buffers.rms_output, kHidden, {lw.w_gate, lw.w_up}, {8192, 8192},
-               {buffers.gate, buffers.up});
+      if (st.native_proj) {  // gate = silu(gate x) * (up x), one launch
+        native(buffers.rms_output, kHidden, {lw.w_gate, lw.w_up}, {8192, 8192}, {buffers.gate},
+               TVP_PROJ_SWIGLU);
       } else {
         project(gateProjection, buffers.rms_output, kHidden, lw.w_gate, buffers.gate, 8192);
         project(upProjection, buffers.rms_output, kHidden, lw.w_up, buffers.up, 8192);
+        if (stream) siluKernel<<<batch, 1024, 0, stream>>>(buffers.gate, buffers.up);
+        else silu(buffers.gate, buffers.up, batch);
       }
-      if (stream) siluKernel<<<batch, 1024, 0, stream>>>(buffers.gate, buffers.up);
-      else silu(buffers.gate, buffers.up, batch);
-      if (st.native_proj)
-        native(buffers.gate, 8192, {lw.w_down}, {kHidden}, {buffers.down});
-      else
+      if (st.native_proj) {  // hidden += down, one launch
+        native(buffers.gate, 8192, {lw.w_down}, {kHidden}, {hidden_states}, TVP_PROJ_RESIDUAL);
+      } else {
         project(downProjection, buffers.gate, 8192, lw.w_down, buffers.down, kHidden);
-      residual(buffers.down);
+        residual(buffers.down);
+      }
     }
     rmsNormKernel<<<batch, 1024, 0, stream>>>(hidden_states, buffers.rms_output, weights.final_norm);
     if (!st.batched) return;
@@ -368,7 +374,7 @@ std::vector<int> decodeBatchPaged(cublasHandle_t cublas_handle, __nv_bfloat16* h
       const int n = VOCAB_SIZE;
       void* out = logits;
       check_tvp(tvp_decode_projections(reinterpret_cast<const tvp_bf16*>(buffers.rms_output),
-                                       batch, kHidden, 1, &w, &n, &out, 1, stream));
+                                       batch, kHidden, 1, &w, &n, &out, TVP_PROJ_F32, stream));
     } else if (cublasGemmEx(cublas_handle, CUBLAS_OP_T, CUBLAS_OP_N, VOCAB_SIZE, batch, kHidden, &alpha,
                      weights.embedding, CUDA_R_16BF, kHidden, buffers.rms_output, CUDA_R_16BF,
                      kHidden, &beta, logits, CUDA_R_32F, VOCAB_SIZE, CUBLAS_COMPUTE_32F,

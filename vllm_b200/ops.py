@@ -232,16 +232,27 @@ def greedy_argmax(logits, out=None, workspace=None, stream=None):
     return out
 
 
-def decode_projections(x, weights, outs=None, out_f32=False, stream=None):
+_EPILOGUES = {"bf16": 0, "f32": 1, "residual": 2, "swiglu": 3}
+
+
+def decode_projections(x, weights, outs=None, epilogue="bf16", stream=None):
     """The decode step's projections of 1-8 rows by up to three weight matrices
-    that share them, in one launch: outs[i][t] = weights[i] @ x[t].
+    that share them, in one launch: y[i][t] = weights[i] @ x[t].
 
     x: BF16 [rows, k] (k a multiple of 256); weights[i]: BF16 [n_i, k] (n_i a
-    multiple of 16), the reference's weight layout; outs[i]: [rows, n_i], BF16,
-    or FP32 when ``out_f32`` (the LM head).  FP32 accumulation in a fixed
-    order, one rounding.  Returns the list of outputs."""
+    multiple of 16), the reference's weight layout.  FP32 accumulation in a
+    fixed order.  ``epilogue``:
+      "bf16"      outs[i] = bf16(y[i])                    [rows, n_i] BF16
+      "f32"       outs[i] = y[i] (the LM head)            [rows, n_i] FP32
+      "residual"  outs[i] += bf16(y[i]) as one BF16 add (residualAdd fused;
+                  ``outs`` required: the hidden rows)
+      "swiglu"    two weights (gate, up) of one shape; outs = [out]:
+                  out = bf16(g (1 / (1 + exp(-g))) u), g, u = bf16(y[0]), bf16(y[1])
+    Returns the list of outputs."""
     lib = N.load()
     weights = list(weights)
+    if epilogue not in _EPILOGUES:
+        raise ValueError(f"epilogue must be one of {sorted(_EPILOGUES)}")
     dev = x.device
     _need(x, "x", torch.bfloat16, dev)
     if x.dim() != 2:
@@ -249,22 +260,32 @@ def decode_projections(x, weights, outs=None, out_f32=False, stream=None):
     rows, k = x.shape
     if not 1 <= len(weights) <= 3:
         raise ValueError("one to three weight matrices")
-    odt = torch.float32 if out_f32 else torch.bfloat16
     for i, w in enumerate(weights):
         _need(w, f"weights[{i}]", torch.bfloat16, dev)
         if w.dim() != 2 or w.shape[1] != k:
             raise ValueError(f"weights[{i}] must be [n, {k}]")
+    swiglu = epilogue == "swiglu"
+    if swiglu and (len(weights) != 2 or weights[0].shape != weights[1].shape):
+        raise ValueError("swiglu takes two weights of one shape (gate, up)")
+    shapes = [(rows, weights[0].shape[0])] if swiglu else [(rows, w.shape[0]) for w in weights]
+    odt = torch.float32 if epilogue == "f32" else torch.bfloat16
     if outs is None:
-        outs = [torch.empty(rows, w.shape[0], dtype=odt, device=dev) for w in weights]
-    for i, (o, w) in enumerate(zip(outs, weights)):
+        if epilogue == "residual":
+            raise ValueError("the residual epilogue needs outs (the rows it adds to)")
+        outs = [torch.empty(*sh, dtype=odt, device=dev) for sh in shapes]
+    outs = list(outs)
+    if len(outs) != len(shapes):
+        raise ValueError(f"{len(shapes)} output(s) expected")
+    for i, (o, sh) in enumerate(zip(outs, shapes)):
         _need(o, f"outs[{i}]", odt, dev)
-        if tuple(o.shape) != (rows, w.shape[0]):
-            raise ValueError(f"outs[{i}] must be [{rows}, {w.shape[0]}]")
+        if tuple(o.shape) != sh:
+            raise ValueError(f"outs[{i}] must be {list(sh)}")
     cnt = len(weights)
+    ptrs = [o.data_ptr() for o in outs] + [None] * (cnt - len(outs))
     wp = (ctypes.c_void_p * cnt)(*[w.data_ptr() for w in weights])
-    op = (ctypes.c_void_p * cnt)(*[o.data_ptr() for o in outs])
+    op = (ctypes.c_void_p * cnt)(*ptrs)
     ns = (ctypes.c_int * cnt)(*[w.shape[0] for w in weights])
-    rc = lib.tvp_decode_projections(_ptr(x), rows, k, cnt, wp, ns, op, int(bool(out_f32)),
+    rc = lib.tvp_decode_projections(_ptr(x), rows, k, cnt, wp, ns, op, _EPILOGUES[epilogue],
                                     _stream(stream))
     N.check(rc, "tvp_decode_projections")
     return outs
