@@ -127,3 +127,31 @@ def test_swiglu_epilogue_is_the_reference_silu(reference_engine, rows):
     torch.cuda.synchronize()
     assert torch.equal(got, expect)
     assert torch.equal(got, again)
+
+
+def test_back_to_back_launches_read_the_previous_output():
+    """Each launch lets the next one start early and streams its weights before
+    it waits for the previous grid; the input rows must still be the previous
+    launch's finished output.  `act` is NaN before every chain, so a read ahead
+    of the wait would leave NaNs in y."""
+    x, (wg, wu) = make(4, 2048, [8192, 8192], seed=81)
+    _, (wd,) = make(4, 8192, [2048], seed=82)
+    act = torch.empty(4, 8192, dtype=torch.bfloat16, device="cuda")
+    hidden = torch.empty(4, 2048, dtype=torch.bfloat16, device="cuda")
+    h0 = torch.randn(4, 2048, device="cuda").to(torch.bfloat16)
+    results = []
+    for _ in range(4):
+        act.fill_(float("nan"))
+        hidden.copy_(h0)
+        ops.decode_projections(x, [wg, wu], outs=[act], epilogue="swiglu")
+        ops.decode_projections(act, [wd], outs=[hidden], epilogue="residual")
+        results.append(hidden.clone())
+    torch.cuda.synchronize()
+    act_ref = ops.decode_projections(x, [wg, wu], epilogue="swiglu")[0]
+    torch.cuda.synchronize()
+    y_ref = ops.decode_projections(act_ref, [wd])[0]
+    torch.cuda.synchronize()
+    expect = h0 + y_ref
+    for r in results:
+        assert not bool(r.isnan().any())
+        assert torch.equal(r, expect)

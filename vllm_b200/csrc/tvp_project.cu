@@ -25,6 +25,13 @@
 //  * The warps' 16 x 8 FP32 partial tiles are summed in shared memory in warp
 //    order, so the result does not depend on timing (deterministic), then
 //    rounded once to the output type.
+//  * Launched as a programmatic dependent launch: the kernel lets the next
+//    launch in the stream start at once (griddepcontrol.launch_dependents)
+//    and issues its first weight loads before it waits for the previous grid
+//    (griddepcontrol.wait), since weights never depend on it; the input rows
+//    are read, and every output written, only after the wait.  Two
+//    projections in a row (gate+up, then down) so overlap the second's weight
+//    stream with the first's tail.
 //  * Epilogues fold the reference's next elementwise kernel into the store,
 //    with its exact operations and rounding points: the residual connection
 //    (residualKernel, src/model/resConnection.cu:6-10: a BF16 add into the
@@ -97,6 +104,9 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
   for (int m = 0; m < kMats; ++m) c[m][0] = c[m][1] = c[m][2] = c[m][3] = 0.f;
   const int blocks = slice / kProjBlock;
   const size_t row8 = (size_t)8 * p.k;
+  // The next launch in the stream may start now; it reads nothing this grid
+  // writes before its own wait below.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   for (int b0 = 0; b0 < blocks; b0 += kUnroll) {
     uint4 va[kMats][kUnroll], vb[kMats][kUnroll], vx[kUnroll];
 #pragma unroll
@@ -108,9 +118,16 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
           va[m][i] = ld_stream_v4(wa[m] + off);
           vb[m][i] = ld_stream_v4(wa[m] + row8 + off);
         }
-        vx[i] = has_x ? __ldg(reinterpret_cast<const uint4*>(xr + off)) : make_uint4(0, 0, 0, 0);
       }
     }
+    // The input rows may be the previous grid's output: wait for it (a no-op
+    // after the first batch, and when this launch was not programmatic).
+    if (b0 == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < kUnroll; ++i)
+      if (b0 + i < blocks)
+        vx[i] = has_x ? __ldg(reinterpret_cast<const uint4*>(xr + (b0 + i) * kProjBlock))
+                      : make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int i = 0; i < kUnroll; ++i) {
       if (b0 + i < blocks) {
@@ -202,21 +219,22 @@ int tvp_decode_projections(const tvp_bf16* x, int rows, int k, int count, const 
     p.n[i] = n[i];
     p.cta_end[i] = (int)ctas;
   }
-  const cudaStream_t s = static_cast<cudaStream_t>(stream);
   // 16 warps (one CTA per SM) when each of 8 warps would stream more than
   // 512 columns, so that long rows keep enough loads in flight per SM.
   const bool wide = k > 4096 && k % 512 == 0;
-  if (swiglu) {
-    if (wide)
-      decode_projection_kernel<16, 2, 4><<<(unsigned)ctas, 16 * 32, 0, s>>>(p);
-    else
-      decode_projection_kernel<8, 2, 4><<<(unsigned)ctas, 8 * 32, 0, s>>>(p);
-  } else if (wide) {
-    decode_projection_kernel<16, 1, 8><<<(unsigned)ctas, 16 * 32, 0, s>>>(p);
-  } else {
-    decode_projection_kernel<8, 1, 8><<<(unsigned)ctas, 8 * 32, 0, s>>>(p);
-  }
-  return cudaGetLastError() == cudaSuccess ? TVP_OK : TVP_ERR_RUNTIME;
+  void (*kernel)(const ProjParams) =
+      swiglu ? (wide ? decode_projection_kernel<16, 2, 4> : decode_projection_kernel<8, 2, 4>)
+             : (wide ? decode_projection_kernel<16, 1, 8> : decode_projection_kernel<8, 1, 8>);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ctas);
+  cfg.blockDim = dim3(wide ? 16 * 32 : 8 * 32);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, p) == cudaSuccess ? TVP_OK : TVP_ERR_RUNTIME;
 }
 
 }  // extern "C"
