@@ -220,7 +220,9 @@ int tvp_greedy_argmax(const float* d_logits, int rows, int vocab, long long row_
  * w, n and out are HOST arrays of `count` (1..3) entries.  rows 1..8; k a
  * multiple of 256; every n[i] a multiple of 16; x and w[i] 16-byte aligned,
  * out[i] aligned to its element and not overlapping x.  No workspace, no
- * synchronisation: the launch goes on `stream`.
+ * synchronisation: the launch goes on `stream`, as a programmatic dependent
+ * launch that streams its first weights before it waits for the previous
+ * kernel in the stream (it reads x and writes out only after that wait).
  */
 #define TVP_PROJ_MAX 3
 #define TVP_PROJ_BF16 0
