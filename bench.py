@@ -49,6 +49,25 @@ def env_int(name, default):
         return default
 
 
+class L2Flush:
+    """Evicts L2 (126 MB) between timed launches: 256 MB written, then 256 MB of
+    another buffer read, both outside the timed interval.  The read leaves L2
+    holding clean lines of an unrelated buffer, so the next launch finds
+    neither its own data in L2 nor dirty lines whose write-back to DRAM would
+    be charged to it."""
+
+    NOTE = "flushed between timed launches (256 MB written, then 256 MB of another buffer read)"
+
+    def __init__(self, dev, nbytes=256 << 20):
+        import torch
+        self.w = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.r = torch.ones(nbytes // 4, dtype=torch.int32, device=dev)
+
+    def __call__(self, i):
+        self.w.fill_(i & 0xFF)
+        return self.r.sum()
+
+
 def hbm_peak():
     try:
         peaks = json.loads(PEAKS_FILE.read_text())
@@ -567,8 +586,8 @@ def bench_long_context_heads(dev, iters=20):
     from vllm_b200 import ops
     peak, kind = hbm_peak()
     res = {"workload": "long_context 16 x 32768, 1 layer, pools of kv_heads of the 8 heads",
-           "peak_source": kind, "l2": "flushed between timed launches (256 MB written)"}
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+           "peak_source": kind, "l2": L2Flush.NOTE}
+    flush = L2Flush(dev)
     for kv_heads in (4, 2, 1):
         case, kp, vp, q = long_context_pools(dev, kv_heads)
         tables = torch.from_numpy(case.tables).to(dev)
@@ -582,7 +601,7 @@ def bench_long_context_heads(dev, iters=20):
               for _ in range(iters)]
         torch.cuda.synchronize(dev)
         for i, (a, b) in enumerate(ev):
-            flush.fill_(i & 0xFF)
+            flush(i)
             a.record()
             ops.paged_decode_attention(q, kp, vp, 0, tables, lens, ws, out=out)
             b.record()
@@ -614,8 +633,8 @@ def bench_head_sharded(dev, rank, world, local_rank, iters=20):
     stream = torch.cuda.current_stream(dev)
     res = {"workload": f"long_context 16 x 32768, 1 layer, {kv_heads} KV head(s) per GPU",
            "all_gather_bytes_per_rank": 16 * kv_heads * W.GROUP * W.HEAD_DIM * 2,
-           "l2": "flushed between timed layers (256 MB written)"}
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+           "l2": L2Flush.NOTE}
+    flush = L2Flush(dev)
 
     def timed(fn):
         for _ in range(3):
@@ -625,7 +644,7 @@ def bench_head_sharded(dev, rank, world, local_rank, iters=20):
         dist.barrier(device_ids=[local_rank])
         torch.cuda.synchronize(dev)
         for i, (a, b) in enumerate(ev):
-            flush.fill_(i & 0xFF)
+            flush(i)
             a.record(stream)
             fn()
             b.record(stream)
@@ -675,7 +694,7 @@ def bench_prefill(dev, iters=20):
     import oracle
     from vllm_b200 import ops
     peak, kind = tensor_peak()
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
     res = {"roofline": "tensor (bf16 mma); flops = 256 (p + 1) per query head per token at position p",
            "peak_source": f"{kind} bf16_tflops {peak}"}
     ref = oracle.load_reference()
@@ -694,7 +713,7 @@ def bench_prefill(dev, iters=20):
         out = torch.empty_like(q)
         times = []
         for i in range(iters + 3):
-            flush.fill_(i & 0xFF)
+            flush(i)
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
             ops.paged_prefill_attention(q, kp, vp, 0, tables, cu, pos0, max(prompts), out=out)
@@ -745,10 +764,10 @@ def bench_decode_small(dev, iters=50):
     lens = torch.from_numpy(case.lens).to(dev)
     ws = ops.DecodeWorkspace(4, dev)
     out = torch.empty_like(q)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
     times = []
     for i in range(iters + 3):
-        flush.fill_(i & 0xFF)
+        flush(i)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         ops.decode_plan(lens, case.tables.shape[1], ws)
@@ -810,7 +829,7 @@ def bench_projections(dev, iters=20):
     emb = w(VOC, H)
     o = lambda n, dt=torch.bfloat16: torch.empty(B, n, dtype=dt, device=dev)
     oq, ok, ov, oo, og, ou, od, ol = o(H), o(KV), o(KV), o(H), o(I), o(I), o(H), o(VOC, torch.float32)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
 
     def timed(fn):
         # Every iteration is enqueued before one synchronisation, so the host's
@@ -818,7 +837,7 @@ def bench_projections(dev, iters=20):
         # 256 MB flush before each launch keeps the host ahead).
         ev = []
         for i in range(iters + 3):
-            flush.fill_(i & 0xFF)
+            flush(i)
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
             fn()

@@ -97,10 +97,32 @@ int ref_store_paged_kv(uint16_t* k_pool, uint16_t* v_pool, int num_blocks, int l
   return finish();
 }
 
+// Reads n16 16-byte words; the sum only keeps the loads from being dropped.
+static __global__ void read_words(const uint4* p, size_t n16, unsigned* sink) {
+  unsigned acc = 0;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const uint4 v = p[i];
+    acc += v.x ^ v.y ^ v.z ^ v.w;
+  }
+  if (acc == 0x9e3779b9u) *sink = acc;  // practically never taken
+}
+
+// Evicts L2 between timed iterations, as the product's timing does: `bytes`
+// (larger than L2) written, then `bytes` of the second half read, so that the
+// timed work finds neither its data nor dirty lines in L2.  `scratch` holds
+// 2 x bytes.
+static void evict_l2(void* scratch, size_t bytes, int i) {
+  cudaMemsetAsync(scratch, i & 0xff, bytes);
+  unsigned char* second = static_cast<unsigned char*>(scratch) + bytes;
+  read_words<<<1184, 256>>>(reinterpret_cast<const uint4*>(second), bytes / 16,
+                            reinterpret_cast<unsigned*>(second));
+}
+
 // tables: host [batch][table_stride]; lens: host attended lengths (L = current_seq_len + 1).
 // When iters > 0, *ms_out receives the mean time of the three-call decode
-// attention sequence per launch set, with `flush_bytes` of a scratch buffer
-// rewritten between iterations (outside the timed interval).
+// attention sequence per launch set, with L2 evicted between iterations
+// (evict_l2 on 2 x `flush_bytes` of scratch, outside the timed interval).
 int ref_paged_decode(const uint16_t* d_q, uint16_t* k_pool, uint16_t* v_pool, int num_blocks,
                      int layer, const int* tables, int table_stride, const int* lens, int batch,
                      uint16_t* d_out, int iters, size_t flush_bytes, float* ms_out) {
@@ -141,13 +163,13 @@ int ref_paged_decode(const uint16_t* d_q, uint16_t* k_pool, uint16_t* v_pool, in
     step();
     if (cudaDeviceSynchronize() != cudaSuccess) throw std::runtime_error("decode failed");
     if (iters > 0 && ms_out) {
-      if (flush_bytes && cudaMalloc(&flush, flush_bytes) != cudaSuccess)
+      if (flush_bytes && cudaMalloc(&flush, 2 * flush_bytes) != cudaSuccess)
         throw std::runtime_error("cudaMalloc flush");
       cudaEventCreate(&e0);
       cudaEventCreate(&e1);
       double total = 0.0;
       for (int i = 0; i < iters; ++i) {
-        if (flush) cudaMemsetAsync(flush, i & 0xff, flush_bytes);
+        if (flush) evict_l2(flush, flush_bytes, i);
         cudaEventRecord(e0);
         step();
         cudaEventRecord(e1);
@@ -198,13 +220,13 @@ int ref_prefill_attention(const uint16_t* d_q, const uint16_t* d_k, const uint16
     step();
     if (cudaDeviceSynchronize() != cudaSuccess) throw std::runtime_error("prefill failed");
     if (iters > 0 && ms_out) {
-      if (flush_bytes && cudaMalloc(&flush, flush_bytes) != cudaSuccess)
+      if (flush_bytes && cudaMalloc(&flush, 2 * flush_bytes) != cudaSuccess)
         throw std::runtime_error("cudaMalloc flush");
       cudaEventCreate(&e0);
       cudaEventCreate(&e1);
       double total = 0.0;
       for (int i = 0; i < iters; ++i) {
-        if (flush) cudaMemsetAsync(flush, i & 0xff, flush_bytes);
+        if (flush) evict_l2(flush, flush_bytes, i);
         cudaEventRecord(e0);
         step();
         cudaEventRecord(e1);
