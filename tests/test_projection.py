@@ -58,3 +58,47 @@ def test_projection_wrapper_checks_shapes():
     x = torch.zeros(4, 256, dtype=torch.bfloat16)
     with pytest.raises(ValueError):
         ops.decode_projections(x, [torch.zeros(16, 256, dtype=torch.bfloat16)])  # not CUDA
+
+
+def test_fragment_mapping_covers_every_k_once():
+    """Host model of K5's index arithmetic (tvp_project.cu): the lane loads
+    (16 B of weight rows g and g + 8 and of input row g, at k = 8q .. 8q + 7 of
+    a 32-column block), their placement in the two m16n8k16 MMAs, the MMA's
+    fragment ownership (PTX ISA: a0/a2 rows g, a1/a3 rows g + 8, k pairs 2q and
+    2q + 8; b0/b1 k pairs 2q and 2q + 8 of column g; c0..c3 rows g, g + 8,
+    columns 2q, 2q + 1) and the epilogue's map from accumulator r of lane ln to
+    (weight row, input row).  The emulated block product must equal W X^T."""
+    import numpy as np
+    rng = np.random.default_rng(0)
+    W = rng.standard_normal((16, 32))
+    X = rng.standard_normal((8, 32))
+    acc = np.zeros((32, 4))  # per lane c0..c3
+    for mma in range(2):
+        A = np.full((16, 16), np.nan)
+        B = np.full((16, 8), np.nan)
+        for lane in range(32):
+            g, q = lane >> 2, lane & 3
+            wa, wb, xv = W[g, 8 * q:8 * q + 8], W[g + 8, 8 * q:8 * q + 8], X[g, 8 * q:8 * q + 8]
+            lo, hi = slice(4 * mma, 4 * mma + 2), slice(4 * mma + 2, 4 * mma + 4)
+            for regs, (row, kk) in ((wa[lo], (g, 2 * q)), (wb[lo], (g + 8, 2 * q)),
+                                    (wa[hi], (g, 2 * q + 8)), (wb[hi], (g + 8, 2 * q + 8))):
+                assert np.isnan(A[row, kk:kk + 2]).all()  # each slot written once
+                A[row, kk:kk + 2] = regs
+            for regs, kk in ((xv[lo], 2 * q), (xv[hi], 2 * q + 8)):
+                assert np.isnan(B[kk:kk + 2, g]).all()
+                B[kk:kk + 2, g] = regs
+        assert not np.isnan(A).any() and not np.isnan(B).any()
+        D = A @ B
+        for lane in range(32):
+            g, q = lane >> 2, lane & 3
+            acc[lane] += [D[g, 2 * q], D[g, 2 * q + 1], D[g + 8, 2 * q], D[g + 8, 2 * q + 1]]
+    expect = W @ X.T  # [weight row][input row]
+    seen = np.zeros((16, 8), bool)
+    for tid in range(128):  # the epilogue's threads
+        r, ln = tid >> 5, tid & 31
+        row = (ln >> 2) + (8 if r & 2 else 0)
+        t = 2 * (ln & 3) + (r & 1)
+        assert not seen[row, t]
+        seen[row, t] = True
+        assert abs(acc[ln, r] - expect[row, t]) < 1e-9
+    assert seen.all()
