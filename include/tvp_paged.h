@@ -14,7 +14,7 @@
  *   head_dim 64, 16-token pages, 4 query heads per KV head (GQA),
  *   8 KV heads x 64 = 512 channels per cached token, 32 query heads.
  *
- * Pool layout (identical to the reference, src/model/paged_kvcache.cu:160):
+ * Pool layout (identical to the reference, src/model/paged_kvcache.cu:131):
  *   element (layer, page, slot, kv_head, d) of the K (or V) pool lives at
  *   ((layer * num_pages + page) * 16 + slot) * (kv_heads * 64) + kv_head * 64 + d
  * so a page of one layer is kv_heads * 2 KiB of contiguous BF16 per pool.
@@ -92,7 +92,7 @@ int tvp_device_sm_count(int* out_sms);
  * Replaces, in one launch:
  *   rope(k)/ropeBatch(k)                 src/model/RoPe.cu:31-62 (K, in place)
  *   rope(q)/ropeBatch(q)                 src/model/RoPe.cu:31-62 (q, in place; optional)
- *   storePagedKV                         src/model/paged_kvcache.cu:147-166 (prefill)
+ *   storePagedKV                         src/model/paged_kvcache.cu:119-139 (prefill)
  *   storePagedKVBatch / ...Kernel        src/model/paged_attention.cu:89-99,123-131 (decode)
  *
  * Token i (0 <= i < num_tokens) belongs to block-table row
@@ -247,7 +247,10 @@ int tvp_decode_projections(const tvp_bf16* x, int rows, int k, int count, const 
  *     batches beyond 46,968 rows with 8 KV heads).
  *   - The first call on a device resolves the array's device address on that
  *     device (cudaGetSymbolAddress); make that first call before any stream
- *     capture.
+ *     capture.  The address is kept for the life of the process, so the entry
+ *     point must not be used across cudaDeviceReset (the array may move).
+ *   - Every argument check runs before anything is enqueued: a rejected call
+ *     touches neither the array nor the error word.
  *   - Every call uses the same array: calls that can overlap on the GPU (other
  *     streams, other host threads on the same device) race and must be
  *     serialised by the caller.  Each call re-plans, so no state from an
@@ -313,7 +316,7 @@ int tvp_head_gather_destroy(tvp_head_gather* g);
 
 /* ======================================================================= *
  * Host API mirror: PagedKVCache / SequenceKVState / PagedBatchMetadata.
- * Same allocator semantics as src/model/paged_kvcache.cu:65-145 (LIFO free
+ * Same allocator semantics as src/model/paged_kvcache.cu:37-117 (LIFO free
  * list seeded descending, lazy ceil(L/16) pages, exhaustion checked before
  * mutation, O(n) double-free rejection), with the 1024-token context cap
  * made a per-cache parameter (max_seq_len, 1024 reproduces the reference).
@@ -322,11 +325,11 @@ typedef struct tvp_cache tvp_cache; /* PagedKVCache  (include/paged_kvcache.cuh:
 typedef struct tvp_seq tvp_seq;     /* SequenceKVState (include/paged_kvcache.cuh:16-19) */
 typedef struct tvp_batch tvp_batch; /* PagedBatchMetadata (include/paged_attention.cuh:6-15) */
 
-/* allocatePagedKVCache (src/model/paged_kvcache.cu:65-90).  device_storage=0
+/* allocatePagedKVCache (src/model/paged_kvcache.cu:37-62).  device_storage=0
  * builds the allocator only (no pools), for host-side tests. */
 int tvp_cache_create(int num_blocks, int num_layers, int kv_heads, int max_seq_len,
                      int device_storage, tvp_cache** out);
-/* freePagedKVCache (src/model/paged_kvcache.cu:92-98). */
+/* freePagedKVCache (src/model/paged_kvcache.cu:64-70). */
 void tvp_cache_destroy(tvp_cache* cache);
 int tvp_cache_pools(const tvp_cache* cache, tvp_bf16** k_pool, tvp_bf16** v_pool,
                     int* num_blocks);
@@ -335,9 +338,9 @@ int tvp_cache_free_count(const tvp_cache* cache);
 int tvp_cache_free_list(const tvp_cache* cache, int32_t* out, int capacity);
 /* Overwrites the free list (bottom..top); for seeded shuffled pools. */
 int tvp_cache_set_free_list(tvp_cache* cache, const int32_t* blocks, int count);
-/* allocatePhysicalBlock (src/model/paged_kvcache.cu:100-108). */
+/* allocatePhysicalBlock (src/model/paged_kvcache.cu:72-80). */
 int tvp_allocate_physical_block(tvp_cache* cache, int* out_block);
-/* freePhysicalBlock (src/model/paged_kvcache.cu:110-117). */
+/* freePhysicalBlock (src/model/paged_kvcache.cu:82-89). */
 int tvp_free_physical_block(tvp_cache* cache, int block);
 
 int tvp_seq_create(tvp_seq** out);
@@ -346,12 +349,12 @@ int tvp_seq_length(const tvp_seq* seq);
 int tvp_seq_set_length(tvp_seq* seq, int current_seq_len);
 /* Copies the block table; returns its length. */
 int tvp_seq_block_table(const tvp_seq* seq, int32_t* out, int capacity);
-/* reserveSequenceBlocks (src/model/paged_kvcache.cu:128-145). */
+/* reserveSequenceBlocks (src/model/paged_kvcache.cu:100-117). */
 int tvp_reserve_sequence_blocks(tvp_cache* cache, tvp_seq* seq, int total_seq_len);
-/* freeSequenceBlocks (src/model/paged_kvcache.cu:119-126). */
+/* freeSequenceBlocks (src/model/paged_kvcache.cu:91-98). */
 int tvp_free_sequence_blocks(tvp_cache* cache, tvp_seq* seq);
 
-/* storePagedKV (src/model/paged_kvcache.cu:147-166): reserve + append
+/* storePagedKV (src/model/paged_kvcache.cu:119-139): reserve + append
  * num_tokens rows of k, v (device) at current_seq_len.. through K1; with
  * rope_q non-NULL the fused form also applies RoPE to k (in place) and q,
  * replacing rope(q), rope(k), storePagedKV of src/model/paged_transformer.cu:34-36. */

@@ -23,7 +23,6 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "_build" / "liboracle.so"
 REF_LIB_PATH = HERE / "_ref" / "libtvp_ref.so"
-REFERENCE_DIR = Path(os.environ.get("TVP_REFERENCE_DIR", "/root/reference"))
 
 _lib = None
 _ref = None
@@ -31,13 +30,20 @@ _ref = None
 
 def build(with_reference: bool = True) -> None:
     """Runs oracle/Makefile: the C restatement always, the reference build when
-    the reference tree is present (it exists only on the build machine)."""
+    the reference tree is present.  Only the Makefile knows where that tree is
+    (its REF variable; the environment variable TVP_REFERENCE_DIR overrides it);
+    its ``has-ref`` target answers whether the sources are there."""
     make = shutil.which("make")
     if make is None:
         raise RuntimeError("make not found")
-    subprocess.run([make, "-C", str(HERE)], check=True)
-    if with_reference and (REFERENCE_DIR / "src" / "model" / "paged_attention.cu").exists():
-        subprocess.run([make, "-C", str(HERE), "ref", "e2e", f"REF={REFERENCE_DIR}"], check=True)
+    extra = [f"REF={os.environ['TVP_REFERENCE_DIR']}"] if os.environ.get("TVP_REFERENCE_DIR") else []
+    subprocess.run([make, "-C", str(HERE), *extra], check=True)
+    if not with_reference:
+        return
+    present = subprocess.run([make, "-s", "-C", str(HERE), "has-ref", *extra],
+                             capture_output=True).returncode == 0
+    if present:
+        subprocess.run([make, "-C", str(HERE), "ref", "e2e", *extra], check=True)
 
 
 def load() -> ctypes.CDLL:

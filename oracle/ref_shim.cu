@@ -6,7 +6,7 @@
 // run the unmodified reference path on a B200 as an oracle and as the
 // gather+cuBLAS baseline:
 //   ref_rope / ref_rope_batch   -> rope / ropeBatch         (src/model/RoPe.cu:31-62)
-//   ref_store_paged_kv          -> storePagedKV             (src/model/paged_kvcache.cu:147-166)
+//   ref_store_paged_kv          -> storePagedKV             (src/model/paged_kvcache.cu:119-139)
 //   ref_paged_decode            -> preparePagedBatch, computePagedAttentionScores,
 //                                  softmaxRows per (row, head), pagedAttentionScoresTimesV,
 //                                  freePagedBatch, in the order of

@@ -8,7 +8,7 @@
  * Each function cites the reference code it restates (paths inside the
  * arpitsri28/vllm tree):
  *   orc_rope                 src/model/RoPe.cu:8-29 (ropeKernel), :31-62
- *   orc_store_paged          src/model/paged_kvcache.cu:147-166 (storePagedKV)
+ *   orc_store_paged          src/model/paged_kvcache.cu:119-139 (storePagedKV)
  *   orc_decode_attention     src/model/attention.cu:53-93 (scores), src/model/softmax.cu:6-45,
  *                            src/model/attention.cu:95-142 (P.V), driven as
  *                            src/model/paged_transformer.cu:85-94
@@ -89,7 +89,7 @@ void orc_rope(uint16_t* x, int tokens, int proj_dim, const int32_t* positions,
 }
 
 /* Element offset of (layer, physical page, slot) in a pool of rows of kv_dim,
- * src/model/paged_kvcache.cu:160. */
+ * src/model/paged_kvcache.cu:131. */
 size_t orc_page_offset(int layer, int num_pages, int phys, int slot, int kv_dim) {
   return (((size_t)layer * num_pages + phys) * ORC_PAGE + slot) * (size_t)kv_dim;
 }

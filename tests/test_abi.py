@@ -164,3 +164,41 @@ def test_head_gather_rejects_bad_arguments_on_host(native):
     assert native.tvp_paged_decode_attention_gather(
         fake, fake, fake, 8, 1, 0, 4, 16, fake, 4, fake, 2, 0.125, 148, fake, 1 << 20, None, 0,
         None, None) == N.TVP_ERR_INVALID_ARGUMENT
+
+
+def test_noalloc_checks_every_argument_and_its_limit_on_host(native):
+    """The no-allocation decode refuses bad arguments before it enqueues
+    anything (so a rejected call leaves its shared device array untouched),
+    and refuses a batch whose workspace exceeds its fixed 4 MiB array.  With
+    148 CTAs the limit falls between 46,968 and 46,969 rows at 8 KV heads and
+    between 147,056 and 147,057 rows at 4 KV heads.  Every case returns before
+    any CUDA call (fake, never dereferenced pointers; no GPU needed)."""
+    fake = ctypes.c_void_p(0x10000)
+    args = dict(q=fake, k=fake, v=fake, pages=8, layers=16, layer=0, kvh=8, qh=32, tables=fake,
+                stride=4, lens=fake, batch=2, scale=0.125, ctas=148, out=fake, err=None,
+                stream=None)
+
+    def call(**over):
+        a = dict(args, **over)
+        return native.tvp_paged_decode_attention_noalloc(
+            a["q"], a["k"], a["v"], a["pages"], a["layers"], a["layer"], a["kvh"], a["qh"],
+            a["tables"], a["stride"], a["lens"], a["batch"], a["scale"], a["ctas"], a["out"],
+            a["err"], a["stream"])
+
+    assert call(q=None) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(out=None) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(k=None) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(layer=16) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(batch=0) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(ctas=-1) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(scale=float("nan")) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(qh=16) == N.TVP_ERR_UNSUPPORTED
+    assert call(kvh=3, qh=12) == N.TVP_ERR_UNSUPPORTED
+    assert call(out=ctypes.c_void_p(0x10008)) == N.TVP_ERR_INVALID_ARGUMENT
+    assert call(k=ctypes.c_void_p(0x10008)) == N.TVP_ERR_INVALID_ARGUMENT
+
+    limit = 4 << 20
+    for heads, rows in ((8, 46_968), (4, 147_056)):
+        assert native.tvp_decode_workspace_bytes(rows, heads, 148) <= limit
+        assert native.tvp_decode_workspace_bytes(rows + 1, heads, 148) > limit
+        assert call(kvh=heads, qh=4 * heads, batch=rows + 1) == N.TVP_ERR_WORKSPACE

@@ -26,17 +26,20 @@ pytestmark = pytest.mark.gpu
 def _noalloc(q, k_pool, v_pool, tables, lens, out, err, num_ctas=0):
     lib = N.load()
     num_layers, num_pages = k_pool.shape[0], k_pool.shape[1]
+    kv_heads = k_pool.shape[3] // 64
     return lib.tvp_paged_decode_attention_noalloc(
         ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(k_pool.data_ptr()),
-        ctypes.c_void_p(v_pool.data_ptr()), num_pages, num_layers, 0, 8, 32,
+        ctypes.c_void_p(v_pool.data_ptr()), num_pages, num_layers, 0, kv_heads, 4 * kv_heads,
         ctypes.c_void_p(tables.data_ptr()), tables.shape[1], ctypes.c_void_p(lens.data_ptr()),
         lens.numel(), 0.125, num_ctas, ctypes.c_void_p(out.data_ptr()),
         ctypes.c_void_p(err.data_ptr()), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
 
 
-@pytest.mark.parametrize("lens", [[700, 33, 1500, 16, 4096, 129, 1], [17, 64, 129, 256]])
-def test_noalloc_matches_workspace_entry_point_on_two_calls(lens):
-    case = W.decode_random(123 + len(lens), lens)
+@pytest.mark.parametrize("kv_heads,lens", [(8, [700, 33, 1500, 16, 4096, 129, 1]),
+                                           (8, [17, 64, 129, 256]),
+                                           (4, [900, 17, 2500, 64, 1])])
+def test_noalloc_matches_workspace_entry_point_on_two_calls(kv_heads, lens):
+    case = W.decode_random(123 + len(lens), lens, kv_heads=kv_heads)
     expected, err_bits = run_decode(case)  # tvp_decode_plan + tvp_paged_decode_attention
     assert err_bits == 0
     q, k, v = dev_bf16(case.q), dev_bf16(case.k_pool), dev_bf16(case.v_pool)
@@ -65,3 +68,29 @@ def test_noalloc_rejects_a_batch_beyond_its_fixed_workspace():
         ctypes.c_void_p(err.data_ptr()), None)
     assert rc == N.TVP_ERR_WORKSPACE
     assert lib.tvp_decode_workspace_bytes(huge, 8, 0) > 4 << 20
+
+
+def test_rejected_call_enqueues_nothing():
+    """A call refused by an argument check (here: no output buffer) returns
+    before the plan is enqueued: the error word stays clear and the next valid
+    call still matches the workspace entry point."""
+    case = W.decode_random(140, [300, 45, 1000])
+    expected, _ = run_decode(case)
+    q, k, v = dev_bf16(case.q), dev_bf16(case.k_pool), dev_bf16(case.v_pool)
+    tables, seq_lens = dev_i32(case.tables), dev_i32(case.lens)
+    err = ops.new_error_word("cuda")
+    lib = N.load()
+    rc = lib.tvp_paged_decode_attention_noalloc(
+        ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(k.data_ptr()),
+        ctypes.c_void_p(v.data_ptr()), k.shape[1], k.shape[0], 0, 8, 32,
+        ctypes.c_void_p(tables.data_ptr()), tables.shape[1], ctypes.c_void_p(seq_lens.data_ptr()),
+        seq_lens.numel(), 0.125, 0, None, ctypes.c_void_p(err.data_ptr()),
+        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert rc == N.TVP_ERR_INVALID_ARGUMENT
+    assert int(err.item()) == 0
+    out = torch.full_like(q, float("nan"))
+    assert _noalloc(q, k, v, tables, seq_lens, out, err) == N.TVP_OK
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert_close_bf16(host_bf16(out), f32(expected), 1e-2, 2e-2, "no-alloc after a rejected call")

@@ -118,7 +118,7 @@ class SequenceKVState:
 
 def allocatePagedKVCache(num_blocks: int, num_layers: int = 16, max_seq_len: int = 1024,
                          device_storage: bool = True) -> PagedKVCache:
-    """src/model/paged_kvcache.cu:65-90; device_storage=False builds the allocator only."""
+    """src/model/paged_kvcache.cu:37-62; device_storage=False builds the allocator only."""
     h = c_void_p()
     N.check(N.load().tvp_cache_create(num_blocks, num_layers, N.KV_HEADS, max_seq_len,
                                       int(device_storage), ctypes.byref(h)), "allocatePagedKVCache")
@@ -151,7 +151,7 @@ def reserveSequenceBlocks(cache: PagedKVCache, seq: SequenceKVState, total_seq_l
 
 def storePagedKV(cache: PagedKVCache, seq: SequenceKVState, layer: int, k, v, num_tokens: int,
                  apply_rope: bool = False, rope_q=None, stream=None) -> None:
-    """storePagedKV (src/model/paged_kvcache.cu:147-166); with apply_rope the
+    """storePagedKV (src/model/paged_kvcache.cu:119-139); with apply_rope the
     fused kernel also rotates k in place (and q when given)."""
     for t, name in ((k, "k"), (v, "v")):
         if t is not None and (not t.is_cuda or t.dtype != torch.bfloat16 or not t.is_contiguous()):

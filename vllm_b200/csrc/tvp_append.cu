@@ -3,7 +3,7 @@
 // One CTA per token row.  The CTA rotates the row's q heads in place (optional),
 // rotates its K heads, and writes K and V straight into the token's physical
 // page slot.  Replaces rope/ropeBatch (src/model/RoPe.cu:31-62) followed by
-// storePagedKV (src/model/paged_kvcache.cu:147-166, a host loop of synchronous
+// storePagedKV (src/model/paged_kvcache.cu:119-139, a host loop of synchronous
 // D2D copies) or storePagedKVBatchKernel (src/model/paged_attention.cu:89-99).
 #include "tvp_params.cuh"
 

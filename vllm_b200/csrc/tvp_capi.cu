@@ -65,6 +65,23 @@ inline int map_cuda(cudaError_t e) { return e == cudaSuccess ? TVP_OK : TVP_ERR_
 
 }  // namespace
 
+int check_decode_args(const void* q, const void* k_pool, const void* v_pool, const void* out,
+                      int num_pages, int num_layers, int layer, int kv_heads, int q_heads,
+                      const int32_t* d_block_tables, int table_stride, const int32_t* d_seq_lens,
+                      int batch, float scale, int mode, int num_ctas) {
+  if (!q || !k_pool || !v_pool || !out || !d_block_tables || !d_seq_lens || num_pages <= 0 ||
+      num_layers <= 0 || layer < 0 || layer >= num_layers || table_stride <= 0 || batch <= 0 ||
+      num_ctas < 0 || !std::isfinite(scale))
+    return TVP_ERR_INVALID_ARGUMENT;
+  if (!decode_heads_supported(kv_heads) || q_heads != kv_heads * kGroup) return TVP_ERR_UNSUPPORTED;
+  if (mode != TVP_MODE_FAST && mode != TVP_MODE_COMPAT) return TVP_ERR_UNSUPPORTED;
+  // TMA row coordinates are 32-bit: the pools may hold at most 2^31 - 1 token rows.
+  if ((long long)num_layers * num_pages * kPage > 0x7fffffffLL) return TVP_ERR_UNSUPPORTED;
+  if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(q, 4) || !aligned(out, 16))
+    return TVP_ERR_INVALID_ARGUMENT;
+  return TVP_OK;
+}
+
 int prepare_decode(const void* q, const void* k_pool, const void* v_pool, int num_pages,
                    int num_layers, int layer, int kv_heads, int q_heads,
                    const int32_t* d_block_tables, int table_stride, const int32_t* d_seq_lens,
@@ -200,16 +217,10 @@ int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const 
                                const int32_t* d_seq_lens, int batch, float scale, int mode,
                                int num_ctas, void* d_workspace, size_t workspace_bytes,
                                tvp_bf16* out, int32_t* d_error, tvp_stream_t stream) {
-  if (!q || !k_pool || !v_pool || !out || !d_block_tables || !d_seq_lens || num_pages <= 0 ||
-      num_layers <= 0 || layer < 0 || layer >= num_layers || table_stride <= 0 || batch <= 0 ||
-      num_ctas < 0 || !std::isfinite(scale))
-    return TVP_ERR_INVALID_ARGUMENT;
-  if (!decode_heads_supported(kv_heads) || q_heads != kv_heads * kGroup) return TVP_ERR_UNSUPPORTED;
-  if (mode != TVP_MODE_FAST && mode != TVP_MODE_COMPAT) return TVP_ERR_UNSUPPORTED;
-  // TMA row coordinates are 32-bit: the pools may hold at most 2^31 - 1 token rows.
-  if ((long long)num_layers * num_pages * kPage > 0x7fffffffLL) return TVP_ERR_UNSUPPORTED;
-  if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(q, 4) || !aligned(out, 16))
-    return TVP_ERR_INVALID_ARGUMENT;
+  const int arc = check_decode_args(q, k_pool, v_pool, out, num_pages, num_layers, layer, kv_heads,
+                                    q_heads, d_block_tables, table_stride, d_seq_lens, batch,
+                                    scale, mode, num_ctas);
+  if (arc != TVP_OK) return arc;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (mode == TVP_MODE_COMPAT) {
     CompatParams p;

@@ -3,7 +3,7 @@
 // deployment, where GPU r keeps heads [r KVH, (r + 1) KVH) of every page in a
 // pool of rows KVH x 64 channels wide, computes query heads 4 r KVH ..
 // 4 (r + 1) KVH - 1 and the ranks then all-gather their slices.  The
-// logical -> physical block tables are the reference's (src/model/paged_kvcache.cu:119-145);
+// logical -> physical block tables are the reference's (src/model/paged_kvcache.cu:72-117);
 // the attention is the same as the reference's decode block
 // (src/model/paged_transformer.cu:85-94) restricted to these heads.
 //

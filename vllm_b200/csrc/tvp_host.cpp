@@ -1,5 +1,5 @@
 // Host side of the paged-KV path: the reference's allocator and batch
-// metadata (src/model/paged_kvcache.cu:41-166, src/model/paged_attention.cu:20-87)
+// metadata (src/model/paged_kvcache.cu:19-139, src/model/paged_attention.cu:20-87)
 // re-expressed in C++ over the fused kernels, plus the C-ABI handle functions
 // of include/tvp_paged.h that expose it without C++ types.
 #include <algorithm>
@@ -37,7 +37,7 @@ bool in_free_list(const PagedKVCache& cache, int block) {
          cache.free_blocks.end();
 }
 
-// Same checks as validateSequenceBlocks (src/model/paged_kvcache.cu:53-63):
+// Same checks as validateSequenceBlocks (src/model/paged_kvcache.cu:25-35):
 // every entry in range, not free, not repeated earlier in the table.
 void validate_sequence_blocks(const PagedKVCache& cache, const SequenceKVState& sequence) {
   validate_cache(cache);

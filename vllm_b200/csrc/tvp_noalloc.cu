@@ -12,6 +12,7 @@
 #include <mutex>
 
 #include "tvp_common.cuh"
+#include "tvp_params.cuh"
 
 namespace {
 
@@ -25,7 +26,11 @@ static __device__ __align__(256) unsigned char g_static_workspace[kStaticWorkspa
 
 // Device address of g_static_workspace per device.  In host code the array's
 // name is only a host-side stand-in: the address a kernel may use must come
-// from cudaGetSymbolAddress, called with the device current.
+// from cudaGetSymbolAddress, called with the device current.  It is resolved
+// once per device, on the first call there, and kept for the life of the
+// process: after cudaDeviceReset (or any teardown of the device's primary
+// context) the library's module is loaded again and the array may move, so
+// this entry point must not be used across a device reset.
 void* g_workspace_ptr[64] = {};
 std::mutex g_workspace_mutex;
 
@@ -54,7 +59,12 @@ int tvp_paged_decode_attention_noalloc(const tvp_bf16* q, const tvp_bf16* k_pool
                                        const int32_t* d_seq_lens, int batch, float scale,
                                        int num_ctas, tvp_bf16* out, int32_t* d_error,
                                        tvp_stream_t stream) {
-  if (batch <= 0 || num_ctas < 0) return TVP_ERR_INVALID_ARGUMENT;
+  // Every argument check of the decode runs before anything is enqueued, so a
+  // rejected call leaves the shared array and the error word untouched.
+  const int arc = tvp::check_decode_args(q, k_pool, v_pool, out, num_pages, num_layers, layer,
+                                         kv_heads, q_heads, d_block_tables, table_stride,
+                                         d_seq_lens, batch, scale, TVP_MODE_FAST, num_ctas);
+  if (arc != TVP_OK) return arc;
   const size_t need = tvp_decode_workspace_bytes(batch, kv_heads, num_ctas);
   if (need == 0)
     return (kv_heads == 1 || kv_heads == 2 || kv_heads == 4 || kv_heads == TVP_KV_HEADS)

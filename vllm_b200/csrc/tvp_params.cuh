@@ -104,6 +104,12 @@ cudaError_t launch_paged_decode(const DecodeParams& p, long long pool_rows, int 
 cudaError_t launch_paged_decode_heads(const DecodeParams& p, const CUtensorMap& k_map,
                                       const CUtensorMap& v_map, int num_ctas,
                                       cudaStream_t stream);
+// Host-side argument checks of tvp_paged_decode_attention, everything but the
+// workspace: TVP_OK or the error code that entry point returns.  No CUDA call.
+int check_decode_args(const void* q, const void* k_pool, const void* v_pool, const void* out,
+                      int num_pages, int num_layers, int layer, int kv_heads, int q_heads,
+                      const int32_t* d_block_tables, int table_stride, const int32_t* d_seq_lens,
+                      int batch, float scale, int mode, int num_ctas);
 // Argument checks, workspace layout and parameter block of the FAST decode
 // (shared by tvp_paged_decode_attention and its gather form); TVP_OK or an error.
 int prepare_decode(const void* q, const void* k_pool, const void* v_pool, int num_pages,

@@ -59,11 +59,26 @@ struct ProjParams {
   int count, rows, k, epilogue;
 };
 
+// Weights: read-only for the whole life of every launch, so the
+// non-coherent path is valid for them.
 __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
   uint4 r;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                : "l"(p));
+  return r;
+}
+
+// Input rows: with a programmatic launch they are the previous grid's output,
+// written while this grid is already resident, so they must not go through
+// the non-coherent (read-only) path.  A plain weak global load after
+// griddepcontrol.wait sees them.
+__device__ __forceinline__ uint4 ld_coherent_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p)
+               : "memory");
   return r;
 }
 
@@ -126,8 +141,7 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
 #pragma unroll
     for (int i = 0; i < kUnroll; ++i)
       if (b0 + i < blocks)
-        vx[i] = has_x ? __ldg(reinterpret_cast<const uint4*>(xr + (b0 + i) * kProjBlock))
-                      : make_uint4(0, 0, 0, 0);
+        vx[i] = has_x ? ld_coherent_v4(xr + (b0 + i) * kProjBlock) : make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int i = 0; i < kUnroll; ++i) {
       if (b0 + i < blocks) {
