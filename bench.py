@@ -1,11 +1,14 @@
 """Benchmark of the B200 paged-KV decode path (tiny-vLLM Llama-3.2-1B geometry).
 
-Workload (per GPU; weak scaling, requests sharded across GPUs, no collective on
-the data path): decode_sweep — 256 rows with attended lengths L ~ U[512, 8192]
+Workload: decode_sweep — 256 rows with attended lengths L ~ U[512, 8192]
 (seed 4), 16 layers, 32 Q / 8 KV heads, head_dim 64, BF16 N(0, 1) K/V in
-16-token pages scattered over a pool sized to fit.  One step = one decode step
-of the hot path over all 16 layers: the plan, then per layer the fused
-RoPE(q, k) + paged append of the new token and the fused GQA decode attention.
+16-token pages scattered over a pool sized to fit.  With N GPUs the 256 rows
+are sharded by request (strong scaling: the job is the same at every N; each
+GPU owns its rows, its page pool and its tables; no collective on the data
+path).  One step = one decode step of the hot path over all 16 layers, replayed
+as one CUDA graph: the plan, then per layer the fused RoPE(q, k) + paged append
+of the new token and the fused GQA decode attention.  `weak_scaling` (N > 1)
+gives every GPU the whole 256-row workload instead.
 
 Metric: paged-decode KV GB/s = K+V bytes attended (sum_L * 2 KiB per layer) per
 second, whole job; also decode tok/s and the fraction of measured HBM peak.
@@ -85,11 +88,11 @@ def algorithmic_bytes(lens: np.ndarray) -> dict:
     return {"kv": kv, "q_out": qo, "tables": tables, "total": kv + qo + tables}
 
 
-def config_block(world, batch, layers=16):
+def config_block(world, global_rows, layers=16):
     return {
         "workload": "decode_sweep",
-        "rows_per_gpu": batch,
-        "global_rows": batch * world,
+        "global_rows": global_rows,
+        "rows_per_gpu": f"{global_rows} / {world}, sharded by request (greedy longest-first by sum L)",
         "seq_len": "L ~ U[512, 8192] (seed 4)",
         "layers": layers,
         "q_heads": 32,
@@ -97,7 +100,9 @@ def config_block(world, batch, layers=16):
         "head_dim": 64,
         "page_tokens": 16,
         "parallelism": f"request-sharded x{world} (no collective)",
-        "l2": "inputs larger than L2 (>=2.2 GB of K+V per layer launch)",
+        "step": "one CUDA-graph replay: plan + 16 x (RoPE/append, decode attention)",
+        "l2": "inputs larger than L2 (>=2.2 GB of K+V per layer launch at 1 GPU; "
+              ">=0.28 GB per launch at 8 GPUs)",
     }
 
 
@@ -135,23 +140,24 @@ def run_reference_arm(args, rank, world):
     if rank != 0:
         return
     rows = 32
-    samples = []
+    samples, step_ms = [], []
     for _ in range(args.warmup):
         time_cpu(rows, 0.5)
     for _ in range(args.steps):
         cb, el = time_cpu(rows, args.cpu_seconds / max(args.steps, 1))
         samples.append(cb["value"])
+        step_ms.append(el * 1e3)
     value = statistics.median(samples)
     cb["value"] = round(value, 3)
-    # Each timed step is a bounded sample; ms_per_step is one full step of the
-    # workload (256 rows, 16 layers) at the measured rate.
-    step_bytes = algorithmic_bytes(W.sweep_lengths(4, 256))["kv"] * 16
+    # Each timed step is a bounded sample of the workload (32 rows, 1 layer,
+    # repeated for its share of --cpu-seconds); ms_per_step is its wall time.
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(step_bytes / (value * 1e9) * 1e3, 1),
-        "ms_per_step_basis": "one full decode_sweep step (256 rows x 16 layers) at the sample rate",
-        "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(statistics.median(step_ms), 1),
+        "ms_per_step_basis": "wall time of one timed step: a bounded sample (32 rows of "
+                             "decode_sweep, 1 layer, repeated), not a full decode step",
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": config_block(world, 256), "cpu_baseline": cb,
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -262,101 +268,161 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------- our arm ---
-def run_ours(args, rank, world, local_rank):
-    import torch
-    import torch.distributed as dist
-    from vllm_b200 import ops
+def shard_case(global_case, world, rank, seed=4):
+    """Rank `rank`'s share of the global decode_sweep: its rows (greedy
+    longest-first by sum of L, vllm_b200.sharding) with their own page pool and
+    block tables, as a GPU that owns those requests holds them.  One rank gets
+    the global case itself."""
+    from vllm_b200 import sharding
+    if world == 1:
+        return global_case, np.arange(global_case.batch)
+    rows = sharding.shard_by_request(global_case.lens, world)[rank]
+    lens = global_case.lens[rows]
+    rng = np.random.default_rng(seed + 1000 + 7919 * (rank + 1))
+    need = int(sum(W.pages_for(int(L)) for L in lens))
+    num_pages = need + 64
+    tables = W.scattered_tables(rng, lens, num_pages)
+    return W.DecodeCase(lens=lens, tables=tables, num_pages=num_pages,
+                        num_layers=global_case.num_layers), rows
 
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    case = W.decode_sweep(seed=4, batch=args.rows)
-    case.num_layers = args.layers
-    B, P, layers = case.batch, case.num_pages, case.num_layers
-    lens = case.lens
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(1234 + rank)
-    shape = (layers, P, 16, W.KV_DIM)
-    k_pool = torch.empty(shape, dtype=torch.bfloat16, device=dev)
-    v_pool = torch.empty(shape, dtype=torch.bfloat16, device=dev)
-    for l in range(layers):
-        k_pool[l].normal_(generator=gen)
-        v_pool[l].normal_(generator=gen)
-    tables = torch.from_numpy(case.tables).to(dev)
-    seq_lens = torch.from_numpy(lens).to(dev)
-    positions = seq_lens - 1
-    q_all = torch.randn((layers, B, W.Q_DIM), generator=gen, device=dev).to(torch.bfloat16)
-    k_new = torch.randn((layers, B, W.KV_DIM), generator=gen, device=dev).to(torch.bfloat16)
-    v_new = torch.randn((layers, B, W.KV_DIM), generator=gen, device=dev).to(torch.bfloat16)
-    out = torch.empty((layers, B, W.Q_DIM), dtype=torch.bfloat16, device=dev)
-    err = ops.new_error_word(dev)
-    ws = ops.DecodeWorkspace(B, dev)
-    stream = torch.cuda.current_stream(dev)
-    stride = case.tables.shape[1]
 
-    def step(events=None):
-        ops.decode_plan(seq_lens, stride, ws, error=err, stream=stream)
+class DecodeStep:
+    """One GPU's decode step over its rows: the plan, then per layer the fused
+    RoPE + paged append of the new token (K1) and the decode attention (K2).
+    Pools and inputs are seeded and live in HBM."""
+
+    def __init__(self, case, dev, seed):
+        import torch
+        from vllm_b200 import ops
+        self.ops, self.dev, self.case = ops, dev, case
+        B, P, layers = case.batch, case.num_pages, case.num_layers
+        self.layers = layers
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed)
+        shape = (layers, P, 16, W.KV_DIM)
+        self.k_pool = torch.empty(shape, dtype=torch.bfloat16, device=dev)
+        self.v_pool = torch.empty(shape, dtype=torch.bfloat16, device=dev)
         for l in range(layers):
-            ops.rope_append(k_pool, v_pool, l, tables, positions, k_new[l], v_new[l], q=q_all[l],
-                            writeback_k=False, error=err, stream=stream)
+            self.k_pool[l].normal_(generator=gen)
+            self.v_pool[l].normal_(generator=gen)
+        self.tables = torch.from_numpy(case.tables).to(dev)
+        self.seq_lens = torch.from_numpy(case.lens).to(dev)
+        self.positions = self.seq_lens - 1
+        self.q_all = torch.randn((layers, B, W.Q_DIM), generator=gen, device=dev).to(torch.bfloat16)
+        self.k_new = torch.randn((layers, B, W.KV_DIM), generator=gen, device=dev).to(torch.bfloat16)
+        self.v_new = torch.randn((layers, B, W.KV_DIM), generator=gen, device=dev).to(torch.bfloat16)
+        self.out = torch.empty((layers, B, W.Q_DIM), dtype=torch.bfloat16, device=dev)
+        self.err = ops.new_error_word(dev)
+        self.ws = ops.DecodeWorkspace(B, dev)
+        self.stride = case.tables.shape[1]
+
+    def __call__(self, stream, q=None, k=None, v=None, events=None, after_layer=None,
+                 before_layer=None):
+        ops = self.ops
+        q = self.q_all if q is None else q
+        k = self.k_new if k is None else k
+        v = self.v_new if v is None else v
+        ops.decode_plan(self.seq_lens, self.stride, self.ws, error=self.err, stream=stream)
+        for l in range(self.layers):
+            if before_layer is not None:
+                before_layer(l)
+            ops.rope_append(self.k_pool, self.v_pool, l, self.tables, self.positions, k[l], v[l],
+                            q=q[l], writeback_k=False, error=self.err, stream=stream)
             if events is not None:
                 events[l][0].record(stream)
-            ops.paged_decode_attention(q_all[l], k_pool, v_pool, l, tables, seq_lens, ws,
-                                       out=out[l], error=err, stream=stream)
+            ops.paged_decode_attention(q[l], self.k_pool, self.v_pool, l, self.tables,
+                                       self.seq_lens, self.ws, out=self.out[l], error=self.err,
+                                       stream=stream)
             if events is not None:
                 events[l][1].record(stream)
+            if after_layer is not None:
+                after_layer(l)
+
+    def check(self):
+        import torch
+        torch.cuda.synchronize(self.dev)
+        assert int(self.err.item()) == 0, f"device error bits {int(self.err.item())}"
+
+
+def measure_steps(step, args, world, local_rank, clocks=None):
+    """Device time of args.steps decode steps, max over ranks: each step is one
+    replay of a CUDA graph of the step (its 1 + 2 x layers launches), timed
+    with CUDA events on the replay stream between barriers.  Returns
+    (ms per step, average K2 launch ms of this rank, clock record)."""
+    import torch
+    import torch.distributed as dist
+    dev = step.dev
+    stream = torch.cuda.current_stream(dev)
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local_rank])
 
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize(dev)
-    assert int(err.item()) == 0, f"device error bits {int(err.item())}"
-
-    # ---- device-resident timing ----
-    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(layers)]
+        step(stream)
+    step.check()
+    # the dominant kernel's live launch time: events around every K2 launch of
+    # args.steps eager steps (outside the graph, so each event brackets one launch)
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(step.layers)]
           for _ in range(args.steps)]
+    for s in range(args.steps):
+        step(stream, events=ev[s])
+    step.check()
+    attn_ms = statistics.mean(e[0].elapsed_time(e[1]) for s in ev for e in s)
+
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        step(side)  # warm the side stream once outside capture
+    stream.wait_stream(side)
+    torch.cuda.synchronize(dev)
+    with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+        step(torch.cuda.current_stream(dev))
+    for _ in range(args.warmup):
+        graph.replay()
+    step.check()
+
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = ClockSampler(dev)
     barrier()
     torch.cuda.synchronize(dev)
-    clocks.start()
+    if clocks is not None:
+        clocks.start()
     t0.record(stream)
-    for s in range(args.steps):
-        step(ev[s])
+    for _ in range(args.steps):
+        graph.replay()
     t1.record(stream)
     torch.cuda.synchronize(dev)
     barrier()
-    clock_info = clocks.stop()
-    ms_total = max_over_ranks(t0.elapsed_time(t1))
-    launch_ms = [e[0].elapsed_time(e[1]) for s in ev for e in s]
-    attn_ms = statistics.mean(launch_ms)
-    ms_per_step = ms_total / args.steps
-    nbytes = algorithmic_bytes(lens)
-    kv_step = nbytes["kv"] * layers
-    value = kv_step * world / (ms_per_step / 1e3) / 1e9
-    tok_s = B * world / (ms_per_step / 1e3)
+    clock_info = clocks.stop() if clocks is not None else None
+    step.check()
+    ms_total = t0.elapsed_time(t1)
+    if world > 1:
+        t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    del graph
+    return ms_total / args.steps, attn_ms, clock_info
 
-    # ---- end to end through the C-ABI with host buffers ----
-    q_h = q_all.cpu().pin_memory()
-    k_h = k_new.cpu().pin_memory()
-    v_h = v_new.cpu().pin_memory()
-    out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    q_d, k_d, v_d = torch.empty_like(q_all), torch.empty_like(k_new), torch.empty_like(v_new)
 
-    # Copies overlap the layers as in a serving loop: layer l's inputs come in
-    # on an H2D stream and layer l waits only for them; layer l's output goes
-    # out on a D2H stream as soon as the layer is done.  The step ends on the
-    # compute stream after the last output copy, so every byte of every step
-    # is copied inside the timed region.
+def measure_e2e(step, args, world, local_rank):
+    """The same steps through the C-ABI with host buffers: every step copies
+    its q, k, v rows in from pinned host memory and its attention rows out,
+    inside the timed region.  Layer l's inputs arrive on an H2D stream and
+    layer l waits only for them; layer l's output leaves on a D2H stream as
+    soon as the layer is done, as in a serving loop.  Returns (ms per step, max
+    over ranks; H2D bytes; D2H bytes)."""
+    import torch
+    import torch.distributed as dist
+    dev = step.dev
+    stream = torch.cuda.current_stream(dev)
+    layers = step.layers
+    q_h = step.q_all.cpu().pin_memory()
+    k_h = step.k_new.cpu().pin_memory()
+    v_h = step.v_new.cpu().pin_memory()
+    out_h = torch.empty(step.out.shape, dtype=step.out.dtype).pin_memory()
+    q_d, k_d, v_d = (torch.empty_like(step.q_all), torch.empty_like(step.k_new),
+                     torch.empty_like(step.v_new))
     h2d_stream = torch.cuda.Stream(dev)
     d2h_stream = torch.cuda.Stream(dev)
     step_done = torch.cuda.Event()
@@ -372,18 +438,18 @@ def run_ours(args, rank, world, local_rank):
                 v_d[l].copy_(v_h[l], non_blocking=True)
                 arrived.append(torch.cuda.Event())
                 arrived[-1].record(h2d_stream)
-        ops.decode_plan(seq_lens, stride, ws, error=err, stream=stream)
-        for l in range(layers):
+
+        def before(l):
             stream.wait_event(arrived[l])
-            ops.rope_append(k_pool, v_pool, l, tables, positions, k_d[l], v_d[l], q=q_d[l],
-                            writeback_k=False, error=err, stream=stream)
-            ops.paged_decode_attention(q_d[l], k_pool, v_pool, l, tables, seq_lens, ws,
-                                       out=out[l], error=err, stream=stream)
+
+        def after(l):
             done = torch.cuda.Event()
             done.record(stream)
             d2h_stream.wait_event(done)
             with torch.cuda.stream(d2h_stream):
-                out_h[l].copy_(out[l], non_blocking=True)
+                out_h[l].copy_(step.out[l], non_blocking=True)
+
+        step(stream, q=q_d, k=k_d, v=v_d, before_layer=before, after_layer=after)
         sent = torch.cuda.Event()
         sent.record(d2h_stream)
         stream.wait_event(sent)
@@ -391,7 +457,8 @@ def run_ours(args, rank, world, local_rank):
 
     for _ in range(2):
         e2e_step()
-    barrier()
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -399,18 +466,71 @@ def run_ours(args, rank, world, local_rank):
         e2e_step()
     e1.record(stream)
     torch.cuda.synchronize(dev)
-    barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    step.check()
     h2d = (q_h.numel() + k_h.numel() + v_h.numel()) * 2
     d2h = out_h.numel() * 2
-    e2e_value = kv_step * world / (e2e_ms / 1e3) / 1e9
-    assert int(err.item()) == 0, f"device error bits {int(err.item())}"
+    return ms / args.steps, h2d, d2h
+
+
+def gather_rank_stats(dev, world, values):
+    """[world][len(values)] of every rank's values (one all_gather)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(values, dtype=torch.float64, device=dev)
+    if world == 1:
+        return [list(values)]
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [o.tolist() for o in out]
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    global_case = W.decode_sweep(seed=4, batch=args.rows)
+    global_case.num_layers = args.layers
+    layers = args.layers
+    case, rows = shard_case(global_case, world, rank)
+    step = DecodeStep(case, dev, seed=1234 + rank)
+
+    clocks = ClockSampler(dev)
+    ms_per_step, attn_ms, clock_info = measure_steps(step, args, world, local_rank, clocks)
+    global_kv_step = algorithmic_bytes(global_case.lens)["kv"] * layers
+    value = global_kv_step / (ms_per_step / 1e3) / 1e9
+    tok_s = global_case.batch / (ms_per_step / 1e3)
+    e2e_ms, h2d, d2h = measure_e2e(step, args, world, local_rank)
+    e2e_value = global_kv_step / (e2e_ms / 1e3) / 1e9
+    nbytes = algorithmic_bytes(case.lens)
+    per_rank = gather_rank_stats(dev, world, [case.batch, float(case.lens.sum()),
+                                              attn_ms * 1e3, nbytes["total"]])
+
+    weak = None
+    if world > 1 and not args.no_extras:
+        # every rank with the whole 256-row workload (per-GPU work fixed as N grows)
+        step.k_pool = step.v_pool = None
+        del step
+        wstep = DecodeStep(global_case, dev, seed=1234 + rank)
+        wms, _, _ = measure_steps(wstep, args, world, local_rank)
+        wbytes = algorithmic_bytes(global_case.lens)["kv"] * layers * world
+        weak = {"value": round(wbytes / (wms / 1e3) / 1e9, 2), "unit": UNIT,
+                "ms_per_step": round(wms, 4), "rows_per_gpu": global_case.batch,
+                "global_rows": global_case.batch * world, "scaling": "weak"}
+        wstep.k_pool = wstep.v_pool = None
+        del wstep
+        torch.cuda.empty_cache()
 
     # KV-head-sharded long_context (every rank takes part; after the timed runs)
     head_sharded = None
     if world > 1 and W.KV_HEADS % world == 0 and not args.no_extras:
-        del k_pool, v_pool
-        k_pool = v_pool = None
         head_sharded = bench_head_sharded(dev, rank, world, local_rank)
 
     if rank != 0:
@@ -426,23 +546,33 @@ def run_ours(args, rank, world, local_rank):
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) BF16 K/V/q, seeded lengths and page scatter)",
-        "config": config_block(world, B, layers),
+        "config": config_block(world, global_case.batch, layers),
         "decode_tok_s": round(tok_s, 1),
         "hbm_peak_frac": round(value / world / peak, 4),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
                      "kernel": "tvp::paged_decode_kernel<7,2,true,true>",
                      "algorithmic_bytes_per_launch": nbytes["total"],
-                     "avg_launch_ms": round(attn_ms, 4), "peak_source": f"{peak_kind} hbm_gbs"},
+                     "avg_launch_ms": round(attn_ms, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                     "rank": 0},
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
+                "scope": "rank 0's copies; value over all ranks' bytes, max-over-ranks time"},
         "gpu_launches": args.steps * (1 + 2 * layers),
         "clocks": clock_info,
+        "per_rank": [{"rank": r, "rows": int(v[0]), "sum_L": int(v[1]),
+                      "k2_us_per_launch": round(v[2], 2),
+                      "k2_GBps": round(v[3] / (v[2] / 1e6) / 1e9, 1)}
+                     for r, v in enumerate(per_rank)],
     }
+    if weak is not None:
+        line["weak_scaling"] = weak
     if world == 1 and not args.no_extras:
-        line.update(extras(args, dev, case, k_pool, v_pool, q_all, out, tables, seq_lens, ws))
+        line.update(extras(args, dev, case, step.k_pool, step.v_pool, step.q_all, step.out,
+                           step.tables, step.seq_lens, step.ws))
     if head_sharded is not None:
         line["long_context_head_sharded"] = head_sharded
     if world == 1 and not args.no_cpu_baseline:

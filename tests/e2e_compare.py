@@ -8,6 +8,11 @@ runs on a GPU machine with oracle/_ref/libtvp_e2e_{ref,tvp}.so built.
    the argmax differs, the gap between the two candidates in the reference's own
    logits after its BF16 rounding (src/model/argmax.cu:24), in BF16 ulps.
 
+3. Every engine mode also generates freely, and its sequences are compared
+   with the reference's: a free-running sequence can only leave the
+   reference's at the first step where the teacher-forced argmax differed,
+   since up to that step both runs decode the same inputs.
+
 Prints one JSON summary line."""
 from __future__ import annotations
 
@@ -46,6 +51,8 @@ def compare() -> dict:
     tmp = Path(tempfile.mkdtemp())
     free = runner(["--engine", "ref", "--runs", "1"])
     gen = np.array(free["tokens"], np.int32)            # [4][128]
+    free_runs = {m: np.array(runner(["--engine", "tvp", "--mode", m, "--runs", "1"])["tokens"],
+                             np.int32) for m in ("compat", "fast", "batched", "native")}
     forced = gen[:, :-1]                                 # inputs of decode steps 0..126
     (tmp / "forced.json").write_text(json.dumps(forced.tolist()))
     logs = {}
@@ -87,7 +94,21 @@ def compare() -> dict:
         rfirst, ofirst = results["ref"]["first_tokens"], results[name]["first_tokens"]
         first_gaps = [gap(np.asarray(logs["ref_prefill"][r], np.float32), rfirst[r], ofirst[r])
                       for r in range(len(rfirst)) if rfirst[r] != ofirst[r]]
+        # first differing index of each free-running sequence (None: identical),
+        # and the first teacher-forced disagreement, as a token index (step + 1)
+        free_div, forced_div = [], []
+        for r in range(gen.shape[0]):
+            d = np.nonzero(free_runs[name][r] != gen[r])[0]
+            free_div.append(int(d[0]) if d.size else None)
+            if rfirst[r] != ofirst[r]:
+                forced_div.append(0)
+            else:
+                e = np.nonzero(ours[r] != rtok[r])[0]
+                forced_div.append(int(e[0]) + 1 if e.size else None)
         summary[name] = {
+            "free_running_identical": [d is None for d in free_div],
+            "free_running_first_divergence": free_div,
+            "teacher_forced_first_disagreement": forced_div,
             "first_tokens_match": rfirst == ofirst,
             "first_token_gap_bf16_ulps": sorted(first_gaps),
             "argmax_agreement": float(agree.mean()),
