@@ -22,6 +22,7 @@
 
 #include "argmax.cuh"
 #include "embedding.cuh"
+#include "rmsnorm.cuh"
 #include "paged_transformer.cuh"
 #include "request.cuh"
 #include "scheduler.cuh"
@@ -132,6 +133,67 @@ int e2e_generate(const int* prompts, int num_requests, int prompt_len, int max_n
       out_counts[r] = (int)g.size();
       for (int i = 0; i < max_new; ++i) out_tokens[(size_t)r * max_new + i] = i < (int)g.size() ? g[i] : -1;
     }
+    return 0;
+  } catch (const std::invalid_argument&) {
+    return -1;
+  } catch (const std::exception&) {
+    return -2;
+  }
+}
+
+// The reference's RMSNorm over `rows` rows of 2048 (src/model/rmsNorm.cu:3-22),
+// launched with the shape its engine uses (paged_transformer.cu:68), on the
+// legacy default stream.
+int e2e_ref_rmsnorm(void* input, void* output, void* gain, int rows) {
+  rmsNormKernel<<<rows, 1024>>>(static_cast<__nv_bfloat16*>(input),
+                                static_cast<__nv_bfloat16*>(output),
+                                static_cast<__nv_bfloat16*>(gain));
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+// Continuous batching over ragged requests: request r has prompt
+// prompts[prompt_offsets[r] .. prompt_offsets[r + 1]) and max_new[r] new
+// tokens; generateContinuous runs them through max_batch slots.  out_tokens:
+// [num_requests][max_out] (-1 padded), out_counts[r] tokens generated.
+// The scheduler's events are written as records of
+//   {iteration, slot, request_id, admitted, free_blocks, n_blocks, blocks[n_blocks]}
+// into events (capacity events_cap ints); *events_len is the ints written.
+int e2e_generate_requests(const int* prompts, const int* prompt_offsets, const int* max_new,
+                          int num_requests, int max_batch, int max_seq_len, int max_out,
+                          int* out_tokens, int* out_counts, int* events, int events_cap,
+                          int* events_len) {
+  if (!g_model || num_requests < 0) return -1;
+  try {
+    std::vector<Request> requests(num_requests);
+    for (int r = 0; r < num_requests; ++r) {
+      requests[r].request_id = r;
+      requests[r].prompt_tokens.assign(prompts + prompt_offsets[r], prompts + prompt_offsets[r + 1]);
+      requests[r].max_new_tokens = max_new[r];
+    }
+    std::vector<SchedulerEvent> ev;
+    generateContinuous(g_model->handle, g_model->weights, requests, max_batch, max_seq_len, &ev);
+    if (cudaDeviceSynchronize() != cudaSuccess) return -2;
+    for (int r = 0; r < num_requests; ++r) {
+      const auto& g = requests[r].generated_tokens;
+      out_counts[r] = (int)g.size();
+      for (int i = 0; i < max_out; ++i) out_tokens[(size_t)r * max_out + i] = i < (int)g.size() ? g[i] : -1;
+      if (!requests[r].finished || !requests[r].kv_state.block_table.empty() ||
+          requests[r].kv_state.current_seq_len != 0)
+        return -3;  // a finished request must hold no pages
+    }
+    int n = 0;
+    for (const auto& e : ev) {
+      const int need = 6 + (int)e.blocks.size();
+      if (n + need > events_cap) return -4;
+      events[n++] = e.iteration;
+      events[n++] = e.slot;
+      events[n++] = e.request_id;
+      events[n++] = e.admitted ? 1 : 0;
+      events[n++] = e.free_blocks;
+      events[n++] = (int)e.blocks.size();
+      for (int b : e.blocks) events[n++] = b;
+    }
+    *events_len = n;
     return 0;
   } catch (const std::invalid_argument&) {
     return -1;

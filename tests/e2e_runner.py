@@ -29,6 +29,59 @@ def prompts(requests: int, length: int, seed: int) -> np.ndarray:
     return np.random.default_rng(seed).integers(0, 128000, size=(requests, length)).astype(np.int32)
 
 
+# Continuous-batching scenario: 7 requests with ragged prompts and output
+# lengths through 3 slots (as the reference's batch test drives its scheduler,
+# tests/paged_inference_test.cu:149-224), context cap 128.
+SCHED_PROMPTS = [37, 12, 64, 5, 90, 23, 48]
+SCHED_NEW = [9, 3, 14, 1, 6, 11, 4]
+SCHED_SLOTS = 3
+SCHED_MAX_SEQ = 128
+
+
+def generate_requests(lib, prompt_list, max_new, slots, max_seq):
+    i32p = ctypes.POINTER(ctypes.c_int32)
+    flat = np.ascontiguousarray(np.concatenate([np.asarray(x, np.int32) for x in prompt_list]),
+                                np.int32)
+    offs = np.concatenate([[0], np.cumsum([len(x) for x in prompt_list])]).astype(np.int32)
+    new = np.asarray(max_new, np.int32)
+    n = len(prompt_list)
+    max_out = max(1, int(new.max()))
+    out = np.zeros((n, max_out), np.int32)
+    counts = np.zeros(n, np.int32)
+    ev = np.zeros(1 << 16, np.int32)
+    ev_len = ctypes.c_int(0)
+    lib.e2e_generate_requests.argtypes = [i32p, i32p, i32p, ctypes.c_int, ctypes.c_int,
+                                          ctypes.c_int, ctypes.c_int, i32p, i32p, i32p,
+                                          ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
+    rc = lib.e2e_generate_requests(flat.ctypes.data_as(i32p), offs.ctypes.data_as(i32p),
+                                   new.ctypes.data_as(i32p), n, slots, max_seq, max_out,
+                                   out.ctypes.data_as(i32p), counts.ctypes.data_as(i32p),
+                                   ev.ctypes.data_as(i32p), ev.size, ctypes.byref(ev_len))
+    if rc != 0:
+        raise SystemExit(f"generateContinuous failed ({rc})")
+    events, i = [], 0
+    while i < ev_len.value:
+        it, slot, rid, adm, free, nb = (int(x) for x in ev[i:i + 6])
+        events.append({"iteration": it, "slot": slot, "request_id": rid, "admitted": bool(adm),
+                       "free_blocks": free, "blocks": ev[i + 6:i + 6 + nb].tolist()})
+        i += 6 + nb
+    tokens = [out[r, :counts[r]].tolist() for r in range(n)]
+    return tokens, events
+
+
+def scheduler_case(lib, seed):
+    rng = np.random.default_rng(seed + 17)
+    plist = [rng.integers(0, 128000, size=L).astype(np.int32) for L in SCHED_PROMPTS]
+    tokens, events = generate_requests(lib, plist, SCHED_NEW, SCHED_SLOTS, SCHED_MAX_SEQ)
+    single = [generate_requests(lib, [plist[r]], [SCHED_NEW[r]], 1, SCHED_MAX_SEQ)[0][0]
+              for r in range(len(plist))]
+    edge_tokens, edge_events = generate_requests(lib, [np.array([128000], np.int32), plist[0]],
+                                                 [0, 1], 1, SCHED_MAX_SEQ)
+    return {"slots": SCHED_SLOTS, "max_seq_len": SCHED_MAX_SEQ, "max_new": SCHED_NEW,
+            "prompt_lens": SCHED_PROMPTS, "continuous": tokens, "events": events,
+            "single": single, "edge_tokens": edge_tokens, "edge_events": edge_events}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--engine", choices=sorted(LIBS), required=True)
@@ -41,6 +94,9 @@ def main():
     ap.add_argument("--runs", type=int, default=2)
     ap.add_argument("--teacher-forced", help="JSON file: tokens [requests][steps] fed as decode inputs")
     ap.add_argument("--logits-out", help="with --teacher-forced: .npy of FP32 logits [steps][requests][vocab]")
+    ap.add_argument("--scheduler-case", action="store_true",
+                    help="continuous batching of ragged requests through fewer slots, each "
+                         "request alone, and the 0- and 1-token edge requests (JSON out)")
     args = ap.parse_args()
     os.environ["TVP_DECODE_MODE"] = args.mode
     lib = ctypes.CDLL(os.fspath(LIBS[args.engine]))
@@ -50,6 +106,10 @@ def main():
                                  ctypes.c_int, i32p, i32p, ctypes.POINTER(ctypes.c_double)]
     if lib.e2e_init(args.seed) != 0:
         raise SystemExit("weight setup failed")
+    if args.scheduler_case:
+        json.dump(scheduler_case(lib, args.seed), sys.stdout)
+        print()
+        return
     p = prompts(args.requests, args.prompt, args.seed)
     if args.teacher_forced:
         forced = np.ascontiguousarray(json.load(open(args.teacher_forced)), dtype=np.int32)

@@ -64,3 +64,17 @@ def test_workspace_is_reusable():
         assert np.array_equal(run(x, workspace=ws), oracle.greedy_argmax(x))
     counters = ws[-4 * 4:].view(torch.int32)  # the per-row counters end the workspace
     assert int(counters.abs().sum()) == 0
+
+
+def test_workspace_serves_calls_of_any_row_count():
+    """A decode loop's batch shrinks and grows as requests finish and slots
+    refill; one workspace sized for the largest batch serves every call.  Rows
+    4, then 1, 3, 2, 4, 1: each call's tokens are the oracle's."""
+    rng = np.random.default_rng(19)
+    lib = N.load()
+    ws = torch.zeros(lib.tvp_greedy_argmax_workspace_bytes(4), dtype=torch.uint8, device="cuda")
+    for rows in (4, 1, 3, 2, 4, 1):
+        x = rng.normal(size=(rows, VOCAB)).astype(np.float32)
+        assert np.array_equal(run(x, workspace=ws), oracle.greedy_argmax(x)), rows
+    counters = ws[-4 * 4:].view(torch.int32)
+    assert int(counters.abs().sum()) == 0

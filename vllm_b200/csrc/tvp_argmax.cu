@@ -15,6 +15,15 @@
 // better candidate and a plain max merges them.  The last block of a row to
 // finish (a counter per row) merges the row's kChunks keys and writes the
 // token; it then zeroes the counter for the next call.
+//
+// Workspace: the row keys from the start, the per-row counters at the end,
+// counter r in the (r + 1)-th int from the end.  A counter's place depends
+// only on the workspace's size, never on the row count of a call, so one
+// workspace serves calls with any number of rows: every counter a call reads
+// was zeroed by the call that last used it (or by the caller, once), and the
+// keys, which a call writes before it reads them, never share bytes with a
+// counter.  (With the counters right after `rows` rows of keys, a call with
+// fewer rows than the one before would read that call's keys as counters.)
 #include <cuda_bf16.h>
 
 #include "tvp_common.cuh"
@@ -57,8 +66,9 @@ __device__ __forceinline__ unsigned long long block_max(unsigned long long key,
 
 __global__ void __launch_bounds__(kArgmaxThreads)
     greedy_argmax_kernel(const float* __restrict__ logits, int vocab, long long row_stride,
-                         unsigned long long* __restrict__ partials, int* __restrict__ counters,
+                         unsigned long long* __restrict__ partials, int* __restrict__ counters_end,
                          int32_t* __restrict__ tokens) {
+  int* const counter = counters_end - 1 - blockIdx.y;  // this row's counter
   __shared__ unsigned long long warp_keys[kArgmaxThreads / 32];
   __shared__ int is_last;
   const int row = blockIdx.y, chunk = blockIdx.x;
@@ -74,7 +84,7 @@ __global__ void __launch_bounds__(kArgmaxThreads)
   if (threadIdx.x == 0) {
     partials[(size_t)row * kChunks + chunk] = best;
     __threadfence();
-    is_last = atomicAdd(counters + row, 1) == kChunks - 1;
+    is_last = atomicAdd(counter, 1) == kChunks - 1;
   }
   __syncthreads();
   if (!is_last) return;
@@ -86,7 +96,7 @@ __global__ void __launch_bounds__(kArgmaxThreads)
     const float first = __bfloat162float(__float2bfloat16_rn(x[0]));
     // k != 0 whenever logit 0 is a number (it is a candidate itself)
     tokens[row] = (first != first || k == 0ull) ? 0 : (int32_t)(~(uint32_t)(k & 0xffffffffull));
-    counters[row] = 0;
+    *counter = 0;
   }
 }
 
@@ -108,12 +118,13 @@ int tvp_greedy_argmax(const float* d_logits, int rows, int vocab, long long row_
   if (!d_logits || !d_tokens || rows <= 0 || rows > 65535 || vocab <= 0 || row_stride < vocab)
     return TVP_ERR_INVALID_ARGUMENT;
   if (!d_workspace || workspace_bytes < tvp_greedy_argmax_workspace_bytes(rows) ||
-      (reinterpret_cast<uintptr_t>(d_workspace) & 7u))
+      (reinterpret_cast<uintptr_t>(d_workspace) & 7u) || (workspace_bytes & 3u))
     return TVP_ERR_WORKSPACE;
   auto* partials = static_cast<unsigned long long*>(d_workspace);
-  int* counters = reinterpret_cast<int*>(partials + (size_t)rows * kChunks);
+  // counter r at ints_total - 1 - r (see the workspace note above)
+  int* counters_end = reinterpret_cast<int*>(static_cast<char*>(d_workspace) + workspace_bytes);
   greedy_argmax_kernel<<<dim3(kChunks, rows), kArgmaxThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      d_logits, vocab, row_stride, partials, counters, d_tokens);
+      d_logits, vocab, row_stride, partials, counters_end, d_tokens);
   return cudaGetLastError() == cudaSuccess ? TVP_OK : TVP_ERR_RUNTIME;
 }
 
