@@ -192,11 +192,26 @@ def test_sweep_sample_rows():
     out, err = run_decode(case)
     assert err == 0
     assert_close_bf16(out, exact_out(case), ATOL, RTOL, "sweep sample")
-    # COMPAT keeps whole rows in shared memory: rows up to 4096 tokens
-    short = W.decode_random(92, np.minimum(lens, 4096))
-    compat, err = run_decode(short, mode=N.TVP_MODE_COMPAT)
+    # COMPAT on the same rows (up to 8192 tokens: two 4096-token chunks)
+    compat, err = run_decode(case, mode=N.TVP_MODE_COMPAT)
     assert err == 0
-    assert_close_bf16(compat, exact_out(short), ATOL, RTOL, "sweep sample compat")
+    assert_close_bf16(compat, exact_out(case), ATOL, RTOL, "sweep sample compat")
+
+
+@pytest.mark.parametrize("lens", [[32768, 20000, 5], [4096, 4097, 8191, 8192, 12289, 1]])
+def test_compat_rows_beyond_one_chunk_match_oracle_to_an_ulp(lens):
+    """COMPAT sums rows longer than its 4096-token shared-memory chunk chunk by
+    chunk, in the reference's pairwise-tree order over the whole row: against
+    the oracle (the same tree over the whole row, computed on the CPU) it stays
+    within one BF16 ulp on a small fraction of outputs, as on short rows."""
+    case = W.decode_random(95 + len(lens), lens)
+    out, err = run_decode(case, mode=N.TVP_MODE_COMPAT)
+    assert err == 0
+    a, e = f32(out), f32(oracle_out(case))
+    diff = np.abs(a - e)
+    assert (diff <= np.maximum(np.abs(e) * 2.0 ** -7, 1e-3)).all()
+    assert (diff > 0).mean() < 0.05
+    assert_close_bf16(out, exact_out(case), ATOL, RTOL, "compat long rows vs exact")
 
 
 def test_fast_path_agrees_with_reference_gather_cublas(ref_lib):
