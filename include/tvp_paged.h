@@ -72,7 +72,7 @@ typedef void* tvp_stream_t;  /* cudaStream_t */
 #define TVP_MODE_FAST 0
 /* COMPAT: the reference's rounding points (src/model/attention.cu:53-142,
  * src/model/softmax.cu:6-45): BF16 scores, exact max, expf, pairwise-tree sum,
- * BF16 probabilities, FP32 P.V, BF16 output.  Lengths up to 4096. */
+ * BF16 probabilities, FP32 P.V, BF16 output.  Lengths up to 1,048,576. */
 #define TVP_MODE_COMPAT 1
 
 /* ---- flags of tvp_rope_append ------------------------------------------ */
@@ -183,10 +183,12 @@ int tvp_paged_prefill_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const
  * (src/model/argmax.cu:16-45): logits rounded to BF16, NaNs skipped, the
  * largest value wins with ties to the lowest index, and a row whose logit 0
  * is NaN selects 0.  d_logits: FP32 [rows][row_stride] (row_stride >= vocab);
- * d_tokens: int32 [rows], written on `stream`.  The workspace
- * (tvp_greedy_argmax_workspace_bytes(rows), 8-byte aligned) must be zeroed
- * once before its first use; every call leaves it zeroed.  Calls that share a
- * workspace must not overlap on the GPU.
+ * d_tokens: int32 [rows], written on `stream`.  The workspace (at least
+ * tvp_greedy_argmax_workspace_bytes(rows) bytes, 8-byte aligned, size a
+ * multiple of 4) must be zeroed once before its first use; every call leaves
+ * it zeroed, and one workspace serves calls of any row count up to what its
+ * size allows (its per-row counters sit at fixed places from its end).  Calls
+ * that share a workspace must not overlap on the GPU.
  */
 size_t tvp_greedy_argmax_workspace_bytes(int rows);
 int tvp_greedy_argmax(const float* d_logits, int rows, int vocab, long long row_stride,

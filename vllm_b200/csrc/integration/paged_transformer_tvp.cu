@@ -9,7 +9,8 @@
 //   prefill  rope(q), rope(k), storePagedKV        (paged_transformer.cu:34-36)
 //            -> one tvp_rope_append
 //   decode   preparePagedBatch's per-step mallocs  (paged_transformer.cu:65,135)
-//            -> persistent device tables + one tvp_decode_plan per step
+//            -> persistent device tables updated in place (only the entries
+//               that changed, asynchronously) + one tvp_decode_plan per step
 //            ropeBatch(q), ropeBatch(k), storePagedKVBatch, the paged gather,
 //            32*B score GEMVs, 32*B softmax launches, the second gather and
 //            32*B P.V GEMVs                        (paged_transformer.cu:80-94)
@@ -98,6 +99,12 @@ void check_tvp(int rc) {
 struct PathState {
   int32_t* prefill = nullptr;  // [table (64) | positions (1024) | rows (1024) | cu_q (2) | pos0 (1)]
   int32_t* decode = nullptr;   // [tables (4 x 64) | positions (4) | lengths (4)]
+  // Pinned mirror of `decode` as last uploaded: a step copies only the
+  // entries that differ from it (the positions and lengths, and a table row
+  // when it gained a page or its slot took a new request), asynchronously on
+  // the stream the step runs on.
+  int32_t* h_decode = nullptr;
+  bool h_decode_valid = false;
   int32_t* error = nullptr;    // [error word | tokens (kMaxBatch)]: one read per step
   void* workspace = nullptr;
   size_t workspace_bytes = 0;
@@ -133,6 +140,8 @@ PathState& path_state() {
                           (kTableStride + 2 * kMaxContext + 4) * sizeof(int32_t)));
     check_cuda(cudaMalloc(reinterpret_cast<void**>(&st.decode),
                           (kMaxBatch * kTableStride + 2 * kMaxBatch) * sizeof(int32_t)));
+    check_cuda(cudaMallocHost(reinterpret_cast<void**>(&st.h_decode),
+                              (kMaxBatch * kTableStride + 2 * kMaxBatch) * sizeof(int32_t)));
     check_cuda(cudaMalloc(reinterpret_cast<void**>(&st.error), (1 + kMaxBatch) * sizeof(int32_t)));
     check_cuda(cudaMemset(st.error, 0, (1 + kMaxBatch) * sizeof(int32_t)));
     st.argmax_workspace_bytes = tvp_greedy_argmax_workspace_bytes(kMaxBatch);
@@ -154,6 +163,37 @@ PathState& path_state() {
     ready[dev] = true;
   }
   return st;
+}
+
+// Brings st.decode up to `want` with one cudaMemcpyAsync per run of changed
+// entries inside a table row or the positions/lengths block, from the pinned
+// mirror, on `stream` (ahead of the step's kernels there).  The mirror entries
+// a copy reads are not rewritten before the copy ran: every step ends with a
+// synchronisation with the device (the token read) before the next one starts.
+void upload_decode_tables(PathState& st, const std::vector<int32_t>& want, cudaStream_t stream) {
+  const int regions[kMaxBatch + 1][2] = {
+      {0, kTableStride}, {kTableStride, 2 * kTableStride}, {2 * kTableStride, 3 * kTableStride},
+      {3 * kTableStride, 4 * kTableStride}, {kMaxBatch * kTableStride,
+                                             kMaxBatch * kTableStride + 2 * kMaxBatch}};
+  static_assert(kMaxBatch == 4, "one region per table row plus positions/lengths");
+  for (const auto& region : regions) {
+    int i = region[0];
+    while (i < region[1]) {
+      if (st.h_decode_valid && st.h_decode[i] == want[i]) {
+        ++i;
+        continue;
+      }
+      int j = i;
+      while (j < region[1] && !(st.h_decode_valid && st.h_decode[j] == want[j])) {
+        st.h_decode[j] = want[j];
+        ++j;
+      }
+      check_cuda(cudaMemcpyAsync(st.decode + i, st.h_decode + i, (j - i) * sizeof(int32_t),
+                                 cudaMemcpyHostToDevice, stream));
+      i = j;
+    }
+  }
+  st.h_decode_valid = true;
 }
 
 void raise_device_errors(PathState& st) {
@@ -273,8 +313,10 @@ std::vector<int> decodeBatchPaged(cublasHandle_t cublas_handle, __nv_bfloat16* h
     staging[kMaxBatch * kTableStride + kMaxBatch + row] = sequence.current_seq_len + 1;
   }
   PathState& st = path_state();
-  check_cuda(cudaMemcpy(st.decode, staging.data(), staging.size() * sizeof(int32_t),
-                        cudaMemcpyHostToDevice));
+  // Only what changed since the last step, asynchronously on the step's
+  // stream: the legacy default stream (compat, fast) or the batched step's
+  // stream, where the graph launch follows it.
+  upload_decode_tables(st, staging, st.batched ? st.stream : nullptr);
   const int32_t* d_tables = st.decode;
   const int32_t* d_pos = st.decode + kMaxBatch * kTableStride;
   const int32_t* d_len = d_pos + kMaxBatch;
