@@ -20,13 +20,14 @@
 // (sequence, KV head), no waiting).
 //
 // CTA layout: one producer warp and SETS x 8 consumer warps.  The producer
-// streams one page per stage into shared memory with tiled TMA loads: per KV
-// head one 2 KiB box {64 channels x 16 tokens} of K and one of V, through 2-D
-// tensor maps over the pools (rows of 512 channels), 128-byte swizzled so that
-// the consumers' ldmatrix reads of 8 tokens hit 8 different bank groups.  A
-// box is the largest unit that is contiguous in a page *and* swizzlable;
-// one bulk copy per 1 KiB token row streamed at only ~4.4 TB/s on B200,
-// these boxes stream at the copy roofline.
+// streams one page per stage into shared memory with two tiled TMA loads, one
+// box {64 channels x 16 tokens x 8 heads} of K and one of V, through 3-D
+// tensor maps that view a pool's rows of 512 channels as (channel, token,
+// head).  Each box lands as eight head-major 2 KiB tiles, 128-byte swizzled so
+// that the consumers' ldmatrix reads of 8 tokens hit 8 different bank groups.
+// (One 2-D box per head and page, sixteen TMA instructions per page, left the
+// producer issue-bound at ~0.84 of the HBM rate; one bulk copy per 1 KiB token
+// row streamed at only ~4.4 TB/s.)
 // Consumer warp g of set s owns KV head g on the pages i of each sequence
 // piece with i % SETS == s (the sets' states are merged at the piece's end).
 // With an odd number of stages consecutive rounds of a stage go to different
@@ -221,13 +222,14 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
         mbar_arrive_expect_tx(full, ok ? (uint32_t)kStageBytes : 0u);
       }
       __syncwarp();
-      if (ok && lane < 2 * kMaxKvHeads) {
-        // lanes 0-7: K box of head `lane`; lanes 8-15: V box of head `lane - 8`
-        const int h = lane & (kMaxKvHeads - 1);
-        const uint32_t dst = smem_base + stage * kStageBytes +
-                             (lane < kMaxKvHeads ? 0 : kMaxKvHeads * kTileBytes) + h * kTileBytes;
-        tma_load_2d(dst, lane < kMaxKvHeads ? &k_map : &v_map, h * kHeadDim,
-                    (int)(p.layer_row_base + (long long)phys * kPage), full);
+      if (ok && lane < 2) {
+        // lane 0: the page's K, lane 1: its V, each as one box of all 8 heads
+        // (16 KiB, landing as 8 head-major 2 KiB tiles).  One TMA instruction
+        // per 2 KiB head tile took ~0.6 us per page to issue, longer than the
+        // page takes to stream at the HBM rate; two take ~0.1 us.
+        const uint32_t dst = smem_base + stage * kStageBytes + lane * kMaxKvHeads * kTileBytes;
+        tma_load_3d(dst, lane == 0 ? &k_map : &v_map, 0,
+                    (int)(p.layer_row_base + (long long)phys * kPage), 0, full);
       }
       issued = kk + 1;
       if (++stage == STAGES) {
@@ -469,6 +471,37 @@ bool pool_tensor_map(const void* pool, long long rows, int kv_heads, CUtensorMap
   return true;
 }
 
+bool page_tensor_map(const void* pool, long long rows, int kv_heads, CUtensorMap* out) {
+  struct Entry {
+    const void* pool;
+    long long rows;
+    int kv_heads;
+    CUtensorMap map;
+  };
+  static thread_local Entry cache[4];
+  static thread_local int next = 0;
+  for (const Entry& e : cache)
+    if (e.pool == pool && e.rows == rows && e.kv_heads == kv_heads) {
+      *out = e.map;
+      return true;
+    }
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)rows, (cuuint64_t)kv_heads};
+  const cuuint64_t strides[2] = {(cuuint64_t)(kv_heads * kHeadDim * 2), (cuuint64_t)(kHeadDim * 2)};
+  const cuuint32_t box[3] = {(cuuint32_t)kHeadDim, (cuuint32_t)kPage, (cuuint32_t)kv_heads};
+  const cuuint32_t elem_strides[3] = {1, 1, 1};
+  CUtensorMap map;
+  if (encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(pool), dims, strides,
+             box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  cache[next] = {pool, rows, kv_heads, map};
+  next = (next + 1) % 4;
+  *out = map;
+  return true;
+}
+
 namespace {
 
 enum class DecodeForm { kUnknown, kSplit, kPlain };
@@ -503,9 +536,14 @@ cudaError_t launch_paged_decode(const DecodeParams& p, long long pool_rows, int 
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  // Page boxes (3-D maps) for pools of 2 or more heads; a 1-head pool's page
+  // of one head is already one 2 KiB box of the 2-D map.
   CUtensorMap k_map, v_map;
-  if (!pool_tensor_map(p.k_pool, pool_rows, p.kv_heads, &k_map) ||
-      !pool_tensor_map(p.v_pool, pool_rows, p.kv_heads, &v_map))
+  const bool paged = p.kv_heads > 1;
+  if (!(paged ? page_tensor_map(p.k_pool, pool_rows, p.kv_heads, &k_map)
+              : pool_tensor_map(p.k_pool, pool_rows, p.kv_heads, &k_map)) ||
+      !(paged ? page_tensor_map(p.v_pool, pool_rows, p.kv_heads, &v_map)
+              : pool_tensor_map(p.v_pool, pool_rows, p.kv_heads, &v_map)))
     return cudaErrorInvalidValue;
   if (p.kv_heads != kMaxKvHeads) return launch_paged_decode_heads(p, k_map, v_map, num_ctas, stream);
   const DecodeForm form = decode_form(dev);

@@ -203,14 +203,20 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
         mbar_arrive_expect_tx(full, (uint32_t)(__popc(mask) * KVH * 2 * kTileBytes));
       }
       __syncwarp();
-      // lanes 0-7: K tile t = lane, lanes 8-15: V tile t = lane - 8
-      const int t = lane & (kStageTiles - 1), o = t / KVH, h = t % KVH;
+      // lanes 0..PS-1: the K box of page o = lane, lanes PS..2PS-1: its V box;
+      // a box holds the page's KVH heads and lands as KVH tiles t = o KVH + h
+      // (a 3-D page box for KVH > 1, the one-head box of the 2-D map for 1).
+      const int o = lane % PS;
       const int tile_phys = __shfl_sync(0xffffffffu, cur_phys, o);
-      if (lane < 2 * kStageTiles && ((mask >> o) & 1u)) {
+      if (lane < 2 * PS && ((mask >> o) & 1u)) {
+        const bool is_v = lane >= PS;
         const uint32_t dst = smem_base + stage * kStageBytes +
-                             (lane < kStageTiles ? 0 : kStageTiles * kTileBytes) + t * kTileBytes;
-        tma_load_2d(dst, lane < kStageTiles ? &k_map : &v_map, h * kHeadDim,
-                    (int)(p.layer_row_base + (long long)tile_phys * kPage), full);
+                             (is_v ? kStageTiles * kTileBytes : 0) + o * KVH * kTileBytes;
+        const int y = (int)(p.layer_row_base + (long long)tile_phys * kPage);
+        if (KVH > 1)
+          tma_load_3d(dst, is_v ? &v_map : &k_map, 0, y, 0, full);
+        else
+          tma_load_2d(dst, is_v ? &v_map : &k_map, 0, y, full);
       }
       issued = kk + 1;
       if (++stage == STAGES) {

@@ -118,8 +118,14 @@ int prepare_decode(const void* q, const void* k_pool, const void* v_pool, int nu
                    int batch, float scale, int num_ctas, void* d_workspace,
                    size_t workspace_bytes, int32_t* d_error, DecodeParams* p, long long* pool_rows,
                    int* ctas);
-// 2-D tensor map over a pool of `rows` token rows of kv_heads x 64 channels.
+// 2-D tensor map over a pool of `rows` token rows of kv_heads x 64 channels;
+// box = one KV head of one page (64 channels x 16 rows).
 bool pool_tensor_map(const void* pool, long long rows, int kv_heads, CUtensorMap* out);
+// 3-D view of the same pool, (channel, row, head) with strides (2 B,
+// kv_heads x 128 B, 128 B); box = a whole page of every head ({64, 16,
+// kv_heads}), which lands as kv_heads head-major 2 KiB tiles with the same
+// 128-byte swizzle as kv_heads boxes of the 2-D map.
+bool page_tensor_map(const void* pool, long long rows, int kv_heads, CUtensorMap* out);
 cudaError_t launch_compat_decode(const CompatParams& p, int batch, cudaStream_t stream);
 cudaError_t launch_paged_prefill(const PrefillParams& p, long long pool_rows, int max_q_len,
                                  int num_seqs, cudaStream_t stream);
