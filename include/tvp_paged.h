@@ -235,6 +235,48 @@ int tvp_decode_projections(const tvp_bf16* x, int rows, int k, int count, const 
                            const int* n, void* const* out, int epilogue, tvp_stream_t stream);
 
 /*
+ * K5 with TVP_PROJ_RESIDUAL into the hidden rows, followed in the same launch
+ * by the decode step's next RMSNorm: the O and down projections with their
+ * residualAdd (src/model/resConnection.cu:6-17) and the rmsNormKernel launch
+ * after each (src/model/paged_transformer.cu:68,103,116; src/model/rmsNorm.cu:
+ * 3-22), bit for bit.  w: [2048][k]; hidden: [rows][2048] BF16 (updated in
+ * place: hidden += bf16(w x)); then norm_out[t] = bf16((hidden[t] / r_t) g)
+ * with r_t = sqrt(sum_i hidden[t][i]^2 / 2048 + 1e-5), the sum taken in the
+ * reference kernel's order.  The last CTA of the launch computes the norm;
+ * d_counter (one int32 of device memory, zeroed once before first use) counts
+ * the finished CTAs and is zeroed again by that CTA.  rows 1..8, k a multiple
+ * of 256; x, w, hidden, norm_gain, norm_out 16-byte aligned, norm_out
+ * overlapping none of x, hidden, norm_gain.  Programmatic dependent launch,
+ * as tvp_decode_projections.  Launches that share d_counter must not overlap.
+ */
+int tvp_decode_projection_residual_rmsnorm(const tvp_bf16* x, int rows, int k, const tvp_bf16* w,
+                                           tvp_bf16* hidden, const tvp_bf16* norm_gain,
+                                           tvp_bf16* norm_out, int32_t* d_counter,
+                                           tvp_stream_t stream);
+
+/*
+ * K5's Q, K and V projections of one decode token per row, with K1's work in
+ * the epilogue: the reference's qProjection, kProjection, vProjection
+ * (src/model/attention.cu:194-323), ropeBatch of q and k (src/model/RoPe.cu:
+ * 46-62) and storePagedKVBatch (src/model/paged_attention.cu:89-99,123-131)
+ * in one launch, with tvp_rope_append's arithmetic bit for bit.  x: [rows][k]
+ * BF16 (the normalised hidden rows); w_q [2048][k], w_k and w_v [512][k]
+ * (32 query heads, 8 KV heads of 64).  Row t's token sits at position
+ * d_positions[t] of block-table row t: q_out[t] gets its rotated q; its
+ * rotated k and its v go into slot pos % 16 of page
+ * d_block_tables[t * table_stride + pos / 16] of layer `layer` of the pools
+ * (8 KV heads, the reference layout).  A bad position or page id sets
+ * TVP_DEVERR_BAD_TOKEN / TVP_DEVERR_BAD_PAGE in *d_error and that store is
+ * skipped.  rows 1..8, k a multiple of 256, x and weights 16-byte aligned.
+ * Programmatic dependent launch, as tvp_decode_projections.
+ */
+int tvp_decode_qkv_rope_append(const tvp_bf16* x, int rows, int k, const tvp_bf16* w_q,
+                               const tvp_bf16* w_k, const tvp_bf16* w_v, tvp_bf16* q_out,
+                               tvp_bf16* k_pool, tvp_bf16* v_pool, int num_pages, int num_layers,
+                               int layer, const int32_t* d_block_tables, int table_stride,
+                               const int32_t* d_positions, int32_t* d_error, tvp_stream_t stream);
+
+/*
  * K2 without any allocation.  This entry point has no counterpart in the
  * reference.  It is for callers that cannot call cudaMalloc: code whose
  * device memory is owned by a host framework's pool, plug-ins running under a

@@ -202,3 +202,25 @@ def test_noalloc_checks_every_argument_and_its_limit_on_host(native):
         assert native.tvp_decode_workspace_bytes(rows, heads, 148) <= limit
         assert native.tvp_decode_workspace_bytes(rows + 1, heads, 148) > limit
         assert call(kvh=heads, qh=4 * heads, batch=rows + 1) == N.TVP_ERR_WORKSPACE
+
+
+def test_fused_projection_forms_reject_bad_arguments_on_host(native):
+    fake = ctypes.c_void_p(0x10000)
+    odd = ctypes.c_void_p(0x10008)
+    f = native.tvp_decode_projection_residual_rmsnorm
+    assert f(None, 4, 2048, fake, fake, fake, ctypes.c_void_p(0x20000), fake, None) == N.TVP_ERR_INVALID_ARGUMENT
+    assert f(fake, 9, 2048, fake, ctypes.c_void_p(0x20000), fake, ctypes.c_void_p(0x30000), fake,
+             None) == N.TVP_ERR_INVALID_ARGUMENT                      # rows 1..8
+    assert f(fake, 4, 100, fake, ctypes.c_void_p(0x20000), fake, ctypes.c_void_p(0x30000), fake,
+             None) == N.TVP_ERR_INVALID_ARGUMENT                      # k a multiple of 256
+    assert f(fake, 4, 2048, fake, ctypes.c_void_p(0x20000), fake, odd, fake,
+             None) == N.TVP_ERR_INVALID_ARGUMENT                      # 16-byte alignment
+    assert f(fake, 4, 2048, fake, ctypes.c_void_p(0x20000), fake, ctypes.c_void_p(0x20000), fake,
+             None) == N.TVP_ERR_INVALID_ARGUMENT                      # norm_out overlaps hidden
+    g = native.tvp_decode_qkv_rope_append
+    args = [fake, 4, 2048, fake, fake, fake, ctypes.c_void_p(0x40000), fake, fake, 8, 16, 0, fake, 4,
+            fake, None, None]
+    assert g(*args[:11], 16, *args[12:]) == N.TVP_ERR_INVALID_ARGUMENT  # layer out of range
+    assert g(*args[:1], 0, *args[2:]) == N.TVP_ERR_INVALID_ARGUMENT     # no rows
+    assert g(*args[:13], 0, *args[14:]) == N.TVP_ERR_INVALID_ARGUMENT   # table stride
+    assert g(*args[:3], odd, *args[4:]) == N.TVP_ERR_INVALID_ARGUMENT   # weight alignment

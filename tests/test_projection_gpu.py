@@ -155,3 +155,79 @@ def test_back_to_back_launches_read_the_previous_output():
     for r in results:
         assert not bool(r.isnan().any())
         assert torch.equal(r, expect)
+
+
+@pytest.mark.parametrize("rows", [1, 4, 8])
+@pytest.mark.parametrize("k", [2048, 8192])  # O projection, down projection
+def test_residual_rmsnorm_form_is_residual_add_then_the_reference_rmsnorm(reference_engine, rows, k):
+    """tvp_decode_projection_residual_rmsnorm: the residual epilogue, then (the
+    launch's last CTA) the reference's rmsNormKernel of the updated rows, bit
+    for bit; twice in a row on one counter (each launch zeroes it again)."""
+    reference_engine.e2e_ref_rmsnorm.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int]
+    x, (w,) = make(rows, k, [2048], seed=90 + rows + k)
+    g = torch.Generator(device="cuda").manual_seed(rows + 3)
+    hidden0 = (torch.randn(rows, 2048, generator=g, device="cuda") * 3).to(torch.bfloat16)
+    gain = (1 + 0.1 * torch.randn(2048, generator=g, device="cuda")).to(torch.bfloat16)
+    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    # expected: K5 residual form, then the reference kernel on its output
+    want_hidden = hidden0.clone()
+    ops.decode_projections(x, [w], outs=[want_hidden], epilogue="residual")
+    want_norm = torch.empty_like(want_hidden)
+    torch.cuda.synchronize()
+    assert reference_engine.e2e_ref_rmsnorm(want_hidden.data_ptr(), want_norm.data_ptr(),
+                                            gain.data_ptr(), rows) == 0
+    torch.cuda.synchronize()
+    for _ in range(2):
+        hidden = hidden0.clone()
+        norm = torch.full_like(hidden, float("nan"))
+        ops.decode_projection_residual_rmsnorm(x, w, hidden, gain, norm, counter)
+        torch.cuda.synchronize()
+        assert torch.equal(hidden, want_hidden)
+        assert torch.equal(norm, want_norm)
+        assert int(counter.item()) == 0
+
+
+def _pools_and_tables(rows, seed, num_pages=64, layers=3):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    kp = torch.randn(layers, num_pages, 16, 512, generator=g, device="cuda").to(torch.bfloat16)
+    vp = torch.randn(layers, num_pages, 16, 512, generator=g, device="cuda").to(torch.bfloat16)
+    perm = torch.randperm(num_pages, generator=torch.Generator().manual_seed(seed))
+    tables = perm[:rows * 8].reshape(rows, 8).to(torch.int32).cuda()
+    pos = torch.tensor([5, 127, 16, 0, 64, 100, 33, 77][:rows], dtype=torch.int32, device="cuda")
+    return kp, vp, tables, pos
+
+
+@pytest.mark.parametrize("rows", [1, 4, 8])
+def test_qkv_rope_append_form_equals_projections_then_rope_append(rows):
+    """tvp_decode_qkv_rope_append: the three projections, then K1
+    (tvp_rope_append of q and k, v as is) into the same pools, bit for bit:
+    q rows, and every page of every layer afterwards."""
+    x, (wq, wk, wv) = make(rows, 2048, [2048, 512, 512], seed=120 + rows)
+    kp, vp, tables, pos = _pools_and_tables(rows, 7 + rows)
+    layer = 1
+    q, k, v = ops.decode_projections(x, [wq, wk, wv])
+    kp_want, vp_want = kp.clone(), vp.clone()
+    err = ops.new_error_word("cuda")
+    ops.rope_append(kp_want, vp_want, layer, tables, pos, k, v, q=q, error=err)
+    q_got = torch.empty_like(q)
+    ops.decode_qkv_rope_append(x, wq, wk, wv, q_got, kp, vp, layer, tables, pos, error=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(q_got, q)
+    assert torch.equal(kp, kp_want)
+    assert torch.equal(vp, vp_want)
+
+
+def test_qkv_rope_append_reports_a_bad_page_and_skips_it():
+    x, (wq, wk, wv) = make(2, 2048, [2048, 512, 512], seed=140)
+    kp, vp, tables, pos = _pools_and_tables(2, 11)
+    tables[1, pos[1] // 16] = 10_000  # outside the pool
+    before_k, before_v = kp.clone(), vp.clone()
+    err = ops.new_error_word("cuda")
+    q = torch.empty(2, 2048, dtype=torch.bfloat16, device="cuda")
+    ops.decode_qkv_rope_append(x, wq, wk, wv, q, kp, vp, 0, tables, pos, error=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & 1  # TVP_DEVERR_BAD_PAGE
+    # row 0 was appended, row 1 touched nothing
+    changed = (kp != before_k).any(dim=-1) | (vp != before_v).any(dim=-1)
+    assert int(changed.sum()) == 1

@@ -79,6 +79,11 @@ _SIGNATURES = {
                                   c_size_t, c_void_p]),
     "tvp_decode_projections": (c_int, [c_void_p, c_int, c_int, c_int, POINTER(c_void_p),
                                        POINTER(c_int), POINTER(c_void_p), c_int, c_void_p]),
+    "tvp_decode_projection_residual_rmsnorm": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p,
+                                                       c_void_p, c_void_p, c_void_p, c_void_p]),
+    "tvp_decode_qkv_rope_append": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                           c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                           c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "tvp_head_gather_create": (c_int, [c_int, c_int, c_int, c_int, POINTER(c_void_p)]),
     "tvp_head_gather_export": (c_int, [c_void_p, c_void_p]),
     "tvp_head_gather_connect": (c_int, [c_void_p, c_void_p]),

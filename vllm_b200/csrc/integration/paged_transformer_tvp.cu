@@ -34,14 +34,17 @@
 //                     calls (argmax.cu:83-105).  The batched GEMMs sum in
 //                     another order than the one-row ones, so this mode has
 //                     its own parity policy (near-ties only, as fast).
-//   native            batched, with every projection and the LM head on
-//                     tvp_decode_projections instead of cuBLAS: Q, K and V in
-//                     one launch; O with the residual add in its epilogue;
-//                     gate and up with silu in their epilogue; down with the
-//                     residual add.  The same operands and FP32 accumulation
-//                     in another summation order (the fused residual and silu
-//                     keep the reference's rounding points), so fast's parity
-//                     policy again.
+//   native            batched, with every projection and the LM head on K5
+//                     instead of cuBLAS: Q, K and V with RoPE and the page
+//                     append in one launch (tvp_decode_qkv_rope_append); O
+//                     with the residual add and the post-attention RMSNorm
+//                     (tvp_decode_projection_residual_rmsnorm); gate and up
+//                     with silu in their epilogue; down with the residual add
+//                     and the next layer's RMSNorm.  Five launches per layer.
+//                     The same operands and FP32 accumulation in another
+//                     summation order (the fused residual, silu, RoPE and
+//                     RMSNorm keep the reference's rounding points bit for
+//                     bit), so fast's parity policy again.
 #include <cublas_v2.h>
 #include <cuda_runtime.h>
 
@@ -106,6 +109,7 @@ struct PathState {
   int32_t* h_decode = nullptr;
   bool h_decode_valid = false;
   int32_t* error = nullptr;    // [error word | tokens (kMaxBatch)]: one read per step
+  int32_t* norm_counter = nullptr;  // native mode: CTA counter of the fused RMSNorm launches
   void* workspace = nullptr;
   size_t workspace_bytes = 0;
   void* argmax_workspace = nullptr;
@@ -144,6 +148,8 @@ PathState& path_state() {
                               (kMaxBatch * kTableStride + 2 * kMaxBatch) * sizeof(int32_t)));
     check_cuda(cudaMalloc(reinterpret_cast<void**>(&st.error), (1 + kMaxBatch) * sizeof(int32_t)));
     check_cuda(cudaMemset(st.error, 0, (1 + kMaxBatch) * sizeof(int32_t)));
+    check_cuda(cudaMalloc(reinterpret_cast<void**>(&st.norm_counter), sizeof(int32_t)));
+    check_cuda(cudaMemset(st.norm_counter, 0, sizeof(int32_t)));
     st.argmax_workspace_bytes = tvp_greedy_argmax_workspace_bytes(kMaxBatch);
     check_cuda(cudaMalloc(&st.argmax_workspace, st.argmax_workspace_bytes));
     check_cuda(cudaMemset(st.argmax_workspace, 0, st.argmax_workspace_bytes));
@@ -358,23 +364,31 @@ std::vector<int> decodeBatchPaged(cublasHandle_t cublas_handle, __nv_bfloat16* h
                               st.workspace_bytes, st.error, stream));
     for (int layer = 0; layer < kLayers; ++layer) {
       const LayerWeights& lw = weights.layers[layer];
-      rmsNormKernel<<<batch, 1024, 0, stream>>>(hidden_states, buffers.rms_output, lw.input_norm);
+      // native: every RMSNorm but the first runs in the last CTA of the
+      // residual projection before it (tvp_decode_projection_residual_rmsnorm)
+      if (!st.native_proj || layer == 0)
+        rmsNormKernel<<<batch, 1024, 0, stream>>>(hidden_states, buffers.rms_output, lw.input_norm);
       if (st.native_proj) {
-        native(buffers.rms_output, kHidden, {lw.w_q, lw.w_k, lw.w_v}, {kHidden, 512, 512},
-               {buffers.q, buffers.k, buffers.v}, TVP_PROJ_BF16);
+        // Q, K, V, RoPE and the page append in one launch
+        check_tvp(tvp_decode_qkv_rope_append(
+            reinterpret_cast<const tvp_bf16*>(buffers.rms_output), batch, kHidden,
+            reinterpret_cast<const tvp_bf16*>(lw.w_q), reinterpret_cast<const tvp_bf16*>(lw.w_k),
+            reinterpret_cast<const tvp_bf16*>(lw.w_v), reinterpret_cast<tvp_bf16*>(buffers.q),
+            reinterpret_cast<tvp_bf16*>(cache.k_blocks), reinterpret_cast<tvp_bf16*>(cache.v_blocks),
+            cache.num_blocks, kLayers, layer, d_tables, kTableStride, d_pos, st.error, stream));
       } else {
         project(qProjection, buffers.rms_output, kHidden, lw.w_q, buffers.q, kHidden);
         project(kProjection, buffers.rms_output, kHidden, lw.w_k, buffers.k, 512);
         project(vProjection, buffers.rms_output, kHidden, lw.w_v, buffers.v, 512);
+        check_tvp(tvp_rope_append(reinterpret_cast<tvp_bf16*>(cache.k_blocks),
+                                  reinterpret_cast<tvp_bf16*>(cache.v_blocks), cache.num_blocks,
+                                  kLayers, layer, kKvHeads, d_tables, kTableStride, batch, nullptr,
+                                  d_pos, batch, reinterpret_cast<tvp_bf16*>(buffers.k),
+                                  reinterpret_cast<const tvp_bf16*>(buffers.v),
+                                  reinterpret_cast<tvp_bf16*>(buffers.q), kQHeads,
+                                  TVP_APPEND_ROPE_K | TVP_APPEND_ROPE_Q | TVP_APPEND_WRITEBACK_K,
+                                  st.error, stream));
       }
-      check_tvp(tvp_rope_append(reinterpret_cast<tvp_bf16*>(cache.k_blocks),
-                                reinterpret_cast<tvp_bf16*>(cache.v_blocks), cache.num_blocks,
-                                kLayers, layer, kKvHeads, d_tables, kTableStride, batch, nullptr,
-                                d_pos, batch, reinterpret_cast<tvp_bf16*>(buffers.k),
-                                reinterpret_cast<const tvp_bf16*>(buffers.v),
-                                reinterpret_cast<tvp_bf16*>(buffers.q), kQHeads,
-                                TVP_APPEND_ROPE_K | TVP_APPEND_ROPE_Q | TVP_APPEND_WRITEBACK_K,
-                                st.error, stream));
       check_tvp(tvp_paged_decode_attention(
           reinterpret_cast<const tvp_bf16*>(buffers.q),
           reinterpret_cast<const tvp_bf16*>(cache.k_blocks),
@@ -382,15 +396,23 @@ std::vector<int> decodeBatchPaged(cublasHandle_t cublas_handle, __nv_bfloat16* h
           kKvHeads, kQHeads, d_tables, kTableStride, d_len, batch, 0.125f, st.mode, 0,
           st.workspace, st.workspace_bytes, reinterpret_cast<tvp_bf16*>(buffers.attn_output),
           st.error, stream));
-      if (st.native_proj) {  // hidden += O attn, one launch
-        native(buffers.attn_output, kHidden, {lw.w_o}, {kHidden}, {hidden_states},
-               TVP_PROJ_RESIDUAL);
+      // native: hidden += O attn, then its post-attention RMSNorm, one launch
+      auto residual_norm = [&](const __nv_bfloat16* in, int in_dim, const __nv_bfloat16* w,
+                               const __nv_bfloat16* gain) {
+        check_tvp(tvp_decode_projection_residual_rmsnorm(
+            reinterpret_cast<const tvp_bf16*>(in), batch, in_dim,
+            reinterpret_cast<const tvp_bf16*>(w), reinterpret_cast<tvp_bf16*>(hidden_states),
+            reinterpret_cast<const tvp_bf16*>(gain), reinterpret_cast<tvp_bf16*>(buffers.rms_output),
+            st.norm_counter, stream));
+      };
+      if (st.native_proj) {
+        residual_norm(buffers.attn_output, kHidden, lw.w_o, lw.post_attention_norm);
       } else {
         project(outputProjection, buffers.attn_output, kHidden, lw.w_o, buffers.o_output, kHidden);
         residual(buffers.o_output);
+        rmsNormKernel<<<batch, 1024, 0, stream>>>(hidden_states, buffers.rms_output,
+                                                  lw.post_attention_norm);
       }
-      rmsNormKernel<<<batch, 1024, 0, stream>>>(hidden_states, buffers.rms_output,
-                                                lw.post_attention_norm);
       if (st.native_proj) {  // gate = silu(gate x) * (up x), one launch
         native(buffers.rms_output, kHidden, {lw.w_gate, lw.w_up}, {8192, 8192}, {buffers.gate},
                TVP_PROJ_SWIGLU);
@@ -400,14 +422,16 @@ std::vector<int> decodeBatchPaged(cublasHandle_t cublas_handle, __nv_bfloat16* h
         if (stream) siluKernel<<<batch, 1024, 0, stream>>>(buffers.gate, buffers.up);
         else silu(buffers.gate, buffers.up, batch);
       }
-      if (st.native_proj) {  // hidden += down, one launch
-        native(buffers.gate, 8192, {lw.w_down}, {kHidden}, {hidden_states}, TVP_PROJ_RESIDUAL);
+      if (st.native_proj) {  // hidden += down, then the next RMSNorm (the final one last)
+        residual_norm(buffers.gate, 8192, lw.w_down,
+                      layer + 1 < kLayers ? weights.layers[layer + 1].input_norm : weights.final_norm);
       } else {
         project(downProjection, buffers.gate, 8192, lw.w_down, buffers.down, kHidden);
         residual(buffers.down);
       }
     }
-    rmsNormKernel<<<batch, 1024, 0, stream>>>(hidden_states, buffers.rms_output, weights.final_norm);
+    if (!st.native_proj)
+      rmsNormKernel<<<batch, 1024, 0, stream>>>(hidden_states, buffers.rms_output, weights.final_norm);
     if (!st.batched) return;
     // The LM head of lm_head.cu:8-36 over all rows: logits[row] = E h_row.
     const float alpha = 1.0f, beta = 0.0f;

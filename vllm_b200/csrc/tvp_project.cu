@@ -42,6 +42,7 @@
 #include <cuda_bf16.h>
 
 #include "tvp_common.cuh"
+#include "tvp_rope.cuh"
 
 namespace tvp {
 namespace {
@@ -50,6 +51,9 @@ constexpr int kProjRows = 16;      // weight rows per CTA (the MMA's M)
 constexpr int kProjMaxTokens = 8;  // input rows (the MMA's N)
 constexpr int kProjBlock = 32;     // k columns per lane step (two MMAs)
 
+constexpr int kHidden = 2048;       // rows of the RMSNorm fused after a residual epilogue
+constexpr int kEpiRopeAppend = 16;  // internal epilogue: Q/K/V with RoPE and the page append
+
 struct ProjParams {
   const __nv_bfloat16* x;
   const __nv_bfloat16* w[TVP_PROJ_MAX];
@@ -57,7 +61,92 @@ struct ProjParams {
   int n[TVP_PROJ_MAX];
   int cta_end[TVP_PROJ_MAX];  // prefix sums of n / 16 (one matrix per CTA)
   int count, rows, k, epilogue;
+  // Residual epilogue followed by the next RMSNorm (norm_out != nullptr): the
+  // last CTA to finish writes norm_out = rmsnorm(out[0]) x norm_gain.
+  const __nv_bfloat16* norm_gain;
+  __nv_bfloat16* norm_out;
+  int* counter;
+  // kEpiRopeAppend: matrix 0 = q, 1 = k, 2 = v of one token per row; q is
+  // stored rotated into out[0], k rotated and v as is into their page slots.
+  __nv_bfloat16* k_pool;
+  __nv_bfloat16* v_pool;
+  long long layer_row_base;
+  int num_pages, table_stride;
+  const int32_t* tables;
+  const int32_t* pos;
+  int32_t* err;
 };
+
+// Leaf of the reference's sum of squares, (float)a * (float)a +
+// (float)b * (float)b, with the rounding nvcc gives that expression under its
+// default FMA contraction: fma(a, a, b * b) (found by comparing outputs with
+// the reference kernel's over thousands of rows of every magnitude).
+__device__ __forceinline__ float norm_leaf(float a, float b) {
+  return __fmaf_rn(a, a, __fmul_rn(b, b));
+}
+
+// Sum of squares of a 2048-wide row by the reference's tree
+// (rmsNormKernel, src/model/rmsNorm.cu:6-14): leaf t < 1024 is
+// x[t]^2 + x[t + 1024]^2, then for i = 1, 2, ..., 512: leaf[t] += leaf[t + i]
+// where t % 2i == 0.  Lane l forms leaves 32 l .. 32 l + 31 and sums them by
+// the same tree, the lanes' sums meet by the tree's upper levels through
+// shuffles; then the row's output, bf16((x / r) g) with r =
+// sqrt(sum / 2048 + 1e-5) evaluated in double, as the reference writes it.
+// Reads go through L2 (other CTAs of this grid wrote the row).
+__device__ __forceinline__ void rmsnorm_row_warp(const __nv_bfloat16* x, const __nv_bfloat16* gain,
+                                                 __nv_bfloat16* out, int lane) {
+  uint4 a[4], b[4];
+  const uint4* xa = reinterpret_cast<const uint4*>(x + 32 * lane);
+  const uint4* xb = reinterpret_cast<const uint4*>(x + 1024 + 32 * lane);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    a[i] = __ldcg(xa + i);
+    b[i] = __ldcg(xb + i);
+  }
+  float leaf[32];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t wa[4] = {a[i].x, a[i].y, a[i].z, a[i].w};
+    const uint32_t wb[4] = {b[i].x, b[i].y, b[i].z, b[i].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a0 = bf16lo_to_f32(wa[j]), a1 = bf16hi_to_f32(wa[j]);
+      const float b0 = bf16lo_to_f32(wb[j]), b1 = bf16hi_to_f32(wb[j]);
+      leaf[8 * i + 2 * j] = norm_leaf(a0, b0);
+      leaf[8 * i + 2 * j + 1] = norm_leaf(a1, b1);
+    }
+  }
+#pragma unroll
+  for (int st = 1; st < 32; st *= 2)
+#pragma unroll
+    for (int i = 0; i < 32; i += 2 * st) leaf[i] = __fadd_rn(leaf[i], leaf[i + st]);
+  float v = leaf[0];
+#pragma unroll
+  for (int off = 1; off < 32; off *= 2) {
+    const float o = __shfl_down_sync(0xffffffffu, v, off);
+    if ((lane & (2 * off - 1)) == 0) v = __fadd_rn(v, o);
+  }
+  float r = 0.f;
+  if (lane == 0) r = (float)sqrt((double)v / 2048.0 + 1.0e-5);
+  r = __shfl_sync(0xffffffffu, r, 0);
+  const uint4* ga = reinterpret_cast<const uint4*>(gain + 32 * lane);
+  const uint4* gb = reinterpret_cast<const uint4*>(gain + 1024 + 32 * lane);
+  uint4* oa = reinterpret_cast<uint4*>(out + 32 * lane);
+  uint4* ob = reinterpret_cast<uint4*>(out + 1024 + 32 * lane);
+  auto norm2 = [&](uint32_t xw, uint32_t gw) {
+    const float y0 = __fmul_rn(__fdiv_rn(bf16lo_to_f32(xw), r), bf16lo_to_f32(gw));
+    const float y1 = __fmul_rn(__fdiv_rn(bf16hi_to_f32(xw), r), bf16hi_to_f32(gw));
+    return pack_bf16x2(y0, y1);
+  };
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 g0 = __ldg(ga + i), g1 = __ldg(gb + i);
+    oa[i] = make_uint4(norm2(a[i].x, g0.x), norm2(a[i].y, g0.y), norm2(a[i].z, g0.z),
+                       norm2(a[i].w, g0.w));
+    ob[i] = make_uint4(norm2(b[i].x, g1.x), norm2(b[i].y, g1.y), norm2(b[i].z, g1.z),
+                       norm2(b[i].w, g1.w));
+  }
+}
 
 // Weights: read-only for the whole life of every launch, so the
 // non-coherent path is valid for them.
@@ -82,6 +171,59 @@ __device__ __forceinline__ uint4 ld_coherent_v4(const void* p) {
   return r;
 }
 
+// Epilogue of the Q/K/V projection of one decode token per row, fused with
+// RoPE and the page append (K1's work, tvp_append.cu): thread (r, ln) of the
+// first 128 holds the FP32 sum of MMA row (ln / 4) + 8 (r / 2) for token
+// row t.  For q and k the two MMA rows of a thread pair are the two halves
+// (d, d + 32) of a rotate-half pair, exchanged through shared memory; each
+// half is rounded to BF16 (the projection's output) and rotated with K1's
+// arithmetic, bit for bit.  q goes to out[0]; k and v go into slot pos % 16
+// of page tables[t][pos / 16] of the layer's pools.  Threads with
+// (r & 2) == 0 and ln < 4 hold MMA row 0 for each of the 8 token rows: they
+// report a row's bad position or page once.
+__device__ __forceinline__ void rope_append_epilogue(const ProjParams& p, float sum, int mat,
+                                                     int group, int r, int ln, int t) {
+  __shared__ float half[4][32];
+  const float own = __bfloat162float(__float2bfloat16_rn(sum));
+  if (threadIdx.x < 128) half[r][ln] = own;
+  __syncthreads();
+  if (threadIdx.x >= 128 || t >= p.rows) return;
+  const int pos = __ldg(p.pos + t);
+  if (pos < 0 || pos / kPage >= p.table_stride) {
+    if (mat == 0 && (r & 2) == 0 && (ln >> 2) == 0) record_error(p.err, TVP_DEVERR_BAD_TOKEN);
+    return;
+  }
+  const int kv_dim = kMaxKvHeads * kHeadDim;
+  float val = own;
+  int feature;
+  if (mat < 2) {
+    const int pair = (group & 3) * 8 + (ln >> 2), head = group >> 2;
+    const bool upper = (r & 2) != 0;  // the d + 32 half
+    const float other = half[r ^ 2][ln];
+    const float angle = pos * llama3_theta(pair);
+    const float c = cosf(angle), sn = sinf(angle);
+    __nv_bfloat16 xo, yo;
+    rope_rotate(__float2bfloat16_rn(upper ? other : own), __float2bfloat16_rn(upper ? own : other),
+                c, sn, xo, yo);
+    val = __bfloat162float(upper ? yo : xo);
+    feature = head * kHeadDim + pair + (upper ? kHeadDim / 2 : 0);
+    if (mat == 0) {
+      static_cast<__nv_bfloat16*>(p.out[0])[(size_t)t * p.n[0] + feature] = __float2bfloat16_rn(val);
+      return;
+    }
+  } else {
+    feature = group * kProjRows + (ln >> 2) + ((r & 2) ? 8 : 0);
+  }
+  const int phys = __ldg(p.tables + (size_t)t * p.table_stride + pos / kPage);
+  if (phys < 0 || phys >= p.num_pages) {
+    if ((r & 2) == 0 && (ln >> 2) == 0) record_error(p.err, TVP_DEVERR_BAD_PAGE);
+    return;
+  }
+  const size_t dst =
+      (size_t)(p.layer_row_base + (long long)phys * kPage + pos % kPage) * kv_dim + feature;
+  (mat == 1 ? p.k_pool : p.v_pool)[dst] = __float2bfloat16_rn(val);
+}
+
 // kMats = 1: the CTA streams 16 rows of one matrix; kMats = 2 (SwiGLU): the
 // same 16 rows of matrices 0 and 1.  kUnroll blocks of loads are in flight.
 template <int kWarps, int kMats, int kUnroll>
@@ -92,7 +234,7 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
   // the parameter arrays would copy them to local memory).
   const __nv_bfloat16* w0 = p.w[0];
   void* out = p.out[0];
-  int n_out = p.n[0], first = 0;
+  int n_out = p.n[0], first = 0, mat = 0;
   if (kMats == 1) {
 #pragma unroll
     for (int i = 1; i < TVP_PROJ_MAX; ++i)
@@ -101,13 +243,20 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
         out = p.out[i];
         n_out = p.n[i];
         first = p.cta_end[i - 1];
+        mat = i;
       }
   }
   const int group = blockIdx.x - first;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
   const int slice = p.k / kWarps;  // a multiple of kProjBlock
-  const size_t k0 = (size_t)(group * kProjRows + g) * p.k + warp * slice + 8 * q;
+  // Rows of the CTA's 16-row tile: MMA rows g and g + 8 are weight rows
+  // 16 group + g and + 8; for q and k with the RoPE epilogue they are rows
+  // h 64 + 8 u + g and + 32 (group = 4 h + u), the two halves of one
+  // rotate-half pair, so that both halves of every pair meet in this CTA.
+  const bool pair_rows = kMats == 1 && p.epilogue == kEpiRopeAppend && mat < 2;
+  const int row0 = pair_rows ? (group >> 2) * kHeadDim + (group & 3) * 8 : group * kProjRows;
+  const size_t k0 = (size_t)(row0 + g) * p.k + warp * slice + 8 * q;
   const __nv_bfloat16* wa[kMats];
   wa[0] = w0 + k0;
   if (kMats == 2) wa[kMats - 1] = p.w[1] + k0;
@@ -118,7 +267,7 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
 #pragma unroll
   for (int m = 0; m < kMats; ++m) c[m][0] = c[m][1] = c[m][2] = c[m][3] = 0.f;
   const int blocks = slice / kProjBlock;
-  const size_t row8 = (size_t)8 * p.k;
+  const size_t row8 = (size_t)(pair_rows ? kHeadDim / 2 : 8) * p.k;
   // The next launch in the stream may start now; it reads nothing this grid
   // writes before its own wait below.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -161,18 +310,24 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
 #pragma unroll
     for (int r = 0; r < 4; ++r) red[m][warp][r][lane] = c[m][r];
   __syncthreads();
-  if (threadIdx.x < 128) {
-    const int r = threadIdx.x >> 5, ln = threadIdx.x & 31;
-    float s[kMats];
+  // accumulator r of lane ln: MMA row (ln / 4) + 8 (r / 2), input row 2 (ln % 4) + r % 2
+  const int r = (threadIdx.x >> 5) & 3, ln = threadIdx.x & 31;
+  float s[kMats];
 #pragma unroll
-    for (int m = 0; m < kMats; ++m) {
-      s[m] = 0.f;
+  for (int m = 0; m < kMats; ++m) {
+    s[m] = 0.f;
+    if (threadIdx.x < 128) {
 #pragma unroll
       for (int wi = 0; wi < kWarps; ++wi) s[m] += red[m][wi][r][ln];
     }
-    // accumulator r of lane ln: weight row (ln / 4) + 8 (r / 2), input row 2 (ln % 4) + r % 2
+  }
+  const int t = 2 * (ln & 3) + (r & 1);
+  if (kMats == 1 && p.epilogue == kEpiRopeAppend) {
+    rope_append_epilogue(p, s[0], mat, group, r, ln, t);
+    return;
+  }
+  if (threadIdx.x < 128) {
     const int row = group * kProjRows + (ln >> 2) + ((r & 2) ? 8 : 0);
-    const int t = 2 * (ln & 3) + (r & 1);
     if (t < p.rows) {
       const size_t idx = (size_t)t * n_out + row;
       __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(out);
@@ -190,12 +345,59 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
       }
     }
   }
+  if (kMats == 1 && p.norm_out != nullptr) {
+    // The last CTA to finish normalises the rows: every CTA releases its row
+    // stores and counts itself done; the last one acquires them all.
+    __shared__ int is_last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) is_last = atomicAdd(p.counter, 1) == (int)gridDim.x - 1;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    const __nv_bfloat16* hidden = static_cast<const __nv_bfloat16*>(out);
+    for (int row = warp; row < p.rows; row += kWarps)
+      rmsnorm_row_warp(hidden + (size_t)row * kHidden, p.norm_gain, p.norm_out + (size_t)row * kHidden,
+                       lane);
+    if (threadIdx.x == 0) *p.counter = 0;  // ready for the next launch
+  }
 }
 
 }  // namespace
 }  // namespace tvp
 
 using namespace tvp;
+
+namespace {
+
+// Launches K5 over `ctas` CTAs (16 weight rows each): 16 warps (one CTA per
+// SM) when each of 8 warps would stream more than 512 columns, so that long
+// rows keep enough loads in flight per SM; programmatic dependent launch.
+int launch_projection(const ProjParams& p, long long ctas, bool swiglu, cudaStream_t stream) {
+  const bool wide = p.k > 4096 && p.k % 512 == 0;
+  void (*kernel)(const ProjParams) =
+      swiglu ? (wide ? decode_projection_kernel<16, 2, 4> : decode_projection_kernel<8, 2, 4>)
+             : (wide ? decode_projection_kernel<16, 1, 8> : decode_projection_kernel<8, 1, 8>);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ctas);
+  cfg.blockDim = dim3(wide ? 16 * 32 : 8 * 32);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, p) == cudaSuccess ? TVP_OK : TVP_ERR_RUNTIME;
+}
+
+inline bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+inline bool overlaps(const void* a, size_t na, const void* b, size_t nb) {
+  const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+  return x < y + nb && y < x + na;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -222,10 +424,8 @@ int tvp_decode_projections(const tvp_bf16* x, int rows, int k, int count, const 
         (reinterpret_cast<uintptr_t>(w[i]) & 15u) ||
         (stored && (reinterpret_cast<uintptr_t>(out[i]) & (esize - 1))))
       return TVP_ERR_INVALID_ARGUMENT;
-    if (stored) {  // an output must not overlap the input rows
-      const uintptr_t o = reinterpret_cast<uintptr_t>(out[i]), xa = reinterpret_cast<uintptr_t>(x);
-      if (o < xa + xb && xa < o + (size_t)rows * n[i] * esize) return TVP_ERR_INVALID_ARGUMENT;
-    }
+    // an output must not overlap the input rows
+    if (stored && overlaps(out[i], (size_t)rows * n[i] * esize, x, xb)) return TVP_ERR_INVALID_ARGUMENT;
     if (!swiglu || i == 0) ctas += n[i] / kProjRows;
     if (ctas > 0x7fffffffLL) return TVP_ERR_UNSUPPORTED;
     p.w[i] = reinterpret_cast<const __nv_bfloat16*>(w[i]);
@@ -233,22 +433,78 @@ int tvp_decode_projections(const tvp_bf16* x, int rows, int k, int count, const 
     p.n[i] = n[i];
     p.cta_end[i] = (int)ctas;
   }
-  // 16 warps (one CTA per SM) when each of 8 warps would stream more than
-  // 512 columns, so that long rows keep enough loads in flight per SM.
-  const bool wide = k > 4096 && k % 512 == 0;
-  void (*kernel)(const ProjParams) =
-      swiglu ? (wide ? decode_projection_kernel<16, 2, 4> : decode_projection_kernel<8, 2, 4>)
-             : (wide ? decode_projection_kernel<16, 1, 8> : decode_projection_kernel<8, 1, 8>);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)ctas);
-  cfg.blockDim = dim3(wide ? 16 * 32 : 8 * 32);
-  cfg.stream = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, p) == cudaSuccess ? TVP_OK : TVP_ERR_RUNTIME;
+  return launch_projection(p, ctas, swiglu, static_cast<cudaStream_t>(stream));
+}
+
+int tvp_decode_projection_residual_rmsnorm(const tvp_bf16* x, int rows, int k, const tvp_bf16* w,
+                                           tvp_bf16* hidden, const tvp_bf16* norm_gain,
+                                           tvp_bf16* norm_out, int32_t* d_counter,
+                                           tvp_stream_t stream) {
+  if (!x || !w || !hidden || !norm_gain || !norm_out || !d_counter || rows < 1 ||
+      rows > kProjMaxTokens || k < 256 || k % 256 != 0 || !aligned16(x) || !aligned16(w) ||
+      !aligned16(hidden) || !aligned16(norm_gain) || !aligned16(norm_out) ||
+      (reinterpret_cast<uintptr_t>(d_counter) & 3u))
+    return TVP_ERR_INVALID_ARGUMENT;
+  const size_t xb = (size_t)rows * k * 2, hb = (size_t)rows * kHidden * 2;
+  if (overlaps(hidden, hb, x, xb) || overlaps(norm_out, hb, x, xb) ||
+      overlaps(norm_out, hb, hidden, hb) || overlaps(norm_out, hb, norm_gain, kHidden * 2))
+    return TVP_ERR_INVALID_ARGUMENT;
+  ProjParams p{};
+  p.x = reinterpret_cast<const __nv_bfloat16*>(x);
+  p.count = 1;
+  p.rows = rows;
+  p.k = k;
+  p.epilogue = TVP_PROJ_RESIDUAL;
+  p.w[0] = reinterpret_cast<const __nv_bfloat16*>(w);
+  p.out[0] = hidden;
+  p.n[0] = kHidden;
+  p.cta_end[0] = kHidden / kProjRows;
+  p.norm_gain = reinterpret_cast<const __nv_bfloat16*>(norm_gain);
+  p.norm_out = reinterpret_cast<__nv_bfloat16*>(norm_out);
+  p.counter = reinterpret_cast<int*>(d_counter);
+  return launch_projection(p, kHidden / kProjRows, false, static_cast<cudaStream_t>(stream));
+}
+
+int tvp_decode_qkv_rope_append(const tvp_bf16* x, int rows, int k, const tvp_bf16* w_q,
+                               const tvp_bf16* w_k, const tvp_bf16* w_v, tvp_bf16* q_out,
+                               tvp_bf16* k_pool, tvp_bf16* v_pool, int num_pages, int num_layers,
+                               int layer, const int32_t* d_block_tables, int table_stride,
+                               const int32_t* d_positions, int32_t* d_error, tvp_stream_t stream) {
+  constexpr int kQ = TVP_Q_HEADS * kHeadDim, kKv = kMaxKvHeads * kHeadDim;
+  if (!x || !w_q || !w_k || !w_v || !q_out || !k_pool || !v_pool || !d_block_tables ||
+      !d_positions || rows < 1 || rows > kProjMaxTokens || k < 256 || k % 256 != 0 ||
+      num_pages <= 0 || num_layers <= 0 || layer < 0 || layer >= num_layers || table_stride <= 0 ||
+      !aligned16(x) || !aligned16(w_q) || !aligned16(w_k) || !aligned16(w_v) ||
+      (reinterpret_cast<uintptr_t>(q_out) & 1u) || (reinterpret_cast<uintptr_t>(k_pool) & 1u) ||
+      (reinterpret_cast<uintptr_t>(v_pool) & 1u))
+    return TVP_ERR_INVALID_ARGUMENT;
+  if ((long long)num_layers * num_pages * kPage > 0x7fffffffLL) return TVP_ERR_UNSUPPORTED;
+  if (overlaps(q_out, (size_t)rows * kQ * 2, x, (size_t)rows * k * 2)) return TVP_ERR_INVALID_ARGUMENT;
+  ProjParams p{};
+  p.x = reinterpret_cast<const __nv_bfloat16*>(x);
+  p.count = 3;
+  p.rows = rows;
+  p.k = k;
+  p.epilogue = kEpiRopeAppend;
+  p.w[0] = reinterpret_cast<const __nv_bfloat16*>(w_q);
+  p.w[1] = reinterpret_cast<const __nv_bfloat16*>(w_k);
+  p.w[2] = reinterpret_cast<const __nv_bfloat16*>(w_v);
+  p.out[0] = q_out;
+  p.n[0] = kQ;
+  p.n[1] = kKv;
+  p.n[2] = kKv;
+  p.cta_end[0] = kQ / kProjRows;
+  p.cta_end[1] = (kQ + kKv) / kProjRows;
+  p.cta_end[2] = (kQ + 2 * kKv) / kProjRows;
+  p.k_pool = reinterpret_cast<__nv_bfloat16*>(k_pool);
+  p.v_pool = reinterpret_cast<__nv_bfloat16*>(v_pool);
+  p.layer_row_base = (long long)layer * num_pages * kPage;
+  p.num_pages = num_pages;
+  p.table_stride = table_stride;
+  p.tables = d_block_tables;
+  p.pos = d_positions;
+  p.err = d_error;
+  return launch_projection(p, p.cta_end[2], false, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

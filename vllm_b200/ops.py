@@ -289,3 +289,57 @@ def decode_projections(x, weights, outs=None, epilogue="bf16", stream=None):
                                     _stream(stream))
     N.check(rc, "tvp_decode_projections")
     return outs
+
+
+def decode_projection_residual_rmsnorm(x, w, hidden, norm_gain, norm_out, counter, stream=None):
+    """hidden += bf16(w @ x) (the residual epilogue), then in the same launch
+    norm_out = rmsnorm(hidden) * norm_gain with the reference kernel's
+    arithmetic.  x: BF16 [rows, k]; w: BF16 [2048, k]; hidden, norm_out: BF16
+    [rows, 2048]; norm_gain: BF16 [2048]; counter: a zeroed int32 tensor of one
+    element, reused by every call (zeroed again by each launch)."""
+    lib = N.load()
+    dev = x.device
+    _need(x, "x", torch.bfloat16, dev)
+    _need(w, "w", torch.bfloat16, dev)
+    _need(hidden, "hidden", torch.bfloat16, dev)
+    _need(norm_gain, "norm_gain", torch.bfloat16, dev)
+    _need(norm_out, "norm_out", torch.bfloat16, dev)
+    _need(counter, "counter", torch.int32, dev)
+    rows, k = x.shape
+    if w.shape != (2048, k) or hidden.shape != (rows, 2048) or norm_out.shape != (rows, 2048) \
+            or norm_gain.numel() != 2048:
+        raise ValueError("shapes: x [rows, k], w [2048, k], hidden/norm_out [rows, 2048], gain [2048]")
+    rc = lib.tvp_decode_projection_residual_rmsnorm(_ptr(x), rows, k, _ptr(w), _ptr(hidden),
+                                                    _ptr(norm_gain), _ptr(norm_out), _ptr(counter),
+                                                    _stream(stream))
+    N.check(rc, "tvp_decode_projection_residual_rmsnorm")
+    return hidden, norm_out
+
+
+def decode_qkv_rope_append(x, w_q, w_k, w_v, q_out, k_pool, v_pool, layer, block_tables,
+                           positions, error=None, stream=None):
+    """Q/K/V projections of one decode token per row with RoPE and the paged
+    append in the epilogue: q_out = rope(w_q x); rope(w_k x) and w_v x go into
+    each row's page slot at its position (tvp_rope_append's arithmetic).
+    x: BF16 [rows, k]; w_q [2048, k]; w_k, w_v [512, k]; pools [layers, pages,
+    16, 512]; block_tables int32 [rows, stride]; positions int32 [rows]."""
+    lib = N.load()
+    num_layers, num_pages, kv_heads = _pool_geometry(k_pool, v_pool)
+    dev = x.device
+    for t, name in ((x, "x"), (w_q, "w_q"), (w_k, "w_k"), (w_v, "w_v"), (q_out, "q_out")):
+        _need(t, name, torch.bfloat16, dev)
+    _need(block_tables, "block_tables", torch.int32, dev)
+    _need(positions, "positions", torch.int32, dev)
+    rows, k = x.shape
+    if kv_heads != N.KV_HEADS or w_q.shape != (2048, k) or w_k.shape != (512, k) \
+            or w_v.shape != (512, k) or q_out.shape != (rows, 2048) or positions.numel() != rows \
+            or block_tables.dim() != 2 or block_tables.shape[0] < rows:
+        raise ValueError("shapes: x [rows, k], w_q [2048, k], w_k/w_v [512, k], q_out [rows, 2048], "
+                         "8-head pools, block_tables [>=rows, stride], positions [rows]")
+    rc = lib.tvp_decode_qkv_rope_append(_ptr(x), rows, k, _ptr(w_q), _ptr(w_k), _ptr(w_v),
+                                        _ptr(q_out), _ptr(k_pool), _ptr(v_pool), num_pages,
+                                        num_layers, layer, _ptr(block_tables),
+                                        block_tables.shape[1], _ptr(positions), _ptr(error),
+                                        _stream(stream))
+    N.check(rc, "tvp_decode_qkv_rope_append")
+    return q_out
