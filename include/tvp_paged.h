@@ -167,7 +167,9 @@ int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const 
  * d_q_pos0[s] = L0 > 0 a prefill chunk after L0 cached tokens.
  * q, out: [num_tokens][q_heads * 64] BF16, head-major as the reference,
  * 16-byte aligned; max_q_len >= the longest sequence's query count (at most
- * 65535 x 32 tokens: TVP_ERR_UNSUPPORTED beyond).
+ * 65535 x 32 tokens: TVP_ERR_UNSUPPORTED beyond).  Scores are rounded to
+ * BF16 where the reference rounds them, then an online softmax in base 2,
+ * BF16 probabilities into P.V and FP32 accumulation.
  */
 int tvp_paged_prefill_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const tvp_bf16* v_pool,
                                 int num_pages, int num_layers, int layer, int kv_heads, int q_heads,

@@ -85,66 +85,81 @@ __device__ __forceinline__ float norm_leaf(float a, float b) {
   return __fmaf_rn(a, a, __fmul_rn(b, b));
 }
 
-// Sum of squares of a 2048-wide row by the reference's tree
-// (rmsNormKernel, src/model/rmsNorm.cu:6-14): leaf t < 1024 is
-// x[t]^2 + x[t + 1024]^2, then for i = 1, 2, ..., 512: leaf[t] += leaf[t + i]
-// where t % 2i == 0.  Lane l forms leaves 32 l .. 32 l + 31 and sums them by
-// the same tree, the lanes' sums meet by the tree's upper levels through
-// shuffles; then the row's output, bf16((x / r) g) with r =
-// sqrt(sum / 2048 + 1e-5) evaluated in double, as the reference writes it.
-// Reads go through L2 (other CTAs of this grid wrote the row).
-__device__ __forceinline__ void rmsnorm_row_warp(const __nv_bfloat16* x, const __nv_bfloat16* gain,
-                                                 __nv_bfloat16* out, int lane) {
-  uint4 a[4], b[4];
-  const uint4* xa = reinterpret_cast<const uint4*>(x + 32 * lane);
-  const uint4* xb = reinterpret_cast<const uint4*>(x + 1024 + 32 * lane);
+// RMSNorm of `rows` finished rows of 2048 by one CTA of kThreads threads, with
+// the reference's arithmetic (rmsNormKernel, src/model/rmsNorm.cu:3-22): the
+// sum of squares by its tree (leaf t < 1024 is x[t]^2 + x[t + 1024]^2, then
+// for i = 1, 2, ..., 512: leaf[t] += leaf[t + i] where t % 2i == 0), r =
+// sqrt(sum / 2048 + 1e-5) evaluated in double as the reference writes it, and
+// out = bf16((x / r) g) with IEEE division.  Warp w < rows sums row w: lane l
+// forms leaves 32 l .. 32 l + 31 and sums them by the same tree, and the
+// lanes' sums meet by the tree's upper levels through shuffles.  Every thread
+// then writes its share of all rows' outputs; it issues the loads of that
+// share (through L2: other CTAs of the grid wrote the rows) before the sums.
+template <int kThreads>
+__device__ __forceinline__ void rmsnorm_rows_cta(const __nv_bfloat16* x, const __nv_bfloat16* gain,
+                                                 __nv_bfloat16* out, int rows) {
+  constexpr int kVecPerRow = kHidden / 8;                          // 256 uint4 per row
+  constexpr int kMaxVec = kProjMaxTokens * kVecPerRow / kThreads;  // per thread
+  __shared__ float r_row[kProjMaxTokens];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  const uint4* gv = reinterpret_cast<const uint4*>(gain);
+  uint4 mine[kMaxVec], mine_g[kMaxVec];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    a[i] = __ldcg(xa + i);
-    b[i] = __ldcg(xb + i);
-  }
-  float leaf[32];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t wa[4] = {a[i].x, a[i].y, a[i].z, a[i].w};
-    const uint32_t wb[4] = {b[i].x, b[i].y, b[i].z, b[i].w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float a0 = bf16lo_to_f32(wa[j]), a1 = bf16hi_to_f32(wa[j]);
-      const float b0 = bf16lo_to_f32(wb[j]), b1 = bf16hi_to_f32(wb[j]);
-      leaf[8 * i + 2 * j] = norm_leaf(a0, b0);
-      leaf[8 * i + 2 * j + 1] = norm_leaf(a1, b1);
+  for (int j = 0; j < kMaxVec; ++j) {
+    const int i = threadIdx.x + j * kThreads;
+    if (i < rows * kVecPerRow) {
+      mine[j] = __ldcg(xv + i);
+      mine_g[j] = __ldg(gv + i % kVecPerRow);
     }
   }
+  if (warp < rows) {
+    uint4 a[4], b[4];
+    const uint4* xa = xv + warp * kVecPerRow + 4 * lane;
+    const uint4* xb = xa + kVecPerRow / 2;
 #pragma unroll
-  for (int st = 1; st < 32; st *= 2)
+    for (int i = 0; i < 4; ++i) {
+      a[i] = __ldcg(xa + i);
+      b[i] = __ldcg(xb + i);
+    }
+    float leaf[32];
 #pragma unroll
-    for (int i = 0; i < 32; i += 2 * st) leaf[i] = __fadd_rn(leaf[i], leaf[i + st]);
-  float v = leaf[0];
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t wa[4] = {a[i].x, a[i].y, a[i].z, a[i].w};
+      const uint32_t wb[4] = {b[i].x, b[i].y, b[i].z, b[i].w};
 #pragma unroll
-  for (int off = 1; off < 32; off *= 2) {
-    const float o = __shfl_down_sync(0xffffffffu, v, off);
-    if ((lane & (2 * off - 1)) == 0) v = __fadd_rn(v, o);
+      for (int j = 0; j < 4; ++j) {
+        leaf[8 * i + 2 * j] = norm_leaf(bf16lo_to_f32(wa[j]), bf16lo_to_f32(wb[j]));
+        leaf[8 * i + 2 * j + 1] = norm_leaf(bf16hi_to_f32(wa[j]), bf16hi_to_f32(wb[j]));
+      }
+    }
+#pragma unroll
+    for (int st = 1; st < 32; st *= 2)
+#pragma unroll
+      for (int i = 0; i < 32; i += 2 * st) leaf[i] = __fadd_rn(leaf[i], leaf[i + st]);
+    float v = leaf[0];
+#pragma unroll
+    for (int off = 1; off < 32; off *= 2) {
+      const float o = __shfl_down_sync(0xffffffffu, v, off);
+      if ((lane & (2 * off - 1)) == 0) v = __fadd_rn(v, o);
+    }
+    if (lane == 0) r_row[warp] = (float)sqrt((double)v / 2048.0 + 1.0e-5);
   }
-  float r = 0.f;
-  if (lane == 0) r = (float)sqrt((double)v / 2048.0 + 1.0e-5);
-  r = __shfl_sync(0xffffffffu, r, 0);
-  const uint4* ga = reinterpret_cast<const uint4*>(gain + 32 * lane);
-  const uint4* gb = reinterpret_cast<const uint4*>(gain + 1024 + 32 * lane);
-  uint4* oa = reinterpret_cast<uint4*>(out + 32 * lane);
-  uint4* ob = reinterpret_cast<uint4*>(out + 1024 + 32 * lane);
-  auto norm2 = [&](uint32_t xw, uint32_t gw) {
+  __syncthreads();
+  auto norm2 = [](uint32_t xw, uint32_t gw, float r) {
     const float y0 = __fmul_rn(__fdiv_rn(bf16lo_to_f32(xw), r), bf16lo_to_f32(gw));
     const float y1 = __fmul_rn(__fdiv_rn(bf16hi_to_f32(xw), r), bf16hi_to_f32(gw));
     return pack_bf16x2(y0, y1);
   };
+  uint4* ov = reinterpret_cast<uint4*>(out);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint4 g0 = __ldg(ga + i), g1 = __ldg(gb + i);
-    oa[i] = make_uint4(norm2(a[i].x, g0.x), norm2(a[i].y, g0.y), norm2(a[i].z, g0.z),
-                       norm2(a[i].w, g0.w));
-    ob[i] = make_uint4(norm2(b[i].x, g1.x), norm2(b[i].y, g1.y), norm2(b[i].z, g1.z),
-                       norm2(b[i].w, g1.w));
+  for (int j = 0; j < kMaxVec; ++j) {
+    const int i = threadIdx.x + j * kThreads;
+    if (i < rows * kVecPerRow) {
+      const float r = r_row[i / kVecPerRow];
+      ov[i] = make_uint4(norm2(mine[j].x, mine_g[j].x, r), norm2(mine[j].y, mine_g[j].y, r),
+                         norm2(mine[j].z, mine_g[j].z, r), norm2(mine[j].w, mine_g[j].w, r));
+    }
   }
 }
 
@@ -355,10 +370,8 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    const __nv_bfloat16* hidden = static_cast<const __nv_bfloat16*>(out);
-    for (int row = warp; row < p.rows; row += kWarps)
-      rmsnorm_row_warp(hidden + (size_t)row * kHidden, p.norm_gain, p.norm_out + (size_t)row * kHidden,
-                       lane);
+    rmsnorm_rows_cta<kWarps * 32>(static_cast<const __nv_bfloat16*>(out), p.norm_gain, p.norm_out,
+                                  p.rows);
     if (threadIdx.x == 0) *p.counter = 0;  // ready for the next launch
   }
 }
