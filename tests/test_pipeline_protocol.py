@@ -170,3 +170,191 @@ def test_prefill_kernel_plain_waits_are_exact():
         early, over, done = run(units, consumers, 4, gated=False,
                                 rng=random.Random(rng.randrange(1 << 30)), stages=6)
         assert not early and not over and done, units
+
+
+# ---------------------------------------------------------------------------
+# paged_prefill_kernel: the whole protocol of one CTA, with two softmax sides
+# (side s takes the chunks c with c % 2 == s) and the tensor-core operations
+# as asynchronous work that completes in issue order.
+#   producer : chunk c's K/V into stage c % KV_STAGES after kv_empty of c - KV_STAGES
+#   MMA      : S(0), S(1); then per c: wait P(c), PV(c) into O[c % 2], commit
+#              kv_empty(c), S(c + 2) (waits for its K/V); finally commit o_full
+#   side s   : per own chunk c: wait s_full[s]; read S buffer s; maybe rescale
+#              O[s]; write P buffer s; arrive p_full[s] (SIDE_WARPS arrivals);
+#              at the end wait o_full and read O[0], O[1]
+# Hazards checked: reading S(c) before it is computed or after S(c + 2)
+# overwrote it; a PV reading a P buffer not yet (or no longer) holding its
+# chunk; an O rescale while a PV into that O is outstanding; a K/V stage
+# refilled before the MMAs that read it completed; the final read before
+# every PV completed; and deadlock.
+KV_STAGES = 4
+SIDE_WARPS = 2  # 4 in the kernel; 2 show the same interleavings
+
+
+def run_prefill(n_chunks, rng, sides=2, early_s=False):
+    full = [MBarrier(1) for _ in range(KV_STAGES)]
+    empty = [MBarrier(1) for _ in range(KV_STAGES)]
+    s_full = [MBarrier(1) for _ in range(2)]
+    p_full = [MBarrier(SIDE_WARPS) for _ in range(2)]
+    o_full = MBarrier(1)
+    kv_landed = {}          # chunk -> landed
+    kv_slot = [None] * KV_STAGES   # chunk whose K/V a stage holds (issued)
+    s_buf = [None, None]    # chunk whose S the buffer holds (completed MMA)
+    p_buf = [None, None]    # chunk whose P the buffer holds (all warps wrote)
+    p_writes = [0, 0]
+    o_pending = [0, 0]      # PVs issued into O[s] and not completed
+    queue = []              # tensor-core ops in issue order: (kind, chunk) or ("commit", bar)
+    errors = []
+    prod_next = 0
+    in_flight = []
+    # MMA thread program as a list of steps, advanced one at a time
+    mma = {"pc": 0, "c": 0}
+    steps = []
+    steps.append(("S", 0))
+    if n_chunks > 1:
+        steps.append(("S", 1))
+    for c in range(n_chunks):
+        if early_s and c + 2 < n_chunks:  # the broken order: S(c + 2) before P(c) is ready
+            steps += [("S", c + 2), ("waitP", c), ("PV", c), ("commit_empty", c)]
+            continue
+        steps += [("waitP", c), ("PV", c), ("commit_empty", c)]
+        if c + 2 < n_chunks:
+            steps.append(("S", c + 2))
+    steps.append(("commit_o", None))
+    # softmax warps: (side, warp) -> list of own chunks, position, phase within chunk
+    warps = []
+    for s in range(sides):
+        own = list(range(s, n_chunks, 2))
+        for w in range(SIDE_WARPS):
+            warps.append({"side": s, "own": own, "i": 0, "stage": "wait", "final": False})
+
+    def exec_op():
+        kind, c = queue.pop(0)
+        if kind == "S":
+            if kv_slot[c % KV_STAGES] != c or not kv_landed.get(c):
+                errors.append(f"S({c}) read K/V not landed")
+            b = c % 2
+            if s_buf[b] is not None and s_buf[b] != c - 2:
+                errors.append(f"S({c}) overwrote buffer holding S({s_buf[b]})")
+            s_buf[b] = c
+            s_read[b] = 0
+        elif kind == "PV":
+            b = c % 2
+            if p_buf[b] != c:
+                errors.append(f"PV({c}) read P buffer holding {p_buf[b]}")
+            if kv_slot[c % KV_STAGES] != c:
+                errors.append(f"PV({c}) read a refilled V stage")
+            o_pending[b] -= 1
+        elif kind == "commit":
+            c[0].arrive() if isinstance(c, tuple) else c.arrive()
+
+    s_read = [0, 0]
+    for _ in range(400 * (n_chunks + 4)):
+        acts = []
+        if prod_next < n_chunks:
+            st = prod_next % KV_STAGES
+            if prod_next < KV_STAGES or empty[st].try_wait(((prod_next // KV_STAGES) - 1) & 1):
+                acts.append(("issue",))
+        acts += [("land", k) for k in range(len(in_flight))]
+        if queue:
+            acts.append(("exec",))
+        if mma["pc"] < len(steps):
+            kind, c = steps[mma["pc"]]
+            if kind == "S":
+                if full[c % KV_STAGES].try_wait((c // KV_STAGES) & 1):
+                    acts.append(("mma",))
+            elif kind == "waitP":
+                if p_full[c % 2].try_wait((c // 2) & 1):
+                    acts.append(("mma",))
+            else:
+                acts.append(("mma",))
+        for wi, w in enumerate(warps):
+            if w["i"] < len(w["own"]):
+                c = w["own"][w["i"]]
+                if w["stage"] == "wait" and s_full[w["side"]].try_wait((c // 2) & 1):
+                    acts.append(("warp", wi))
+                elif w["stage"] != "wait":
+                    acts.append(("warp", wi))
+            elif not w["final"] and o_full.try_wait(0):
+                acts.append(("final", wi))
+        if not acts:
+            break
+        act = rng.choice(acts)
+        if act[0] == "issue":
+            c = prod_next
+            kv_slot[c % KV_STAGES] = c
+            kv_landed[c] = False
+            full[c % KV_STAGES].arrive(tx=1)
+            in_flight.append(c)
+            prod_next += 1
+        elif act[0] == "land":
+            c = in_flight.pop(act[1])
+            kv_landed[c] = True
+            full[c % KV_STAGES].complete_tx(1)
+        elif act[0] == "exec":
+            exec_op()
+        elif act[0] == "mma":
+            kind, c = steps[mma["pc"]]
+            mma["pc"] += 1
+            if kind == "S":
+                queue.append(("S", c))
+                queue.append(("commit", s_full[c % 2]))
+            elif kind == "PV":
+                o_pending[c % 2] += 1
+                queue.append(("PV", c))
+            elif kind == "commit_empty":
+                queue.append(("commit", empty[c % KV_STAGES]))
+            elif kind == "commit_o":
+                queue.append(("commit", o_full))
+        elif act[0] == "warp":
+            w = warps[act[1]]
+            c = w["own"][w["i"]]
+            b = w["side"]
+            if w["stage"] == "wait":
+                w["stage"] = "read"
+            elif w["stage"] == "read":
+                if s_buf[b] != c:
+                    errors.append(f"side {b} read S buffer holding {s_buf[b]} for chunk {c}")
+                w["stage"] = "rescale" if rng.random() < 0.3 and c >= 2 else "write"
+            elif w["stage"] == "rescale":
+                if o_pending[b]:
+                    errors.append(f"rescale of O[{b}] at chunk {c} with a PV outstanding")
+                w["stage"] = "write"
+            elif w["stage"] == "write":
+                if p_buf[b] is not None and p_buf[b] != c and o_pending[b]:
+                    errors.append(f"P buffer {b} rewritten for chunk {c} before PV({p_buf[b]}) read it")
+                p_writes[b] += 1
+                if p_writes[b] == SIDE_WARPS:
+                    p_buf[b] = c
+                    p_writes[b] = 0
+                p_full[b].arrive()
+                w["stage"] = "wait"
+                w["i"] += 1
+        elif act[0] == "final":
+            w = warps[act[1]]
+            if any(o_pending) or queue and any(k == "PV" for k, _ in queue):
+                errors.append("final read before every PV completed")
+            w["final"] = True
+    done = mma["pc"] == len(steps) and not queue and all(w["final"] for w in warps)
+    bad = any(b.bad for b in full + empty + s_full + p_full + [o_full])
+    return errors, bad, done
+
+
+@pytest.mark.parametrize("n_chunks", [1, 2, 3, 4, 5, 8, 13, 30])
+def test_prefill_two_sided_protocol(n_chunks):
+    rng = random.Random(100 + n_chunks)
+    for _ in range(200):
+        errors, bad, done = run_prefill(n_chunks, random.Random(rng.randrange(1 << 30)))
+        assert not errors, errors[:3]
+        assert not bad and done
+
+
+def test_prefill_model_catches_an_early_score_mma():
+    """The model is not vacuous: issuing S(c + 2) before P(c) is ready lets it
+    overwrite the S buffer that side c % 2 may still be reading."""
+    rng = random.Random(7)
+    found = 0
+    for _ in range(300):
+        errors, _, _ = run_prefill(8, random.Random(rng.randrange(1 << 30)), early_s=True)
+        found += bool(errors)
+    assert found > 0

@@ -14,7 +14,7 @@
 // positions q_pos0[s], q_pos0[s] + 1, ...  A CTA takes one (32-token tile,
 // sequence, KV head); its 128 MMA rows are the tile's (token, query head)
 // pairs of the GQA group, row 4 t + h, so every K/V byte serves 4 heads.
-// Keys go in chunks of 4 pages (64 keys):
+// Keys go in chunks of 4 pages (64 keys).  A CTA has 12 warps:
 //   * warp 0 streams each chunk's K and V boxes (the decode kernels' tensor
 //     maps, 128-byte swizzle) into a 4-stage ring with TMA; page slots past
 //     the tile's last position are filled with zeros by an out-of-range box;
@@ -23,21 +23,24 @@
 //     S in TMEM) and O += P V (M 128, N 64, K 64: P K-major, V MN-major as it
 //     lands from TMA, O in TMEM), each followed by tcgen05.commit to an
 //     mbarrier;
-//   * warps 2-5 (one thread per row, TMEM lane quarter = warp % 4) load Q into
-//     shared memory, then per chunk read their S row from TMEM, mask it
-//     causally, round scores to BF16 where the reference rounds them, keep an
-//     online base-2 softmax with a lazy running max (O in TMEM rescaled only
-//     when the max grows by more than kLazyMargin), and write P as BF16 into
-//     a 128-byte-swizzled A tile of the P V MMA.
-// S (two TMEM buffers) and P (two shared tiles) are double-buffered, so the
-// tensor core computes S(c + 1) while the softmax works on chunk c, and
-// P V(c) while it works on chunk c + 1: the MMA thread issues S(0), S(1),
-// then per chunk c: [wait P(c)] P V(c), S(c + 2).  Each buffer has its own
-// full barrier, so no waiter is ever two phases behind (a parity wait tells
-// only the current phase from the one before it).  An O rescale waits for
-// P V(c - 1) on pv_done; S(c)'s commit already covers P V(c - 2), so that
-// wait, too, is at most one phase behind.  96 KiB of pipeline state and 256
-// TMEM columns per CTA let two CTAs share an SM.
+//   * two softmax sides of four warps, warps 4-7 and 8-11, one thread per row
+//     (TMEM lane quarter = warp % 4).  Side s takes the chunks c with
+//     c % 2 == s: it reads S buffer s from TMEM, rounds the scores to BF16
+//     where the reference rounds them, masks causally, keeps its own online
+//     base-2 softmax (running max, normaliser, lazy rescale of its own
+//     accumulator O_s when the max grows by more than kLazyMargin) and writes
+//     P as BF16 into P buffer s, a 128-byte-swizzled A tile of the P V MMA.
+//     At the end the two sides merge their (max, sum, O) per row.
+// One thread per row and chunk was a chain of 64 exponentials with only two
+// softmax warps per SM sub-partition; two sides double the rows in flight
+// per sub-partition without exchanging anything per chunk.  The producer and
+// MMA warpgroup hands registers to the two softmax warpgroups (setmaxnreg).
+// The MMA thread issues S(0), S(1), then per chunk c: [wait P(c)] P V(c) into
+// O_{c % 2}, S(c + 2).  S(c)'s commit covers every earlier MMA, P V(c - 2)
+// included, so when side c % 2 sees S(c) it may overwrite P buffer c % 2 and
+// rescale O_{c % 2}.  The order is checked by a host model
+// (tests/test_pipeline_protocol.py).  ~112 KiB of pipeline state and 256 TMEM
+// columns per CTA let two CTAs share an SM.
 #include "tvp_tile.cuh"
 #include "tvp_umma.cuh"
 
@@ -54,13 +57,20 @@ constexpr int kTcKvBytes = kTcChunkPages * kTileBytes;  // 8 KiB of K (or of V) 
 constexpr int kTcStageBytes = 2 * kTcKvBytes;           // K, then V
 constexpr int kTcQBytes = kTcRows * 128;                // 64 BF16 per row
 constexpr int kTcPBytes = kTcRows * 128;                // 64 keys per row
-constexpr int kTcThreads = 6 * 32;
-constexpr uint32_t kTcTmemCols = 256;  // S(even chunks) 0-63, S(odd) 64-127, O 128-191
+constexpr int kTcThreads = 12 * 32;
+// S(even chunks) 0-63, S(odd) 64-127, O of side 0 128-191, O of side 1 192-255
+constexpr uint32_t kTcTmemCols = 256;
+// Register split: the warpgroup of warps 0-3 (producer, MMA issuer, two idle
+// warps) drops to kTcLowRegs, the two softmax warpgroups rise to kTcHighRegs.
+// The launch must provide kTcThreads x registers >= the split (checked on the
+// host before the first launch: an unsatisfiable increase would never return).
+constexpr int kTcLowRegs = 32;
+constexpr int kTcHighRegs = 104;
 constexpr int kOffQ = 0;
 constexpr int kOffP = kOffQ + kTcQBytes;                // P(even), then P(odd)
 constexpr int kOffStages = kOffP + 2 * kTcPBytes;
 constexpr int kOffBars = kOffStages + kTcStages * kTcStageBytes;
-// q_full, o_full, drain, pv_done, s_full[2], p_full[2], kv_full[stages], kv_empty[stages]
+// q_full, o_full, drain, (unused), s_full[2], p_full[2], kv_full[stages], kv_empty[stages]
 constexpr int kBarSFull = 4;
 constexpr int kBarPFull = 6;
 constexpr int kBarKvFull = 8;
@@ -83,7 +93,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
   auto bar = [&](int i) { return smem_addr(&bars[i]); };
-  const uint32_t q_full = bar(0), o_full = bar(1), drain = bar(2), pv_done = bar(3);
+  const uint32_t q_full = bar(0), o_full = bar(1), drain = bar(2);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -110,7 +120,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     mbar_init(q_full, 4);
     mbar_init(o_full, 1);
     mbar_init(drain, 1);
-    mbar_init(pv_done, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar(kBarSFull + b), 1);
       mbar_init(bar(kBarPFull + b), 4);
@@ -129,7 +138,14 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
-  const uint32_t tmem = *tmem_slot, tmem_o = tmem + 128;
+  const uint32_t tmem = *tmem_slot;
+  // Threads that meet before Tensor Memory is released: warp 1 and both sides.
+  constexpr int kEndThreads = 32 + 8 * 32;
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kTcLowRegs));
+    if (warp >= 2) return;  // the rest of this warpgroup only hands its registers over
+  }
 
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
@@ -170,7 +186,10 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       issued = c + 1;
     }
     drain_issued_stages<kTcStages>(bars + kBarKvFull, issued, lane, p.err);
-  } else if (warp == 1) {
+    return;
+  }
+
+  if (warp == 1) {
     // ------------------------------ MMA issuer ----------------------------
     if (lane == 0) {
       constexpr uint32_t kIdS = umma_idesc_bf16_f32(kTcRows, kTcChunk, false, false);
@@ -200,16 +219,17 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       issue_s(0);
       if (n_chunks > 1) issue_s(1);
       for (int c = 0; ok && c < n_chunks; ++c) {
-        // O += P(c) V(c): K = the chunk's 64 keys, 16 (one page of V) per MMA.
+        // O_{c % 2} += P(c) V(c): K = the chunk's 64 keys, 16 (one page of V)
+        // per MMA; the first chunk of each side overwrites its accumulator.
         if (!wait(bar(kBarPFull + (c & 1)), (c >> 1) & 1)) break;
         tc_fence_after_sync();
         const uint32_t p_tile = sbase + kOffP + (c & 1) * kTcPBytes;
         const uint32_t v_tile = stage_k(c) + kTcKvBytes;
+        const uint32_t tmem_o = tmem + 128 + 64 * (c & 1);
 #pragma unroll
         for (int kk = 0; kk < kTcChunkPages; ++kk)
           umma_bf16(tmem_o, umma_desc_sw128(p_tile + 32 * kk, 16, 1024),
-                    umma_desc_sw128(v_tile + kk * kTileBytes, 0, 1024), kIdO, (c > 0 || kk > 0));
-        umma_commit(pv_done);
+                    umma_desc_sw128(v_tile + kk * kTileBytes, 0, 1024), kIdO, (c >= 2 || kk > 0));
         umma_commit(bar(kBarKvEmpty + c % kTcStages));
         if (c + 2 < n_chunks) issue_s(c + 2);
       }
@@ -221,165 +241,187 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_DRAIN);
     }
     __syncwarp();
-  } else {
-    // ------------------------------ softmax -------------------------------
-    const int quarter = warp & 3;  // TMEM lanes 32 quarter .. + 31
-    const int row = quarter * 32 + lane;
-    const int t = row >> 2, h = row & 3;
-    const bool valid = t < count;
-    const int qpos = pos0 + t;
-    const int qdim = p.kv_heads * kGroup * kHeadDim;
-    const int hq = g * kGroup + h;
-    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    {
-      // Q row (token t, head hq) into the swizzled A tile of S = Q K^T.
-      const uint4* src =
-          reinterpret_cast<const uint4*>(p.q + (size_t)(tok0 + t) * qdim + hq * kHeadDim);
+    tc_fence_before_sync();
+    named_barrier_sync(1, kEndThreads);
+    tc_fence_after_sync();
+    tmem_dealloc(tmem, kTcTmemCols);
+    return;
+  }
+
+  // ------------------------------ softmax sides ----------------------------
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kTcHighRegs));
+  const int side = (warp - 4) >> 2;  // 0: warps 4-7 (even chunks), 1: warps 8-11 (odd)
+  const int quarter = warp & 3;      // TMEM lanes 32 quarter .. + 31
+  const int row = quarter * 32 + lane;
+  const int t = row >> 2, h = row & 3;
+  const bool valid = t < count;
+  const int qpos = pos0 + t;
+  const int qdim = p.kv_heads * kGroup * kHeadDim;
+  const int hq = g * kGroup + h;
+  const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+  if (side == 0) {
+    // Q row (token t, head hq) into the swizzled A tile of S = Q K^T.
+    const uint4* src =
+        reinterpret_cast<const uint4*>(p.q + (size_t)(tok0 + t) * qdim + hq * kHeadDim);
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc)
-        *reinterpret_cast<uint4*>(smem + kOffQ + sw128_offset(row, cc)) =
-            valid ? __ldg(src + cc) : make_uint4(0, 0, 0, 0);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(q_full);
-    }
-    float m = -INFINITY, l = 0.f;  // running max of the base-2 scores, normaliser
-    bool ok = true;
-    constexpr float kLog2e = 1.4426950408889634f;
-    for (int c = 0; c < n_chunks; ++c) {
-      bool ready = !*abort_flag && mbar_wait_bounded(bar(kBarSFull + (c & 1)), (c >> 1) & 1);
-      ready = __all_sync(0xffffffffu, ready);
-      if (!ready) {
-        if (lane == 0 && !*abort_flag) {
-          *abort_flag = 1;
-          record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
-        }
-        ok = false;
-        break;
+    for (int cc = 0; cc < 8; ++cc)
+      *reinterpret_cast<uint4*>(smem + kOffQ + sw128_offset(row, cc)) =
+          valid ? __ldg(src + cc) : make_uint4(0, 0, 0, 0);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(q_full);
+  }
+  float m = -INFINITY, l = 0.f;  // this side's running max (base-2 units) and normaliser
+  bool ok = true;
+  constexpr float kLog2e = 1.4426950408889634f;
+  const uint64_t scale2 = f2_pack(p.scale, p.scale);
+  for (int c = side; c < n_chunks; c += 2) {
+    bool ready = !*abort_flag && mbar_wait_bounded(bar(kBarSFull + side), (c >> 1) & 1);
+    ready = __all_sync(0xffffffffu, ready);
+    if (!ready) {
+      if (lane == 0 && !*abort_flag) {
+        *abort_flag = 1;
+        record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
       }
-      tc_fence_after_sync();
-      uint32_t sr[2][32];
-      tmem_ld32(tmem + 64 * (c & 1) + lane_base, sr[0]);
-      tmem_ld32(tmem + 64 * (c & 1) + lane_base + 32, sr[1]);
+      ok = false;
+      break;
+    }
+    tc_fence_after_sync();
+    // Scores rounded to BF16 where the reference rounds them (its score GEMM
+    // writes BF16, src/model/attention.cu:10-51), two per conversion, kept as
+    // packed BF16 pairs; keys past the row's position masked (only chunks
+    // that reach the tile's first position need the test).
+    const int key0 = c * kTcChunk;
+    const bool diagonal = key0 + kTcChunk - 1 > pos0;
+    uint32_t pk[kTcChunk / 2];
+    float mxs[8];  // eight independent max chains, merged by a tree
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mxs[i] = -INFINITY;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t sr[32];
+      tmem_ld32(tmem + 64 * side + 32 * half + lane_base, sr);
       tmem_wait_ld();
-      // Scores rounded to BF16 where the reference rounds them (its score GEMM
-      // writes BF16, src/model/attention.cu:10-51), two per conversion; keys
-      // past the row's position masked (only chunks that reach the tile's
-      // first position need the test).
-      const int key0 = c * kTcChunk;
-      const bool diagonal = key0 + kTcChunk - 1 > pos0;
-      float r[kTcChunk];
-      float mxs[8];  // eight independent max chains, merged by a tree
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mxs[i] = -INFINITY;
-      const uint64_t scale2 = f2_pack(p.scale, p.scale);
-#pragma unroll
-      for (int j = 0; j < kTcChunk; j += 2) {
+      for (int j = 0; j < 32; j += 2) {
         float a, b;
-        f2_unpack(f2_mul(f2_pack(__uint_as_float(sr[j >> 5][j & 31]),
-                                 __uint_as_float(sr[j >> 5][(j & 31) + 1])), scale2), a, b);
-        const uint32_t pr = pack_bf16x2(a, b);
-        r[j] = bf16lo_to_f32(pr);
-        r[j + 1] = bf16hi_to_f32(pr);
+        f2_unpack(f2_mul(f2_pack(__uint_as_float(sr[j]), __uint_as_float(sr[j + 1])), scale2), a, b);
         if (diagonal) {
-          if (key0 + j > qpos) r[j] = -INFINITY;
-          if (key0 + j + 1 > qpos) r[j + 1] = -INFINITY;
+          const int key = key0 + 32 * half + j;
+          if (key > qpos) a = -INFINITY;
+          if (key + 1 > qpos) b = -INFINITY;
         }
-        mxs[(j >> 1) & 7] = max3(mxs[(j >> 1) & 7], r[j], r[j + 1]);
+        const uint32_t pr = pack_bf16x2(a, b);
+        pk[16 * half + (j >> 1)] = pr;
+        mxs[(j >> 1) & 7] = max3(mxs[(j >> 1) & 7], bf16lo_to_f32(pr), bf16hi_to_f32(pr));
       }
-      float mx = fmaxf(max3(mxs[0], mxs[1], mxs[2]), max3(mxs[3], mxs[4], max3(mxs[5], mxs[6], mxs[7])));
-      mx *= kLog2e;
-      // Lazy running max: rescale only when a score beats the row's max by
-      // more than kLazyMargin (probabilities stay below 2^kLazyMargin).
-      float alpha = 1.f;
-      if (mx > m + kLazyMargin) {
-        const float mn = fmaxf(m, mx);
-        alpha = m == -INFINITY ? 0.f : fast_exp2(m - mn);
-        m = mn;
-      }
-      if (c > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-        // O holds chunks 0 .. c - 1 once P V(c - 1) completes.
-        bool done = !*abort_flag && mbar_wait_bounded(pv_done, (c - 1) & 1);
-        done = __all_sync(0xffffffffu, done);
-        if (!done) {
-          if (lane == 0 && !*abort_flag) {
-            *abort_flag = 1;
-            record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
-          }
-          ok = false;
-          break;
-        }
-        tc_fence_after_sync();
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t o[32];
-          tmem_ld32(tmem_o + lane_base + 32 * half, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
-          tmem_st32(tmem_o + lane_base + 32 * half, o);
-        }
-        tmem_wait_st();
-      }
-      const float nbase = m == -INFINITY ? 0.f : -m;
-      // P row into this chunk's swizzled A tile of O += P V.
-      unsigned char* p_tile = smem + kOffP + (c & 1) * kTcPBytes;
-      const uint64_t l2e2 = f2_pack(kLog2e, kLog2e), nb2 = f2_pack(nbase, nbase);
-      uint64_t ls2[4];  // four independent paired sums
-#pragma unroll
-      for (int i = 0; i < 4; ++i) ls2[i] = f2_pack(0.f, 0.f);
-#pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int j0 = 8 * cc + 2 * e;
-          float a0, a1;
-          f2_unpack(f2_fma(f2_pack(r[j0], r[j0 + 1]), l2e2, nb2), a0, a1);
-          const float p0 = fast_exp2(a0), p1 = fast_exp2(a1);
-          ls2[e] = f2_add(ls2[e], f2_pack(p0, p1));
-          w[e] = pack_bf16x2(p0, p1);
-        }
-        *reinterpret_cast<uint4*>(p_tile + sw128_offset(row, cc)) = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-      float la, lb;
-      f2_unpack(f2_add(f2_add(ls2[0], ls2[1]), f2_add(ls2[2], ls2[3])), la, lb);
-      const float lsum = la + lb;
-      l = l * alpha + lsum;
-      // The last page's rows past pos_last hold stale data (possibly NaN): zero
-      // them in the V tile before P V reads it (P is 0 there, but 0 x NaN is not).
-      if (c == n_chunks - 1 && warp == 2)
-        zero_stale_v_rows(smem + kOffStages + (c % kTcStages) * kTcStageBytes + kTcKvBytes +
-                              (last_page - c * kTcChunkPages) * kTileBytes,
-                          pos_last % kPage + 1, lane);
-      fence_proxy_async_smem();
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kBarPFull + (c & 1)));
     }
-    bool fin = ok && !*abort_flag && mbar_wait_bounded(o_full, 0);
-    fin = __all_sync(0xffffffffu, fin);
-    if (!fin && ok && lane == 0 && !*abort_flag) {
-      *abort_flag = 1;
-      record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
+    float mx = fmaxf(max3(mxs[0], mxs[1], mxs[2]), max3(mxs[3], mxs[4], max3(mxs[5], mxs[6], mxs[7])));
+    mx *= kLog2e;
+    // Lazy running max: rescale only when a score beats the side's max by
+    // more than kLazyMargin (probabilities stay below 2^kLazyMargin).
+    float alpha = 1.f;
+    if (mx > m + kLazyMargin) {
+      const float mn = fmaxf(m, mx);
+      alpha = m == -INFINITY ? 0.f : fast_exp2(m - mn);
+      m = mn;
     }
-    if (fin) {
-      tc_fence_after_sync();
-      uint32_t o[2][32];
-      tmem_ld32(tmem_o + lane_base, o[0]);
-      tmem_ld32(tmem_o + lane_base + 32, o[1]);
+    if (c >= 2 && __any_sync(0xffffffffu, alpha != 1.f)) {
+      // O_side holds this side's earlier chunks: S(c)'s commit, just waited
+      // for, covered P V(c - 2), the last MMA into it.
+      // 16 columns at a time: the packed scores stay live meanwhile.
+#pragma unroll 1
+      for (int part = 0; part < 4; ++part) {
+        const uint32_t taddr = tmem + 128 + 64 * side + 16 * part + lane_base;
+        uint32_t o[16];
+        tmem_ld16(taddr, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+        tmem_st16(taddr, o);
+      }
+      tmem_wait_st();
+    }
+    const float nbase = m == -INFINITY ? 0.f : -m;
+    // P row into this side's swizzled A tile of O += P V.  S(c)'s commit also
+    // covered P V(c - 2), the last reader of this tile.
+    unsigned char* p_tile = smem + kOffP + side * kTcPBytes;
+    const uint64_t l2e2 = f2_pack(kLog2e, kLog2e), nb2 = f2_pack(nbase, nbase);
+    uint64_t ls2[4];  // four independent paired sums
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ls2[i] = f2_pack(0.f, 0.f);
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t pr = pk[4 * cc + e];
+        float a0, a1;
+        f2_unpack(f2_fma(f2_pack(bf16lo_to_f32(pr), bf16hi_to_f32(pr)), l2e2, nb2), a0, a1);
+        const float p0 = fast_exp2(a0), p1 = fast_exp2(a1);
+        ls2[e] = f2_add(ls2[e], f2_pack(p0, p1));
+        w[e] = pack_bf16x2(p0, p1);
+      }
+      *reinterpret_cast<uint4*>(p_tile + sw128_offset(row, cc)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    float la, lb;
+    f2_unpack(f2_add(f2_add(ls2[0], ls2[1]), f2_add(ls2[2], ls2[3])), la, lb);
+    l = l * alpha + (la + lb);
+    // The last page's rows past pos_last hold stale data (possibly NaN): zero
+    // them in the V tile before P V reads it (P is 0 there, but 0 x NaN is not).
+    if (c == n_chunks - 1 && quarter == 0)
+      zero_stale_v_rows(smem + kOffStages + (c % kTcStages) * kTcStageBytes + kTcKvBytes +
+                            (last_page - c * kTcChunkPages) * kTileBytes,
+                        pos_last % kPage + 1, lane);
+    fence_proxy_async_smem();
+    tc_fence_before_sync();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar(kBarPFull + side));
+  }
+  bool fin = ok && !*abort_flag && mbar_wait_bounded(o_full, 0);
+  fin = __all_sync(0xffffffffu, fin);
+  if (!fin && ok && lane == 0 && !*abort_flag) {
+    *abort_flag = 1;
+    record_error(p.err, TVP_DEVERR_TIMEOUT | TVP_DEVERR_WAIT_FULL);
+  }
+  // Merge the two sides per row: side 1 hands its (max, normaliser) to side 0
+  // through the Q tile, whose last reader (an S MMA) completed before o_full.
+  float* xchg = reinterpret_cast<float*>(smem + kOffQ);
+  if (side == 1) {
+    xchg[2 * row] = m;
+    xchg[2 * row + 1] = l;
+  }
+  named_barrier_sync(2, 8 * 32);
+  if (side == 0 && fin) {
+    const float mb = xchg[2 * row], lb = xchg[2 * row + 1];
+    const float mt = fmaxf(m, mb);
+    const float wa = m == -INFINITY ? 0.f : fast_exp2(m - mt);
+    const float wb = mb == -INFINITY ? 0.f : fast_exp2(mb - mt);
+    const float lt = l * wa + lb * wb;
+    const float inv = lt > 0.f ? 1.f / lt : 0.f;
+    const bool two = n_chunks > 1;  // side 1 wrote its accumulator
+    tc_fence_after_sync();
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t oa[32], ob[32];
+      tmem_ld32(tmem + 128 + 32 * half + lane_base, oa);
+      if (two) tmem_ld32(tmem + 192 + 32 * half + lane_base, ob);
       tmem_wait_ld();
       if (valid) {
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)(tok0 + t) * qdim + hq * kHeadDim);
+        uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)(tok0 + t) * qdim + hq * kHeadDim) +
+                     4 * half;
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
+        for (int cc = 0; cc < 4; ++cc) {
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int d = 8 * cc + 2 * e;
-            w[e] = pack_bf16x2(__uint_as_float(o[d >> 5][d & 31]) * inv,
-                               __uint_as_float(o[(d + 1) >> 5][(d + 1) & 31]) * inv);
+            float x0 = __uint_as_float(oa[d]) * wa, x1 = __uint_as_float(oa[d + 1]) * wa;
+            if (two) {
+              x0 = fmaf(__uint_as_float(ob[d]), wb, x0);
+              x1 = fmaf(__uint_as_float(ob[d + 1]), wb, x1);
+            }
+            w[e] = pack_bf16x2(x0 * inv, x1 * inv);
           }
           dst[cc] = make_uint4(w[0], w[1], w[2], w[3]);
         }
@@ -387,13 +429,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     }
   }
   tc_fence_before_sync();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after_sync();
-    tmem_dealloc(tmem, kTcTmemCols);
-  }
+  named_barrier_sync(1, kEndThreads);
 }
-
 }  // namespace
 
 cudaError_t launch_paged_prefill(const PrefillParams& p, long long pool_rows, int max_q_len,
@@ -403,6 +440,13 @@ cudaError_t launch_paged_prefill(const PrefillParams& p, long long pool_rows, in
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64 || !configured[dev]) {
+    // The register split must fit the launch's pool (threads x registers per
+    // thread); a warpgroup asking for more than is left would wait forever.
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, paged_prefill_kernel);
+    if (e != cudaSuccess) return e;
+    if ((long long)fa.numRegs * kTcThreads < 128LL * kTcLowRegs + 256LL * kTcHighRegs)
+      return cudaErrorInvalidConfiguration;
     e = cudaFuncSetAttribute(paged_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)prefill_smem_bytes());
     if (e != cudaSuccess) return e;
