@@ -279,6 +279,8 @@ int tvp_paged_prefill_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const
   p.table_stride = table_stride;
   p.kv_heads = kv_heads;
   p.scale = scale;
+  int e2 = 0;
+  p.scale_pow2 = scale > 0.f && std::frexp(scale, &e2) == 0.5f;
   p.err = d_error;
   return map_cuda(launch_paged_prefill(p, (long long)num_layers * num_pages * kPage, max_q_len,
                                        num_seqs, static_cast<cudaStream_t>(stream)));

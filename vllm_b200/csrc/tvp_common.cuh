@@ -231,6 +231,13 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return r;
 }
 
+// Lane-wise max of two BF16 pairs (a NaN lane yields the other operand).
+__device__ __forceinline__ uint32_t bf16x2_max(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
 __device__ __forceinline__ float bf16lo_to_f32(uint32_t x) { return __uint_as_float(x << 16); }
 __device__ __forceinline__ float bf16hi_to_f32(uint32_t x) {
   return __uint_as_float(x & 0xffff0000u);

@@ -88,6 +88,7 @@ struct PrefillParams {
   int table_stride;
   int kv_heads;
   float scale;
+  int scale_pow2;  // scale is a positive power of two (the score rounding commutes with it)
   int32_t* err;
 };
 

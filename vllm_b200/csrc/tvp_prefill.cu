@@ -66,6 +66,39 @@ constexpr uint32_t kTcTmemCols = 256;
 // host before the first launch: an unsatisfiable increase would never return).
 constexpr int kTcLowRegs = 32;
 constexpr int kTcHighRegs = 104;
+// Of every kExpStride probability pairs, the last takes its 2^x on the FMA pipe
+// (exp2_fma_x2) instead of the MUFU; 0 = all on the MUFU.  Measured on the
+// 1 x 8192 prompt: none 567 us, a quarter 592 us, half 623 us: the softmax is
+// bound by its instruction issue, not by the MUFU, so none is the default.
+#ifndef TVP_PREFILL_EXP_STRIDE
+#define TVP_PREFILL_EXP_STRIDE 0
+#endif
+constexpr int kExpStride = TVP_PREFILL_EXP_STRIDE;
+
+// 2^x for two lanes without the MUFU, for x <= 10.  Range reduction
+// x = i + f: adding 1.5 * 2^23 rounds x to the integer i, which lands in the
+// low mantissa bits of the sum t; f = x - i lies in [-1/2, 1/2].  2^f is a
+// cubic fitted (least squares on Chebyshev nodes, reweighted toward minimax)
+// to the relative error of 2^f on that interval: 7.5e-5 at most, far below a
+// BF16 probability's 2^-9.  i enters the exponent field by an integer add of
+// t's bits shifted by 23.  Inputs below -125 (masked keys are -inf) give
+// 2^-125, a normal number that adds nothing to a BF16 P.V product.
+__device__ __forceinline__ uint64_t exp2_fma_x2(uint64_t x2) {
+  float a, b;
+  f2_unpack(x2, a, b);
+  const uint64_t x = f2_pack(fmaxf(a, -125.f), fmaxf(b, -125.f));
+  const uint64_t t = f2_add(x, f2_pack(12582912.f, 12582912.f));
+  const uint64_t i = f2_add(t, f2_pack(-12582912.f, -12582912.f));  // round(x), exact
+  const uint64_t f = f2_fma(i, f2_pack(-1.f, -1.f), x);              // x - i, exact
+  uint64_t y = f2_fma(f, f2_pack(0.055171769f, 0.055171769f), f2_pack(0.24261113f, 0.24261113f));
+  y = f2_fma(y, f, f2_pack(0.69326097f, 0.69326097f));
+  y = f2_fma(y, f, f2_pack(0.99992806f, 0.99992806f));
+  float ya, yb, ta, tb;
+  f2_unpack(y, ya, yb);
+  f2_unpack(t, ta, tb);
+  return f2_pack(__int_as_float(__float_as_int(ya) + (__float_as_int(ta) << 23)),
+                 __int_as_float(__float_as_int(yb) + (__float_as_int(tb) << 23)));
+}
 constexpr int kOffQ = 0;
 constexpr int kOffP = kOffQ + kTcQBytes;                // P(even), then P(odd)
 constexpr int kOffStages = kOffP + 2 * kTcPBytes;
@@ -274,6 +307,12 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   float m = -INFINITY, l = 0.f;  // this side's running max (base-2 units) and normaliser
   bool ok = true;
   constexpr float kLog2e = 1.4426950408889634f;
+  // A positive power-of-two scale (the reference's 1/8) commutes with the
+  // BF16 rounding of the scores and folds into the exponent's constant:
+  // bf16(s 2^k) = 2^k bf16(s), and r 2^k log2(e) is the same product as
+  // before, so the bits do not change and a multiply per score is saved.
+  const bool pow2 = p.scale_pow2 != 0;
+  const float c_log2 = pow2 ? p.scale * kLog2e : kLog2e;
   const uint64_t scale2 = f2_pack(p.scale, p.scale);
   for (int c = side; c < n_chunks; c += 2) {
     bool ready = !*abort_flag && mbar_wait_bounded(bar(kBarSFull + side), (c >> 1) & 1);
@@ -294,9 +333,9 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     const int key0 = c * kTcChunk;
     const bool diagonal = key0 + kTcChunk - 1 > pos0;
     uint32_t pk[kTcChunk / 2];
-    float mxs[8];  // eight independent max chains, merged by a tree
+    uint32_t mxp[8];  // eight independent running maxima of BF16 pairs
 #pragma unroll
-    for (int i = 0; i < 8; ++i) mxs[i] = -INFINITY;
+    for (int i = 0; i < 8; ++i) mxp[i] = 0xff80ff80u;  // (-inf, -inf)
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       uint32_t sr[32];
@@ -304,8 +343,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 32; j += 2) {
-        float a, b;
-        f2_unpack(f2_mul(f2_pack(__uint_as_float(sr[j]), __uint_as_float(sr[j + 1])), scale2), a, b);
+        float a = __uint_as_float(sr[j]), b = __uint_as_float(sr[j + 1]);
+        if (!pow2) f2_unpack(f2_mul(f2_pack(a, b), scale2), a, b);
         if (diagonal) {
           const int key = key0 + 32 * half + j;
           if (key > qpos) a = -INFINITY;
@@ -313,11 +352,14 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         }
         const uint32_t pr = pack_bf16x2(a, b);
         pk[16 * half + (j >> 1)] = pr;
-        mxs[(j >> 1) & 7] = max3(mxs[(j >> 1) & 7], bf16lo_to_f32(pr), bf16hi_to_f32(pr));
+        mxp[(j >> 1) & 7] = bf16x2_max(mxp[(j >> 1) & 7], pr);
       }
     }
-    float mx = fmaxf(max3(mxs[0], mxs[1], mxs[2]), max3(mxs[3], mxs[4], max3(mxs[5], mxs[6], mxs[7])));
-    mx *= kLog2e;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) mxp[i] = bf16x2_max(mxp[i], mxp[i + 4]);
+    const uint32_t m2 = bf16x2_max(bf16x2_max(mxp[0], mxp[1]), bf16x2_max(mxp[2], mxp[3]));
+    float mx = fmaxf(bf16lo_to_f32(m2), bf16hi_to_f32(m2));
+    mx *= c_log2;
     // Lazy running max: rescale only when a score beats the side's max by
     // more than kLazyMargin (probabilities stay below 2^kLazyMargin).
     float alpha = 1.f;
@@ -346,7 +388,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     // P row into this side's swizzled A tile of O += P V.  S(c)'s commit also
     // covered P V(c - 2), the last reader of this tile.
     unsigned char* p_tile = smem + kOffP + side * kTcPBytes;
-    const uint64_t l2e2 = f2_pack(kLog2e, kLog2e), nb2 = f2_pack(nbase, nbase);
+    const uint64_t l2e2 = f2_pack(c_log2, c_log2), nb2 = f2_pack(nbase, nbase);
     uint64_t ls2[4];  // four independent paired sums
 #pragma unroll
     for (int i = 0; i < 4; ++i) ls2[i] = f2_pack(0.f, 0.f);
@@ -356,9 +398,16 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const uint32_t pr = pk[4 * cc + e];
-        float a0, a1;
-        f2_unpack(f2_fma(f2_pack(bf16lo_to_f32(pr), bf16hi_to_f32(pr)), l2e2, nb2), a0, a1);
-        const float p0 = fast_exp2(a0), p1 = fast_exp2(a1);
+        const uint64_t arg = f2_fma(f2_pack(bf16lo_to_f32(pr), bf16hi_to_f32(pr)), l2e2, nb2);
+        float p0, p1;
+        if (kExpStride > 0 && e % (kExpStride > 0 ? kExpStride : 1) == kExpStride - 1) {
+          f2_unpack(exp2_fma_x2(arg), p0, p1);
+        } else {
+          float a0, a1;
+          f2_unpack(arg, a0, a1);
+          p0 = fast_exp2(a0);
+          p1 = fast_exp2(a1);
+        }
         ls2[e] = f2_add(ls2[e], f2_pack(p0, p1));
         w[e] = pack_bf16x2(p0, p1);
       }
