@@ -103,6 +103,7 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
                               const __grid_constant__ CUtensorMap v_map) {
   constexpr int PS = kStageTiles / KVH;  // pages per stage
   constexpr int PERIOD = 2 * PS;         // pages between two pages of one way
+  constexpr int W = 16 / KVH;            // ways per KV head
   constexpr int STAGES = kHeadsStages;
   // 1 KiB alignment of the stage tiles (128-byte swizzle); checked, as in K2.
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -258,6 +259,8 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
   int kbase = 0;  // range-local index of the piece's first page
   int c_kk = 0, c_stage = 0;
   uint32_t c_parity = 0;
+  HeadState st;
+  bool fold = false;
   while (pg < p_end) {
     while (pg >= end) {  // next non-empty sequence
       ++s;
@@ -271,7 +274,6 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
 
     uint32_t qb[4][2];
     load_q_frags(p.q + (size_t)s * kOutRow + h * kGroup * kHeadDim, tl, qb);
-    HeadState st;
     st.reset();
 
     for (int i = kbase + ((way - kbase) % PERIOD + PERIOD) % PERIOD; i < kbase + np; i += PERIOD) {
@@ -313,6 +315,10 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
     }
 
     merge_ways<KVH>(st, scratch, way, h, lane);
+    if (piece_end == p_end && !complete) {
+      fold = true;  // the range's last piece: published and folded below
+      break;
+    }
     if (way == 0) {
       reduce_l(st);
       const OutGroup out_group = out_of(s);
@@ -326,6 +332,32 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
     }
     kbase += np;
     pg = piece_end;
+  }
+  if (fold) {
+    // The range's last piece: the W ways of head h have nothing left to do,
+    // so when this CTA arrives last for the sequence all of them fold its
+    // pieces.  Way 0 publishes and counts, then tells the others through
+    // the last word of merge slot h (merging is over: way 0 read the slot
+    // last, and the fold's sums use only its first 2 x 9 x 32 floats).
+    float* slot_h = scratch + (size_t)h * kStateFloats * 32;
+    volatile int* last_word = reinterpret_cast<volatile int*>(slot_h + kStateFloats * 32 - 1);
+    if (way == 0) {
+      reduce_l(st);
+      const bool last = publish_partial(st, p.partials, p.counters, KVH, h, s,
+                                        partial_slot((int)c, first, T, C), first, end, T, C,
+                                        tl, lane);
+      if (lane == 0) *last_word = last ? 1 : 0;
+    }
+    const int fold_bar = 1 + 2 * KVH + h;  // after the merge's level and entry barriers
+    named_barrier_sync(fold_bar, W * 32);
+    if (*last_word) {
+      // Way u's sums: merge slot (u / 2) KVH + h, half u % 2.
+      auto sums = [&](int u) {
+        return scratch + ((size_t)((u >> 1) * KVH + h) * kStateFloats + (u & 1) * 9) * 32 + lane;
+      };
+      combine_partials_ways<W, KVH == 1 ? 1 : 2>(p.partials, KVH, h, first, end, T, C,
+                                                  out_of(s), way, lane, sums, fold_bar);
+    }
   }
 
   if (GATHER) {

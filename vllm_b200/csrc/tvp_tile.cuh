@@ -385,14 +385,13 @@ __device__ __forceinline__ void combine_partials(const float* partials, int grou
   out.store16(h * kHeadDim + d0, packed);
 }
 
-// Publishes a partial piece and, when it is the last of its sequence to arrive,
-// merges all of them (a counter per (sequence, KV head group); no waiting).
-template <int BATCH>
-__device__ __forceinline__ void finish_partial(const HeadState& st, float* partials, int* counters,
-                                               int groups, int g, int s, int slot, int first,
-                                               int end, long long T, long long R,
-                                               const OutGroup& out, const TileLane& tl,
-                                               int lane) {
+// Publishes a partial piece; true in every lane when it is the last piece of
+// its sequence to arrive (a counter per (sequence, KV head group), reset by
+// the last arriver for the next launch; no waiting).
+__device__ __forceinline__ bool publish_partial(const HeadState& st, float* partials, int* counters,
+                                                int groups, int g, int s, int slot, int first,
+                                                int end, long long T, long long R,
+                                                const TileLane& tl, int lane) {
   write_partial(st, partials + ((size_t)slot * groups + g) * kPartialFloats, tl);
   __threadfence();
   __syncwarp();
@@ -406,8 +405,105 @@ __device__ __forceinline__ void finish_partial(const HeadState& st, float* parti
       __threadfence();
     }
   }
-  last = __shfl_sync(0xffffffffu, last, 0);
-  if (last) combine_partials<BATCH>(partials, groups, g, first, end, T, R, out, lane);
+  return __shfl_sync(0xffffffffu, last, 0) != 0;
+}
+
+// Publishes a partial piece and, when it is the last of its sequence to arrive,
+// merges all of them.
+template <int BATCH>
+__device__ __forceinline__ void finish_partial(const HeadState& st, float* partials, int* counters,
+                                               int groups, int g, int s, int slot, int first,
+                                               int end, long long T, long long R,
+                                               const OutGroup& out, const TileLane& tl,
+                                               int lane) {
+  if (publish_partial(st, partials, counters, groups, g, s, slot, first, end, T, R, tl, lane))
+    combine_partials<BATCH>(partials, groups, g, first, end, T, R, out, lane);
+}
+
+// combine_partials spread over the W warps ("ways", way = 0 .. W-1) of one
+// head, for a CTA whose ways have no work left.  Way u folds pieces u, u + W,
+// u + 2W, ... (lane -> query head lane/8, channels (lane%8)*8 .. +7); the
+// loads of its first BATCH pieces go out together with the maxima's, so with
+// n <= W BATCH pieces the whole fold is about one L2 round trip instead of
+// 1 + n / BATCH.  The ways' sums meet in shared memory and way 0 writes the
+// output.  sums(u) gives way u's 9 x 32 floats (field f of lane l at f*32+l);
+// `bar` is a named barrier of the W ways.
+template <int W, int BATCH, typename Sums>
+__device__ __forceinline__ void combine_partials_ways(const float* partials, int groups, int g,
+                                                      int first, int end, long long T, long long R,
+                                                      const OutGroup& out, int way, int lane,
+                                                      Sums sums, int bar) {
+  const int r0 = range_of_page(first, T, R), r1 = range_of_page(end - 1, T, R);
+  const int n = r1 - r0 + 1;
+  const int hq = lane >> 3, d0 = (lane & 7) * 8;
+  float4 mb[BATCH], lb[BATCH], a[BATCH], b[BATCH];
+  auto load_batch = [&](int j0) {  // this way's pieces j0, j0 + W, ...
+#pragma unroll
+    for (int k = 0; k < BATCH; ++k) {
+      const int j = j0 + k * W;
+      mb[k] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      lb[k] = a[k] = b[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (j < n) {
+        const float* part = partial_of(partials, groups, g, r0 + j, r0, first, T, R);
+        mb[k] = __ldcg(reinterpret_cast<const float4*>(part));
+        lb[k] = __ldcg(reinterpret_cast<const float4*>(part + kGroup));
+        const float* src = part + 2 * kGroup + hq * kHeadDim + d0;
+        a[k] = __ldcg(reinterpret_cast<const float4*>(src));
+        b[k] = __ldcg(reinterpret_cast<const float4*>(src + 4));
+      }
+    }
+  };
+  load_batch(way);
+  // Per-head maximum over all pieces (every way computes it).
+  float4 M = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+  for (int j = lane; j < n; j += 32) {
+    const float4 m = __ldcg(reinterpret_cast<const float4*>(
+        partial_of(partials, groups, g, r0 + j, r0, first, T, R)));
+    M.x = fmaxf(M.x, m.x); M.y = fmaxf(M.y, m.y); M.z = fmaxf(M.z, m.z); M.w = fmaxf(M.w, m.w);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    M.x = fmaxf(M.x, __shfl_xor_sync(0xffffffffu, M.x, o));
+    M.y = fmaxf(M.y, __shfl_xor_sync(0xffffffffu, M.y, o));
+    M.z = fmaxf(M.z, __shfl_xor_sync(0xffffffffu, M.z, o));
+    M.w = fmaxf(M.w, __shfl_xor_sync(0xffffffffu, M.w, o));
+  }
+  const float Mh = pick(M, hq);
+  float o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = 0.f;
+  float ls = 0.f;
+  for (int j0 = way; j0 < n; j0 += W * BATCH) {
+    if (j0 != way) load_batch(j0);
+#pragma unroll
+    for (int k = 0; k < BATCH; ++k) {
+      const float mh = pick(mb[k], hq);
+      const float wh = mh == -INFINITY ? 0.f : exp2f(mh - Mh);
+      ls += wh * pick(lb[k], hq);
+      o[0] += wh * a[k].x; o[1] += wh * a[k].y; o[2] += wh * a[k].z; o[3] += wh * a[k].w;
+      o[4] += wh * b[k].x; o[5] += wh * b[k].y; o[6] += wh * b[k].z; o[7] += wh * b[k].w;
+    }
+  }
+  float* mine = sums(way);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) mine[i * 32] = o[i];
+  mine[8 * 32] = ls;
+  named_barrier_sync(bar, W * 32);
+  if (way != 0) return;
+#pragma unroll 1
+  for (int u = 1; u < W; ++u) {
+    const float* other = sums(u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] += other[i * 32];
+    ls += other[8 * 32];
+  }
+  const float inv = ls > 0.f ? 1.f / ls : 0.f;
+  uint4 packed;
+  packed.x = pack_bf16x2(o[0] * inv, o[1] * inv);
+  packed.y = pack_bf16x2(o[2] * inv, o[3] * inv);
+  packed.z = pack_bf16x2(o[4] * inv, o[5] * inv);
+  packed.w = pack_bf16x2(o[6] * inv, o[7] * inv);
+  out.store16(hq * kHeadDim + d0, packed);
 }
 
 }  // namespace tvp
