@@ -115,6 +115,25 @@ def test_page_permutation_gives_identical_bits():
     assert np.array_equal(out1, out2)
 
 
+def racing_last_arrivers_case(seed, kv_heads=8):
+    """8 ranges of 32 pages: sequence 0 fills ranges 0 and 1 and 31 pages of
+    range 2 (whose last page starts sequence 1), so its three pieces finish at
+    about the same time and its last arriver is sometimes a range's last piece
+    (merged through shared memory) and sometimes not (merged in the loop)."""
+    return W.decode_random(seed, [95 * 16, 16, 160 * 16], kv_heads=kv_heads)
+
+
+def test_merge_is_identical_whichever_piece_arrives_last():
+    case = racing_last_arrivers_case(90)
+    ref, err = run_decode(case, num_ctas=8)
+    assert err == 0
+    assert_close_bf16(ref, exact_out(case), ATOL, RTOL)
+    for _ in range(30):
+        out, err = run_decode(case, num_ctas=8)
+        assert err == 0
+        assert np.array_equal(out, ref)
+
+
 def test_stale_slots_past_the_length_never_leak():
     """NaN/Inf bit patterns in unused slots of a row's last page are ignored."""
     case = W.decode_random(41, [17, 40, 1, 250])

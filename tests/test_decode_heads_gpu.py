@@ -77,6 +77,22 @@ def test_page_permutation_is_bit_exact():
     assert np.array_equal(out, out2)
 
 
+@pytest.mark.parametrize("kv_heads", [1, 2, 4])
+def test_merge_is_identical_whichever_piece_arrives_last(kv_heads):
+    """Sequence 0 spans ranges 0, 1 and most of 2 of 8 (32 pages each): its
+    last arriver is sometimes a range's last piece (merged through shared
+    memory) and sometimes not (merged in the page loop); the bits must not
+    depend on which."""
+    case = W.decode_random(91 + kv_heads, [95 * 16, 16, 160 * 16], kv_heads=kv_heads)
+    ref, err = run_decode(case, num_ctas=8)
+    assert err == 0
+    assert_close_bf16(ref, f32(oracle_out(case)), ATOL, RTOL)
+    for _ in range(30):
+        out, err = run_decode(case, num_ctas=8)
+        assert err == 0
+        assert np.array_equal(out, ref)
+
+
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_head_sharded_ranks_reassemble_the_8_head_attention(world):
     """The KV-head-sharded deployment, ranks emulated one after another on one

@@ -43,6 +43,7 @@
 namespace tvp {
 
 constexpr int kMergeFields = 2;  // per-lane values exchanged per merge round (see below)
+constexpr int kTailBarrier = 1 + kMaxKvHeads;  // all consumer warps (ids 1..8: the set merges)
 
 
 // ---------------------------------------------------------------------------
@@ -270,6 +271,8 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
   // and an odd number of stages, consecutive rounds of a slot go to different
   // sets, so a set's wait is gated on the slot's tag (stage_tag_wait).
   int c_kk = 0, c_stage = 0, c_round = 0;
+  HeadState st;
+  bool last_partial = false;  // the range ends inside a sequence that started earlier
   while (pg < p_end) {
     while (pg >= end) {  // next non-empty sequence
       ++s;
@@ -284,7 +287,6 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
     // Q_g^T operand fragments: column n = tr holds query head 4g + tr (tr < 4).
     uint32_t qb[4][2];
     load_q_frags(p.q + (size_t)s * kOutRow + g * kGroup * kHeadDim, tl, qb);
-    HeadState st;
     st.reset();
 
     for (int i = set; i < n; i += SETS) {
@@ -379,6 +381,10 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
       }
     }
 
+    if (piece_end == p_end && !complete) {
+      last_partial = true;  // published and merged below
+      break;
+    }
     if (set == 0) {
       reduce_l(st);
       const OutGroup out_group = local_out(p.out + (size_t)s * kOutRow + g * kGroup * kHeadDim);
@@ -391,6 +397,25 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
     }
     kbase += n;
     pg = piece_end;
+  }
+  if (last_partial) {
+    // The range's last piece ends inside a sequence that started earlier; a
+    // short step's merges all come from such pieces.  Once every consumer warp
+    // has read its last tile the stages are free (every copy issued has landed
+    // and been consumed), and head g's eighth of them stages the sequence's
+    // partials, so that the merge costs one L2 round trip per 27 pieces.
+    named_barrier_sync(kTailBarrier, SETS * kMaxKvHeads * 32);
+    if (set == 0) {
+      reduce_l(st);
+      if (publish_partial(st, p.partials, p.counters, kMaxKvHeads, g, s,
+                          partial_slot((int)c, first, T, C), first, end, T, C, tl, lane)) {
+        constexpr int kShareBytes = STAGES * kStageBytes / kMaxKvHeads;
+        combine_partials_staged(
+            p.partials, kMaxKvHeads, g, first, end, T, C,
+            local_out(p.out + (size_t)s * kOutRow + g * kGroup * kHeadDim), lane,
+            reinterpret_cast<float*>(smem + (size_t)g * kShareBytes), (kShareBytes - 512) / 1024);
+      }
+    }
   }
 }
 

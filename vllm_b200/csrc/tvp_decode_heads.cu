@@ -28,6 +28,7 @@ namespace tvp {
 
 constexpr int kHeadsStages = 6;
 constexpr int kDoneBarrier = 15;  // named barrier of the 16 consumer warps at a gather's end
+constexpr int kTailBarrier = 14;  // the 16 consumer warps, before the stages become merge scratch
 constexpr int kStateFloats = 20;  // m0, m1, l0, l1, acc[16] per lane
 constexpr int kMergeSlots = 8;    // senders of the widest merge level (W / 2 x KVH)
 
@@ -103,7 +104,6 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
                               const __grid_constant__ CUtensorMap v_map) {
   constexpr int PS = kStageTiles / KVH;  // pages per stage
   constexpr int PERIOD = 2 * PS;         // pages between two pages of one way
-  constexpr int W = 16 / KVH;            // ways per KV head
   constexpr int STAGES = kHeadsStages;
   // 1 KiB alignment of the stage tiles (128-byte swizzle); checked, as in K2.
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
   int c_kk = 0, c_stage = 0;
   uint32_t c_parity = 0;
   HeadState st;
-  bool fold = false;
+  bool last_partial = false;  // the range ends inside a sequence that started earlier
   while (pg < p_end) {
     while (pg >= end) {  // next non-empty sequence
       ++s;
@@ -316,7 +316,7 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
 
     merge_ways<KVH>(st, scratch, way, h, lane);
     if (piece_end == p_end && !complete) {
-      fold = true;  // the range's last piece: published and folded below
+      last_partial = true;  // published and merged below
       break;
     }
     if (way == 0) {
@@ -325,38 +325,30 @@ __global__ void __launch_bounds__(decode_threads<2, REGSPLIT>(), 1)
       if (complete)
         write_output(st, out_group, tl);
       else
-        // combine batch: 2 fits the KVH = 1 consumer's registers, 1 the others'
-        finish_partial<KVH == 1 ? 2 : 1>(st, p.partials, p.counters, KVH, h, s,
+        // combine batch 1 (the registers of the staged merge below; the
+        // fold's arithmetic does not depend on the batch)
+        finish_partial<1>(st, p.partials, p.counters, KVH, h, s,
                                          partial_slot((int)c, first, T, C), first, end, T, C,
                                          out_group, tl, lane);
     }
     kbase += np;
     pg = piece_end;
   }
-  if (fold) {
-    // The range's last piece: the W ways of head h have nothing left to do,
-    // so when this CTA arrives last for the sequence all of them fold its
-    // pieces.  Way 0 publishes and counts, then tells the others through
-    // the last word of merge slot h (merging is over: way 0 read the slot
-    // last, and the fold's sums use only its first 2 x 9 x 32 floats).
-    float* slot_h = scratch + (size_t)h * kStateFloats * 32;
-    volatile int* last_word = reinterpret_cast<volatile int*>(slot_h + kStateFloats * 32 - 1);
+  if (last_partial) {
+    // The range's last piece ends inside a sequence that started earlier.
+    // Once every consumer warp has read its last tile, the stage buffers are
+    // free (every copy the producer issued has landed and been consumed), and
+    // head h's share of them holds the sequence's partials for the merge.
+    named_barrier_sync(kTailBarrier, 2 * kStageTiles * 32);
     if (way == 0) {
       reduce_l(st);
-      const bool last = publish_partial(st, p.partials, p.counters, KVH, h, s,
-                                        partial_slot((int)c, first, T, C), first, end, T, C,
-                                        tl, lane);
-      if (lane == 0) *last_word = last ? 1 : 0;
-    }
-    const int fold_bar = 1 + 2 * KVH + h;  // after the merge's level and entry barriers
-    named_barrier_sync(fold_bar, W * 32);
-    if (*last_word) {
-      // Way u's sums: merge slot (u / 2) KVH + h, half u % 2.
-      auto sums = [&](int u) {
-        return scratch + ((size_t)((u >> 1) * KVH + h) * kStateFloats + (u & 1) * 9) * 32 + lane;
-      };
-      combine_partials_ways<W, KVH == 1 ? 1 : 2>(p.partials, KVH, h, first, end, T, C,
-                                                  out_of(s), way, lane, sums, fold_bar);
+      if (publish_partial(st, p.partials, p.counters, KVH, h, s, partial_slot((int)c, first, T, C),
+                          first, end, T, C, tl, lane)) {
+        constexpr int kShareBytes = STAGES * kStageBytes / KVH;
+        combine_partials_staged(p.partials, KVH, h, first, end, T, C, out_of(s), lane,
+                                reinterpret_cast<float*>(smem + (size_t)h * kShareBytes),
+                                (kShareBytes - 512) / 1024);
+      }
     }
   }
 

@@ -420,45 +420,55 @@ __device__ __forceinline__ void finish_partial(const HeadState& st, float* parti
     combine_partials<BATCH>(partials, groups, g, first, end, T, R, out, lane);
 }
 
-// combine_partials spread over the W warps ("ways", way = 0 .. W-1) of one
-// head, for a CTA whose ways have no work left.  Way u folds pieces u, u + W,
-// u + 2W, ... (lane -> query head lane/8, channels (lane%8)*8 .. +7); the
-// loads of its first BATCH pieces go out together with the maxima's, so with
-// n <= W BATCH pieces the whole fold is about one L2 round trip instead of
-// 1 + n / BATCH.  The ways' sums meet in shared memory and way 0 writes the
-// output.  sums(u) gives way u's 9 x 32 floats (field f of lane l at f*32+l);
-// `bar` is a named barrier of the W ways.
-template <int W, int BATCH, typename Sums>
-__device__ __forceinline__ void combine_partials_ways(const float* partials, int groups, int g,
-                                                      int first, int end, long long T, long long R,
-                                                      const OutGroup& out, int way, int lane,
-                                                      Sums sums, int bar) {
+// combine_partials for a warp with shared memory to spare.  The warp copies
+// the partials' output rows (1 KiB each, two cp.async instructions of 512
+// contiguous bytes per piece) into `stage`, a round of up to `cap` pieces at
+// once, so that a round costs one L2 round trip and no registers; the first
+// round's copies go out before the maxima's loads (copies whose 32 source and
+// 32 destination chunks are both contiguous issue fastest).  Lane L folds the
+// piece's floats 8L .. 8L+7; lanes 4-7 of each 8 read their second 16 bytes
+// first, so that each 8-lane phase of a 16-byte shared load covers all 32
+// banks.
+// The piece weights pass through a 32-entry table in `stage` instead of
+// shuffles.  The maxima, weights, normalisers and the fold of the rows in
+// piece order are combine_partials' own operations: the output is
+// bit-identical whichever of the two a sequence's last arriver runs.
+// `stage`: 16-byte aligned, 512 + 1024 cap bytes; cap >= 1.
+__device__ __forceinline__ void combine_partials_staged(const float* partials, int groups, int g,
+                                                        int first, int end, long long T,
+                                                        long long R, const OutGroup& out,
+                                                        int lane, float* stage, int cap) {
   const int r0 = range_of_page(first, T, R), r1 = range_of_page(end - 1, T, R);
   const int n = r1 - r0 + 1;
-  const int hq = lane >> 3, d0 = (lane & 7) * 8;
-  float4 mb[BATCH], lb[BATCH], a[BATCH], b[BATCH];
-  auto load_batch = [&](int j0) {  // this way's pieces j0, j0 + W, ...
-#pragma unroll
-    for (int k = 0; k < BATCH; ++k) {
-      const int j = j0 + k * W;
-      mb[k] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-      lb[k] = a[k] = b[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j < n) {
-        const float* part = partial_of(partials, groups, g, r0 + j, r0, first, T, R);
-        mb[k] = __ldcg(reinterpret_cast<const float4*>(part));
-        lb[k] = __ldcg(reinterpret_cast<const float4*>(part + kGroup));
-        const float* src = part + 2 * kGroup + hq * kHeadDim + d0;
-        a[k] = __ldcg(reinterpret_cast<const float4*>(src));
-        b[k] = __ldcg(reinterpret_cast<const float4*>(src + 4));
-      }
+  const int h = lane >> 3, d0 = (lane & 7) * 8;
+  const int slot0 = partial_slot(r0, first, T, R);
+  auto piece = [&](int j) {
+    return partials + ((size_t)(j == 0 ? slot0 : 2 * (r0 + j)) * groups + g) * kPartialFloats;
+  };
+  float4* wtab = reinterpret_cast<float4*>(stage);         // weights of a chunk's 32 pieces
+  float* rows = stage + 128;                                 // [cap][256 floats]
+  const uint32_t copy_dst = smem_addr(rows) + 16u * lane;  // + 1024 i (piece), + 512
+  auto issue = [&](int j0, int cnt) {  // output rows of pieces j0 .. j0 + cnt - 1
+    for (int i = 0; i < cnt; ++i) {
+      const float* src = piece(j0 + i) + 2 * kGroup + 4 * lane;
+      cp_async_16(copy_dst + 1024u * i, src);
+      cp_async_16(copy_dst + 1024u * i + 512u, src + 128);
     }
   };
-  load_batch(way);
-  // Per-head maximum over all pieces (every way computes it).
-  float4 M = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-  for (int j = lane; j < n; j += 32) {
-    const float4 m = __ldcg(reinterpret_cast<const float4*>(
-        partial_of(partials, groups, g, r0 + j, r0, first, T, R)));
+  int lo = 0, hi = min(cap, n);  // pieces [lo, hi) are (being) staged
+  issue(0, hi);
+  // Maxima over all pieces, loaded directly while the copies are in flight;
+  // lane j keeps m, l of piece j for the first 32 pieces' weights.
+  float4 m_lane = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+  float4 l_lane = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (lane < n) {
+    m_lane = __ldcg(reinterpret_cast<const float4*>(piece(lane)));
+    l_lane = __ldcg(reinterpret_cast<const float4*>(piece(lane) + kGroup));
+  }
+  float4 M = m_lane;
+#pragma unroll 4
+  for (int j = lane + 32; j < n; j += 32) {
+    const float4 m = __ldcg(reinterpret_cast<const float4*>(piece(j)));
     M.x = fmaxf(M.x, m.x); M.y = fmaxf(M.y, m.y); M.z = fmaxf(M.z, m.z); M.w = fmaxf(M.w, m.w);
   }
 #pragma unroll
@@ -468,42 +478,76 @@ __device__ __forceinline__ void combine_partials_ways(const float* partials, int
     M.z = fmaxf(M.z, __shfl_xor_sync(0xffffffffu, M.z, o));
     M.w = fmaxf(M.w, __shfl_xor_sync(0xffffffffu, M.w, o));
   }
-  const float Mh = pick(M, hq);
+  float4 ls = make_float4(0.f, 0.f, 0.f, 0.f);  // this lane's share of the normalisers
   float o[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) o[i] = 0.f;
-  float ls = 0.f;
-  for (int j0 = way; j0 < n; j0 += W * BATCH) {
-    if (j0 != way) load_batch(j0);
-#pragma unroll
-    for (int k = 0; k < BATCH; ++k) {
-      const float mh = pick(mb[k], hq);
-      const float wh = mh == -INFINITY ? 0.f : exp2f(mh - Mh);
-      ls += wh * pick(lb[k], hq);
-      o[0] += wh * a[k].x; o[1] += wh * a[k].y; o[2] += wh * a[k].z; o[3] += wh * a[k].w;
-      o[4] += wh * b[k].x; o[5] += wh * b[k].y; o[6] += wh * b[k].z; o[7] += wh * b[k].w;
+  const int sw = (lane >> 2) & 1;             // read order of this lane's two halves
+  const float* my_x = rows + 8 * lane + 4 * sw;  // read first
+  const float* my_y = rows + 8 * lane + 4 - 4 * sw;
+  for (int base = 0; base < n; base += 32) {
+    // m, l of the next chunk's pieces, in flight while this chunk folds
+    float4 m_next = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    float4 l_next = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (base + 32 + lane < n) {
+      m_next = __ldcg(reinterpret_cast<const float4*>(piece(base + 32 + lane)));
+      l_next = __ldcg(reinterpret_cast<const float4*>(piece(base + 32 + lane) + kGroup));
     }
+    // Lane j: weights of piece base + j for the 4 heads (0 past the last piece).
+    float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (base + lane < n) {
+      const float4 m = m_lane, l = l_lane;
+      w.x = m.x == -INFINITY ? 0.f : exp2f(m.x - M.x);
+      w.y = m.y == -INFINITY ? 0.f : exp2f(m.y - M.y);
+      w.z = m.z == -INFINITY ? 0.f : exp2f(m.z - M.z);
+      w.w = m.w == -INFINITY ? 0.f : exp2f(m.w - M.w);
+      ls.x += w.x * l.x; ls.y += w.y * l.y; ls.z += w.z * l.z; ls.w += w.w * l.w;
+    }
+    __syncwarp();  // the previous chunk's weights are read
+    wtab[lane] = w;
+    __syncwarp();
+    const float* wcol = reinterpret_cast<const float*>(wtab) + h;  // piece jj's weight at 4 jj
+    const int cnt = min(32, n - base);
+    int jj = 0;
+    while (jj < cnt) {
+      const int j = base + jj;
+      if (j == hi) {  // the next round, once every lane has read this one
+        __syncwarp();
+        lo = j;
+        hi = min(j + cap, n);
+        issue(lo, hi - lo);
+      }
+      cp_async_wait_all();
+      __syncwarp();
+      const int stop = min(cnt, hi - base);  // pieces of this chunk in the staged round
+#pragma unroll 4
+      for (; jj < stop; ++jj) {
+        const float wh = wcol[4 * jj];
+        const float4 x = *reinterpret_cast<const float4*>(my_x + 256 * (base + jj - lo));
+        const float4 y = *reinterpret_cast<const float4*>(my_y + 256 * (base + jj - lo));
+        const float4 a = sw ? y : x, b = sw ? x : y;  // channels d0 .. +3, d0 + 4 .. +7
+        o[0] += wh * a.x; o[1] += wh * a.y; o[2] += wh * a.z; o[3] += wh * a.w;
+        o[4] += wh * b.x; o[5] += wh * b.y; o[6] += wh * b.z; o[7] += wh * b.w;
+      }
+    }
+    m_lane = m_next;
+    l_lane = l_next;
   }
-  float* mine = sums(way);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) mine[i * 32] = o[i];
-  mine[8 * 32] = ls;
-  named_barrier_sync(bar, W * 32);
-  if (way != 0) return;
-#pragma unroll 1
-  for (int u = 1; u < W; ++u) {
-    const float* other = sums(u);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] += other[i * 32];
-    ls += other[8 * 32];
+  for (int k = 16; k > 0; k >>= 1) {
+    ls.x += __shfl_xor_sync(0xffffffffu, ls.x, k);
+    ls.y += __shfl_xor_sync(0xffffffffu, ls.y, k);
+    ls.z += __shfl_xor_sync(0xffffffffu, ls.z, k);
+    ls.w += __shfl_xor_sync(0xffffffffu, ls.w, k);
   }
-  const float inv = ls > 0.f ? 1.f / ls : 0.f;
+  const float lsum = pick(ls, h);
+  const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
   uint4 packed;
   packed.x = pack_bf16x2(o[0] * inv, o[1] * inv);
   packed.y = pack_bf16x2(o[2] * inv, o[3] * inv);
   packed.z = pack_bf16x2(o[4] * inv, o[5] * inv);
   packed.w = pack_bf16x2(o[6] * inv, o[7] * inv);
-  out.store16(hq * kHeadDim + d0, packed);
+  out.store16(h * kHeadDim + d0, packed);
 }
 
 }  // namespace tvp
