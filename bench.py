@@ -623,8 +623,9 @@ def extras(args, dev, case, k_pool, v_pool, q_all, out, tables, seq_lens, ws):
 def bench_e2e_llama():
     """The e2e workload (Llama-3.2-1B geometry, seeded random weights, 4 requests
     x 128 prompt + 128 greedy tokens, the reference's scheduler): tokens/s of the
-    unmodified engine and of the engine with this path dropped in (best of 2
-    runs each, same B200, separate processes)."""
+    unmodified engine and of the engine with this path dropped in (best of 3
+    runs each, the first of which also builds the decode step's graph; same
+    B200, separate processes)."""
     libs = [ROOT / "oracle" / "_ref" / f"libtvp_e2e_{n}.so" for n in ("ref", "tvp")]
     if not all(p.exists() for p in libs):
         return {"note": "end-to-end engines not built (make -C oracle e2e)"}
@@ -635,7 +636,7 @@ def bench_e2e_llama():
                        ("ours_batched", ["--engine", "tvp", "--mode", "batched"]),
                        ("ours_native", ["--engine", "tvp", "--mode", "native"])):
         r = subprocess.run([sys.executable, str(ROOT / "tests" / "e2e_runner.py"), *args,
-                            "--runs", "2"], capture_output=True, text=True, timeout=900)
+                            "--runs", "3"], capture_output=True, text=True, timeout=900)
         if r.returncode != 0:
             out[name] = {"error": r.stderr[-300:]}
             continue
