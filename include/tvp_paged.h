@@ -144,6 +144,14 @@ int tvp_decode_plan(const int32_t* d_seq_lens, int batch, int table_stride, int 
  * Pages are read in place.  The workspace must hold a plan made by
  * tvp_decode_plan with the same d_seq_lens contents, batch, kv_heads and
  * num_ctas.
+ * With 8 KV heads in FAST mode the launch is a programmatic dependent launch:
+ * when the kernel before it in the stream releases its dependents early, as
+ * tvp_rope_append and tvp_decode_qkv_rope_append do, this kernel reads the
+ * plan and the block tables while that kernel runs, and waits for it before
+ * it reads q or any page.  So a kernel that releases its dependents early
+ * must not write the plan, the workspace or the block tables when it runs
+ * right before this call; after any other kernel (tvp_decode_plan included)
+ * ordinary stream order holds.
  */
 int tvp_paged_decode_attention(const tvp_bf16* q, const tvp_bf16* k_pool, const tvp_bf16* v_pool,
                                int num_pages, int num_layers, int layer, int kv_heads, int q_heads,

@@ -134,6 +134,48 @@ def test_merge_is_identical_whichever_piece_arrives_last():
         assert np.array_equal(out, ref)
 
 
+def test_attention_right_after_append_sees_the_new_token():
+    """The decode attention starts while the append before it in the stream
+    is still running (programmatic dependent launch).  The new token is built
+    to dominate every head's attention (old keys near zero, its key along the
+    query) with value +5, and its slot holds -5 before each append: an
+    attention that copied the last page too early would return about -5."""
+    rng = np.random.default_rng(77)
+    lens = np.array([130, 17, 1, 500, 16, 33], np.int32)
+    case = W.decode_random(78, lens.tolist())
+    k_pool = (dev_bf16(case.k_pool).float() * 0.01).to(torch.bfloat16)
+    v_pool = dev_bf16(case.v_pool)
+    tables = dev_i32(case.tables)
+    lens_d = dev_i32(lens)
+    pos = dev_i32(lens - 1)
+    B = len(lens)
+    ws = ops.DecodeWorkspace(B, "cuda")
+    err = ops.new_error_word("cuda")
+    ops.decode_plan(lens_d, case.tables.shape[1], ws, error=err)
+    q = dev_bf16(W.normal_bf16(rng, (B, 2048)))
+    # each KV head's new key: 64 x the mean of its 4 query heads, not rotated
+    # (scores of 24 and more against ~0 for up to 499 old keys)
+    k_new = (q.float().view(B, 8, 4, 64).mean(dim=2) * 64).reshape(B, 512).to(torch.bfloat16)
+    v_new = torch.full((B, 512), 5.0, dtype=torch.bfloat16, device="cuda")
+    rows = torch.arange(B, device="cuda")
+    page = tables.long()[rows, (pos // 16).long()]
+    slot = (pos % 16).long()
+    out = torch.empty_like(q)
+    for it in range(20):
+        v_pool[0, page, slot] = -5.0  # stale contents of the new token's slot
+        k_pool[0, page, slot] = k_new
+        ops.rope_append(k_pool, v_pool, 0, tables, pos, k_new.clone(), v_new, rope_k=False,
+                        writeback_k=False, error=err)
+        ops.paged_decode_attention(q, k_pool, v_pool, 0, tables, lens_d, ws, out=out, error=err)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        o = out.float()
+        assert (o > 4.5).all(), f"iteration {it}: min {o.min().item():.3f} (stale slot read?)"
+    exact = oracle.decode_attention_f64(host_bf16(q), host_bf16(k_pool), host_bf16(v_pool), 0,
+                                        case.tables, lens)
+    assert_close_bf16(host_bf16(out), exact, ATOL, RTOL, "after append")
+
+
 def test_stale_slots_past_the_length_never_leak():
     """NaN/Inf bit patterns in unused slots of a row's last page are ignored."""
     case = W.decode_random(41, [17, 40, 1, 250])

@@ -11,6 +11,10 @@
 namespace tvp {
 
 __global__ void __launch_bounds__(256) rope_append_kernel(AppendParams p) {
+  // A decode attention launched after this one (programmatic dependent
+  // launch) may start its own prologue now: it reads what this kernel writes
+  // (q and each row's last page) only after its griddepcontrol.wait.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int t = blockIdx.x;
   const int pos = p.token_pos[t];
   const int seq = p.token_seq ? p.token_seq[t] : t;

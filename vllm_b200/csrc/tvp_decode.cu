@@ -194,6 +194,12 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
                         : 0;
     int stage = 0, round = 0, issued = 0;
     uint32_t empty_parity = 1;  // parity of the previous round of each slot
+    // Launched as a programmatic dependent launch: the kernel before this one
+    // in the stream (the append of the step's new token) may still be
+    // running.  It writes pages and q, never the plan or the block tables, so
+    // the walk's first loads above go out now and the wait comes before the
+    // first page copy.
+    bool waited = false;
     for (int pg = p_begin, kk = 0; pg < p_end; ++pg, ++kk) {
       const int phys = next_phys;
       if (pg + 1 < p_end) {
@@ -214,6 +220,12 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
           }
           break;
         }
+      }
+      if (!waited) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        // the previous grid's page writes, seen by this thread's copies
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        waited = true;
       }
       const bool ok = phys >= 0 && phys < p.num_pages;
       const uint32_t full = smem_addr(&full_bar[stage]);
@@ -245,6 +257,9 @@ __global__ void __launch_bounds__(decode_threads<SETS, REGSPLIT>(), 1)
 
   // ------------------------------ consumers -------------------------------
   if (REGSPLIT) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
+  // q and the rows' last pages may be the previous grid's output, and this
+  // grid's outputs may be inputs it still reads: nothing before the wait.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int set = warp / kMaxKvHeads;
   const int g = warp % kMaxKvHeads;
   const TileLane tl(lane);
@@ -573,15 +588,27 @@ cudaError_t launch_paged_decode(const DecodeParams& p, long long pool_rows, int 
   if (p.kv_heads != kMaxKvHeads) return launch_paged_decode_heads(p, k_map, v_map, num_ctas, stream);
   const DecodeForm form = decode_form(dev);
   if (form == DecodeForm::kUnknown) return cudaErrorInvalidDeviceFunction;
-  if (form == DecodeForm::kSplit)
-    paged_decode_kernel<kSplitStages, 2, true, true>
-        <<<num_ctas, decode_threads<2, true>(), decode_smem_bytes<kSplitStages, 2>(), stream>>>(
-            p, k_map, v_map);
-  else
-    paged_decode_kernel<kPlainStages, 1, true, false>
-        <<<num_ctas, decode_threads<1, false>(), decode_smem_bytes<kPlainStages, 1>(), stream>>>(
-            p, k_map, v_map);
-  return cudaGetLastError();
+  // Programmatic dependent launch: the CTAs start their plan reads, table
+  // walk and first copies while the previous kernel finishes (see the
+  // producer's wait).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)num_ctas);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (form == DecodeForm::kSplit) {
+    cfg.blockDim = dim3(decode_threads<2, true>());
+    cfg.dynamicSmemBytes = decode_smem_bytes<kSplitStages, 2>();
+    return cudaLaunchKernelEx(&cfg, paged_decode_kernel<kSplitStages, 2, true, true>, p, k_map,
+                              v_map);
+  }
+  cfg.blockDim = dim3(decode_threads<1, false>());
+  cfg.dynamicSmemBytes = decode_smem_bytes<kPlainStages, 1>();
+  return cudaLaunchKernelEx(&cfg, paged_decode_kernel<kPlainStages, 1, true, false>, p, k_map,
+                            v_map);
 }
 
 }  // namespace tvp
