@@ -252,16 +252,24 @@ int tvp_decode_projections(const tvp_bf16* x, int rows, int k, int count, const 
  * 3-22), bit for bit.  w: [2048][k]; hidden: [rows][2048] BF16 (updated in
  * place: hidden += bf16(w x)); then norm_out[t] = bf16((hidden[t] / r_t) g)
  * with r_t = sqrt(sum_i hidden[t][i]^2 / 2048 + 1e-5), the sum taken in the
- * reference kernel's order.  The last CTA of the launch computes the norm;
- * d_counter (one int32 of device memory, zeroed once before first use) counts
- * the finished CTAs and is zeroed again by that CTA.  rows 1..8, k a multiple
- * of 256; x, w, hidden, norm_gain, norm_out 16-byte aligned, norm_out
- * overlapping none of x, hidden, norm_gain.  Programmatic dependent launch,
- * as tvp_decode_projections.  Launches that share d_counter must not overlap.
+ * reference kernel's order.  Each CTA sums the squares of its own features
+ * as a subtree of the reference's tree and publishes it; once all 128 CTAs
+ * have arrived, each normalises its own features.  d_scratch holds the
+ * arrival counter (it grows by 128 per launch), an error word and the
+ * subtree sums: TVP_NORM_SCRATCH_BYTES of device memory, 16-byte aligned,
+ * zeroed once before first use.  The CTAs wait for one another, bounded by
+ * 2 s, after which a CTA sets TVP_DEVERR_TIMEOUT in the error word (the int32
+ * at d_scratch + 4) and leaves its norm outputs unwritten; on a device that
+ * cannot hold all 128 CTAs at once the launch's last CTA computes the whole
+ * norm instead.  rows 1..8, k a multiple of 256; x, w, hidden, norm_gain,
+ * norm_out 16-byte aligned, norm_out and d_scratch overlapping none of x,
+ * hidden, norm_gain.  Programmatic dependent launch, as
+ * tvp_decode_projections.  Launches that share d_scratch must not overlap.
  */
+#define TVP_NORM_SCRATCH_BYTES 4352
 int tvp_decode_projection_residual_rmsnorm(const tvp_bf16* x, int rows, int k, const tvp_bf16* w,
                                            tvp_bf16* hidden, const tvp_bf16* norm_gain,
-                                           tvp_bf16* norm_out, int32_t* d_counter,
+                                           tvp_bf16* norm_out, void* d_scratch,
                                            tvp_stream_t stream);
 
 /*

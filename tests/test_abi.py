@@ -208,15 +208,17 @@ def test_fused_projection_forms_reject_bad_arguments_on_host(native):
     fake = ctypes.c_void_p(0x10000)
     odd = ctypes.c_void_p(0x10008)
     f = native.tvp_decode_projection_residual_rmsnorm
-    assert f(None, 4, 2048, fake, fake, fake, ctypes.c_void_p(0x20000), fake, None) == N.TVP_ERR_INVALID_ARGUMENT
-    assert f(fake, 9, 2048, fake, ctypes.c_void_p(0x20000), fake, ctypes.c_void_p(0x30000), fake,
-             None) == N.TVP_ERR_INVALID_ARGUMENT                      # rows 1..8
-    assert f(fake, 4, 100, fake, ctypes.c_void_p(0x20000), fake, ctypes.c_void_p(0x30000), fake,
-             None) == N.TVP_ERR_INVALID_ARGUMENT                      # k a multiple of 256
-    assert f(fake, 4, 2048, fake, ctypes.c_void_p(0x20000), fake, odd, fake,
-             None) == N.TVP_ERR_INVALID_ARGUMENT                      # 16-byte alignment
-    assert f(fake, 4, 2048, fake, ctypes.c_void_p(0x20000), fake, ctypes.c_void_p(0x20000), fake,
-             None) == N.TVP_ERR_INVALID_ARGUMENT                      # norm_out overlaps hidden
+    hid, out, scr = ctypes.c_void_p(0x20000), ctypes.c_void_p(0x30000), ctypes.c_void_p(0x50000)
+    assert f(None, 4, 2048, fake, hid, fake, out, scr, None) == N.TVP_ERR_INVALID_ARGUMENT
+    assert f(fake, 9, 2048, fake, hid, fake, out, scr, None) == N.TVP_ERR_INVALID_ARGUMENT  # rows 1..8
+    assert f(fake, 4, 100, fake, hid, fake, out, scr, None) == N.TVP_ERR_INVALID_ARGUMENT   # k % 256
+    assert f(fake, 4, 2048, fake, hid, fake, odd, scr, None) == N.TVP_ERR_INVALID_ARGUMENT  # alignment
+    assert f(fake, 4, 2048, fake, hid, fake, hid, scr, None) == N.TVP_ERR_INVALID_ARGUMENT  # norm_out on hidden
+    assert f(fake, 4, 2048, fake, hid, fake, out, None, None) == N.TVP_ERR_INVALID_ARGUMENT  # no scratch
+    assert f(fake, 4, 2048, fake, hid, fake, out, ctypes.c_void_p(0x50008),
+             None) == N.TVP_ERR_INVALID_ARGUMENT                                          # scratch alignment
+    assert f(fake, 4, 2048, fake, hid, fake, out, ctypes.c_void_p(0x21000),
+             None) == N.TVP_ERR_INVALID_ARGUMENT                                          # scratch on hidden
     g = native.tvp_decode_qkv_rope_append
     args = [fake, 4, 2048, fake, fake, fake, ctypes.c_void_p(0x40000), fake, fake, 8, 16, 0, fake, 4,
             fake, None, None]

@@ -18,6 +18,7 @@ from pathlib import Path
 import pytest
 import torch
 
+from vllm_b200 import _native as N
 from vllm_b200 import ops
 
 ROOT = Path(__file__).resolve().parents[1]
@@ -160,15 +161,17 @@ def test_back_to_back_launches_read_the_previous_output():
 @pytest.mark.parametrize("rows", [1, 4, 8])
 @pytest.mark.parametrize("k", [2048, 8192])  # O projection, down projection
 def test_residual_rmsnorm_form_is_residual_add_then_the_reference_rmsnorm(reference_engine, rows, k):
-    """tvp_decode_projection_residual_rmsnorm: the residual epilogue, then (the
-    launch's last CTA) the reference's rmsNormKernel of the updated rows, bit
-    for bit; twice in a row on one counter (each launch zeroes it again)."""
+    """tvp_decode_projection_residual_rmsnorm: the residual epilogue, then the
+    reference's rmsNormKernel of the updated rows, bit for bit (each CTA sums
+    its features' squares as a subtree of the reference's tree, and all CTAs
+    normalise their own features once every subtree is in); three times in a
+    row on one scratch."""
     reference_engine.e2e_ref_rmsnorm.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int]
     x, (w,) = make(rows, k, [2048], seed=90 + rows + k)
     g = torch.Generator(device="cuda").manual_seed(rows + 3)
     hidden0 = (torch.randn(rows, 2048, generator=g, device="cuda") * 3).to(torch.bfloat16)
     gain = (1 + 0.1 * torch.randn(2048, generator=g, device="cuda")).to(torch.bfloat16)
-    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    scratch = ops.norm_scratch("cuda")
     # expected: K5 residual form, then the reference kernel on its output
     want_hidden = hidden0.clone()
     ops.decode_projections(x, [w], outs=[want_hidden], epilogue="residual")
@@ -177,14 +180,45 @@ def test_residual_rmsnorm_form_is_residual_add_then_the_reference_rmsnorm(refere
     assert reference_engine.e2e_ref_rmsnorm(want_hidden.data_ptr(), want_norm.data_ptr(),
                                             gain.data_ptr(), rows) == 0
     torch.cuda.synchronize()
-    for _ in range(2):
+    for _ in range(3):
         hidden = hidden0.clone()
         norm = torch.full_like(hidden, float("nan"))
-        ops.decode_projection_residual_rmsnorm(x, w, hidden, gain, norm, counter)
+        ops.decode_projection_residual_rmsnorm(x, w, hidden, gain, norm, scratch)
         torch.cuda.synchronize()
         assert torch.equal(hidden, want_hidden)
         assert torch.equal(norm, want_norm)
-        assert int(counter.item()) == 0
+        assert int(scratch[1].item()) == 0
+
+
+def test_residual_rmsnorm_wait_gives_up_and_reports():
+    """The CTAs of the residual + RMSNorm launch wait for one another at an
+    arrival counter, bounded by 2 s.  A counter that starts off a multiple of
+    the grid (128) makes the last arrival wait for a count nothing reaches:
+    it must give up, set TVP_DEVERR_TIMEOUT in the scratch's error word and
+    leave its 16 norm outputs per row unwritten, while the residual update
+    completes and the other CTAs write theirs (their values are unspecified:
+    the counter no longer says that every subtree is in); the next launch on
+    a good scratch is whole."""
+    x, (w,) = make(4, 2048, [2048], seed=7)
+    hidden0 = torch.randn(4, 2048, device="cuda").to(torch.bfloat16)
+    gain = torch.ones(2048, dtype=torch.bfloat16, device="cuda")
+    want_hidden = hidden0.clone()
+    ops.decode_projections(x, [w], outs=[want_hidden], epilogue="residual")
+    scratch = ops.norm_scratch("cuda")
+    scratch[0] = 1
+    hidden = hidden0.clone()
+    norm = torch.full_like(hidden, float("nan"))
+    ops.decode_projection_residual_rmsnorm(x, w, hidden, gain, norm, scratch)
+    torch.cuda.synchronize()
+    assert int(scratch[1].item()) & N.TVP_DEVERR_TIMEOUT
+    assert torch.equal(hidden, want_hidden)
+    assert int(torch.isnan(norm.float()).sum(dim=1).max()) == 16   # one CTA's features
+    good = ops.norm_scratch("cuda")
+    hidden = hidden0.clone()
+    norm2 = torch.full_like(hidden, float("nan"))
+    ops.decode_projection_residual_rmsnorm(x, w, hidden, gain, norm2, good)
+    torch.cuda.synchronize()
+    assert int(good[1].item()) == 0 and not bool(torch.isnan(norm2.float()).any())
 
 
 def _pools_and_tables(rows, seed, num_pages=64, layers=3):

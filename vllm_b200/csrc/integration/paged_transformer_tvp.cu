@@ -87,6 +87,7 @@ constexpr int kMaxContext = 1024;                     // the engine's context ca
 constexpr int kTableStride = kMaxContext / BLOCK_SIZE;  // 64, as MAX_BLOCKS_PER_SEQUENCE
 constexpr int kMaxBatch = 4;                          // MAX_BATCH_SIZE of the scheduler
 constexpr size_t kCublasWorkspace = 32u << 20;        // cuBLAS workspace of captured steps
+constexpr int kNormScratchAt = 64;                     // ints: 256 B into the error buffer
 
 void check_cuda(cudaError_t status) {
   if (status != cudaSuccess) throw std::runtime_error(cudaGetErrorString(status));
@@ -109,7 +110,10 @@ struct PathState {
   int32_t* h_decode = nullptr;
   bool h_decode_valid = false;
   int32_t* error = nullptr;    // [error word | tokens (kMaxBatch)]: one read per step
-  int32_t* norm_counter = nullptr;  // native mode: CTA counter of the fused RMSNorm launches
+  // native mode: scratch of the fused RMSNorm launches, inside the `error`
+  // allocation at int kNormScratchAt, so that its error word (int 1 of it)
+  // comes back with the step's one read
+  void* norm_scratch = nullptr;
   void* workspace = nullptr;
   size_t workspace_bytes = 0;
   void* argmax_workspace = nullptr;
@@ -122,12 +126,72 @@ struct PathState {
   // batch size, captured on the second step that uses the same buffers.
   cudaStream_t stream = nullptr;
   void* cublas_workspace = nullptr;
-  int32_t* h_out = nullptr;  // pinned copy of [error word | tokens]
+  int32_t* h_out = nullptr;  // pinned copy of [error word | tokens ... | norm scratch's first 2]
   struct StepGraph {
     std::vector<const void*> key;  // every buffer the captured launches point at
     bool warm = false;             // one eager step ran with `key`
     cudaGraphExec_t exec = nullptr;
   } graphs[kMaxBatch + 1];
+  // Batched and native modes: the prefill of a prompt runs on `stream` too, as
+  // a CUDA graph per prompt length (the last kPrefillGraphs lengths seen),
+  // captured on the second prefill of that length on the same buffers.
+  static constexpr int kPrefillGraphs = 8;
+  struct PrefillGraph {
+    int num_tokens = 0;
+    StepGraph g;
+  } prefill_graphs[kPrefillGraphs];
+  int prefill_next = 0;
+};
+
+// Runs `enqueue(st.stream)` as the graph `g` keyed by `key`: replayed when it
+// was recorded for `key`, recorded (and launched) on the second call with
+// `key`, eager on the first, which also loads every kernel.
+template <typename Enqueue>
+void run_step_graph(PathState& st, PathState::StepGraph& g, const std::vector<const void*>& key,
+                    cublasHandle_t cublas_handle, Enqueue&& enqueue) {
+  if (g.exec && g.key == key) {
+    check_cuda(cudaGraphLaunch(g.exec, st.stream));
+  } else if (g.warm && g.key == key) {
+    if (cublasSetWorkspace(cublas_handle, st.cublas_workspace, kCublasWorkspace) !=
+        CUBLAS_STATUS_SUCCESS)
+      throw std::runtime_error("cuBLAS workspace setup failed");
+    check_cuda(cudaStreamBeginCapture(st.stream, cudaStreamCaptureModeThreadLocal));
+    cudaGraph_t graph = nullptr;
+    try {
+      enqueue(st.stream);
+    } catch (...) {
+      cudaStreamEndCapture(st.stream, &graph);
+      if (graph) cudaGraphDestroy(graph);
+      throw;
+    }
+    check_cuda(cudaStreamEndCapture(st.stream, &graph));
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t made = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    check_cuda(made);
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+    g.exec = exec;
+    check_cuda(cudaGraphLaunch(g.exec, st.stream));
+  } else {
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+    g.exec = nullptr;
+    enqueue(st.stream);
+    g.key = key;
+    g.warm = true;
+  }
+}
+
+// cuBLAS works on the path's stream while a batched call runs; the caller's
+// stream (and with it cuBLAS's default workspace) is restored on return.
+struct CublasOnStream {
+  cublasHandle_t handle;
+  cudaStream_t caller = nullptr;
+  CublasOnStream(cublasHandle_t h, cudaStream_t stream) : handle(h) {
+    if (cublasGetStream(handle, &caller) != CUBLAS_STATUS_SUCCESS ||
+        cublasSetStream(handle, stream) != CUBLAS_STATUS_SUCCESS)
+      throw std::runtime_error("cuBLAS stream setup failed");
+  }
+  ~CublasOnStream() { cublasSetStream(handle, caller); }
 };
 
 PathState& path_state() {
@@ -146,10 +210,10 @@ PathState& path_state() {
                           (kMaxBatch * kTableStride + 2 * kMaxBatch) * sizeof(int32_t)));
     check_cuda(cudaMallocHost(reinterpret_cast<void**>(&st.h_decode),
                               (kMaxBatch * kTableStride + 2 * kMaxBatch) * sizeof(int32_t)));
-    check_cuda(cudaMalloc(reinterpret_cast<void**>(&st.error), (1 + kMaxBatch) * sizeof(int32_t)));
-    check_cuda(cudaMemset(st.error, 0, (1 + kMaxBatch) * sizeof(int32_t)));
-    check_cuda(cudaMalloc(reinterpret_cast<void**>(&st.norm_counter), sizeof(int32_t)));
-    check_cuda(cudaMemset(st.norm_counter, 0, sizeof(int32_t)));
+    check_cuda(cudaMalloc(reinterpret_cast<void**>(&st.error),
+                          kNormScratchAt * sizeof(int32_t) + TVP_NORM_SCRATCH_BYTES));
+    check_cuda(cudaMemset(st.error, 0, kNormScratchAt * sizeof(int32_t) + TVP_NORM_SCRATCH_BYTES));
+    st.norm_scratch = st.error + kNormScratchAt;
     st.argmax_workspace_bytes = tvp_greedy_argmax_workspace_bytes(kMaxBatch);
     check_cuda(cudaMalloc(&st.argmax_workspace, st.argmax_workspace_bytes));
     check_cuda(cudaMemset(st.argmax_workspace, 0, st.argmax_workspace_bytes));
@@ -164,7 +228,7 @@ PathState& path_state() {
       check_cuda(cudaStreamCreate(&st.stream));
       check_cuda(cudaMalloc(&st.cublas_workspace, kCublasWorkspace));
       check_cuda(cudaMallocHost(reinterpret_cast<void**>(&st.h_out),
-                                (1 + kMaxBatch) * sizeof(int32_t)));
+                                (kNormScratchAt + 2) * sizeof(int32_t)));
     }
     ready[dev] = true;
   }
@@ -233,50 +297,91 @@ int transformerForwardPaged(cublasHandle_t cublas_handle, __nv_bfloat16* hidden_
   const int32_t* d_rows = st.prefill + kTableStride + num_tokens;
   const int32_t* d_cu_q = st.prefill + kTableStride + 2 * num_tokens;
   const int32_t* d_pos0 = d_cu_q + 2;
-  for (int layer = 0; layer < kLayers; ++layer) {
-    const LayerWeights& lw = weights.layers[layer];
-    rmsNormKernel<<<num_tokens, 1024>>>(hidden_states, buffers.rms_output, lw.input_norm);
-    qProjection(cublas_handle, buffers.rms_output, lw.w_q, buffers.q, num_tokens);
-    kProjection(cublas_handle, buffers.rms_output, lw.w_k, buffers.k, num_tokens);
-    vProjection(cublas_handle, buffers.rms_output, lw.w_v, buffers.v, num_tokens);
-    // RoPE(q), RoPE(k) in place and the page append, in one launch.
-    check_tvp(tvp_rope_append(reinterpret_cast<tvp_bf16*>(cache.k_blocks),
-                              reinterpret_cast<tvp_bf16*>(cache.v_blocks), cache.num_blocks,
-                              kLayers, layer, kKvHeads, d_table, pages, 1, d_rows, d_pos,
-                              num_tokens, reinterpret_cast<tvp_bf16*>(buffers.k),
-                              reinterpret_cast<const tvp_bf16*>(buffers.v),
-                              reinterpret_cast<tvp_bf16*>(buffers.q), kQHeads,
-                              TVP_APPEND_ROPE_K | TVP_APPEND_ROPE_Q | TVP_APPEND_WRITEBACK_K,
-                              st.error, nullptr));
-    if (st.mode == TVP_MODE_FAST) {
-      // Causal attention over the pages just written (no score matrix).
-      check_tvp(tvp_paged_prefill_attention(
-          reinterpret_cast<const tvp_bf16*>(buffers.q),
-          reinterpret_cast<const tvp_bf16*>(cache.k_blocks),
-          reinterpret_cast<const tvp_bf16*>(cache.v_blocks), cache.num_blocks, kLayers, layer,
-          kKvHeads, kQHeads, d_table, pages, d_cu_q, d_pos0, 1, num_tokens, 0.125f,
-          reinterpret_cast<tvp_bf16*>(buffers.attn_output), st.error, nullptr));
-    } else {
-      // COMPAT keeps the reference's own prefill attention (token identity).
-      computeAttentionScores(cublas_handle, buffers.q, buffers.k, buffers.attn_scores, num_tokens);
-      causalMask(buffers.attn_scores, num_tokens);
-      softmaxRows(buffers.attn_scores, kQHeads * num_tokens, num_tokens);
-      attentionScoresTimesV(cublas_handle, buffers.attn_scores, buffers.v, buffers.attn_output,
-                            num_tokens);
+  // The prefill's device work on `stream`; nullptr is the legacy default
+  // stream, where the reference's own op wrappers are called.
+  auto enqueue = [&](cudaStream_t stream) {
+    auto norm = [&](__nv_bfloat16* gain) {
+      rmsNormKernel<<<num_tokens, 1024, 0, stream>>>(hidden_states, buffers.rms_output, gain);
+    };
+    auto residual = [&](__nv_bfloat16* add) {
+      if (stream) residualKernel<<<num_tokens, 1024, 0, stream>>>(hidden_states, add);
+      else residualAdd(hidden_states, add, num_tokens);
+    };
+    for (int layer = 0; layer < kLayers; ++layer) {
+      const LayerWeights& lw = weights.layers[layer];
+      norm(lw.input_norm);
+      qProjection(cublas_handle, buffers.rms_output, lw.w_q, buffers.q, num_tokens);
+      kProjection(cublas_handle, buffers.rms_output, lw.w_k, buffers.k, num_tokens);
+      vProjection(cublas_handle, buffers.rms_output, lw.w_v, buffers.v, num_tokens);
+      // RoPE(q), RoPE(k) in place and the page append, in one launch.
+      check_tvp(tvp_rope_append(reinterpret_cast<tvp_bf16*>(cache.k_blocks),
+                                reinterpret_cast<tvp_bf16*>(cache.v_blocks), cache.num_blocks,
+                                kLayers, layer, kKvHeads, d_table, pages, 1, d_rows, d_pos,
+                                num_tokens, reinterpret_cast<tvp_bf16*>(buffers.k),
+                                reinterpret_cast<const tvp_bf16*>(buffers.v),
+                                reinterpret_cast<tvp_bf16*>(buffers.q), kQHeads,
+                                TVP_APPEND_ROPE_K | TVP_APPEND_ROPE_Q | TVP_APPEND_WRITEBACK_K,
+                                st.error, stream));
+      if (st.mode == TVP_MODE_FAST) {
+        // Causal attention over the pages just written (no score matrix).
+        check_tvp(tvp_paged_prefill_attention(
+            reinterpret_cast<const tvp_bf16*>(buffers.q),
+            reinterpret_cast<const tvp_bf16*>(cache.k_blocks),
+            reinterpret_cast<const tvp_bf16*>(cache.v_blocks), cache.num_blocks, kLayers, layer,
+            kKvHeads, kQHeads, d_table, pages, d_cu_q, d_pos0, 1, num_tokens, 0.125f,
+            reinterpret_cast<tvp_bf16*>(buffers.attn_output), st.error, stream));
+      } else {
+        // COMPAT keeps the reference's own prefill attention (token identity);
+        // it only runs on the legacy stream.
+        computeAttentionScores(cublas_handle, buffers.q, buffers.k, buffers.attn_scores, num_tokens);
+        causalMask(buffers.attn_scores, num_tokens);
+        softmaxRows(buffers.attn_scores, kQHeads * num_tokens, num_tokens);
+        attentionScoresTimesV(cublas_handle, buffers.attn_scores, buffers.v, buffers.attn_output,
+                              num_tokens);
+      }
+      outputProjection(cublas_handle, buffers.attn_output, lw.w_o, buffers.o_output, num_tokens);
+      residual(buffers.o_output);
+      norm(lw.post_attention_norm);
+      gateProjection(cublas_handle, buffers.rms_output, lw.w_gate, buffers.gate, num_tokens);
+      upProjection(cublas_handle, buffers.rms_output, lw.w_up, buffers.up, num_tokens);
+      if (stream) siluKernel<<<num_tokens, 1024, 0, stream>>>(buffers.gate, buffers.up);
+      else silu(buffers.gate, buffers.up, num_tokens);
+      downProjection(cublas_handle, buffers.gate, lw.w_down, buffers.down, num_tokens);
+      residual(buffers.down);
     }
-    outputProjection(cublas_handle, buffers.attn_output, lw.w_o, buffers.o_output, num_tokens);
-    residualAdd(hidden_states, buffers.o_output, num_tokens);
-    rmsNormKernel<<<num_tokens, 1024>>>(hidden_states, buffers.rms_output, lw.post_attention_norm);
-    gateProjection(cublas_handle, buffers.rms_output, lw.w_gate, buffers.gate, num_tokens);
-    upProjection(cublas_handle, buffers.rms_output, lw.w_up, buffers.up, num_tokens);
-    silu(buffers.gate, buffers.up, num_tokens);
-    downProjection(cublas_handle, buffers.gate, lw.w_down, buffers.down, num_tokens);
-    residualAdd(hidden_states, buffers.down, num_tokens);
+    norm(weights.final_norm);
+    lmHeadProjection(cublas_handle, buffers.rms_output + (num_tokens - 1) * kHidden,
+                     weights.embedding, logits);
+  };
+  if (!st.batched) {
+    enqueue(nullptr);
+  } else {
+    // On the path's blocking stream, so ordered after the engine's
+    // legacy-stream work (the embedding gather) and before its argmax below.
+    CublasOnStream on_stream(cublas_handle, st.stream);
+    PathState::PrefillGraph* slot = nullptr;
+    for (auto& e : st.prefill_graphs)
+      if (e.num_tokens == num_tokens) slot = &e;
+    if (!slot) {
+      slot = &st.prefill_graphs[st.prefill_next];
+      st.prefill_next = (st.prefill_next + 1) % PathState::kPrefillGraphs;
+      if (slot->g.exec) cudaGraphExecDestroy(slot->g.exec);
+      *slot = PathState::PrefillGraph{};
+      slot->num_tokens = num_tokens;
+    }
+    const std::vector<const void*> key = {
+        hidden_states, buffers.rms_output, buffers.q, buffers.k, buffers.v, buffers.attn_output,
+        buffers.o_output, buffers.gate, buffers.up, buffers.down, logits, cache.k_blocks,
+        cache.v_blocks, reinterpret_cast<const void*>(static_cast<intptr_t>(cache.num_blocks)),
+        reinterpret_cast<const void*>(static_cast<intptr_t>(pages)), weights.embedding,
+        weights.final_norm, weights.layers[0].w_q, cublas_handle};
+    if (cublasSetWorkspace(cublas_handle, st.cublas_workspace, kCublasWorkspace) !=
+        CUBLAS_STATUS_SUCCESS)
+      throw std::runtime_error("cuBLAS workspace setup failed");
+    run_step_graph(st, slot->g, key, cublas_handle, enqueue);
   }
+  check_cuda(cudaGetLastError());
   sequence.current_seq_len += num_tokens;
-  rmsNormKernel<<<num_tokens, 1024>>>(hidden_states, buffers.rms_output, weights.final_norm);
-  lmHeadProjection(cublas_handle, buffers.rms_output + (num_tokens - 1) * kHidden,
-                   weights.embedding, logits);
   const int token = argmaxLogits(logits);
   raise_device_errors(st);
   return token;
@@ -403,7 +508,7 @@ std::vector<int> decodeBatchPaged(cublasHandle_t cublas_handle, __nv_bfloat16* h
             reinterpret_cast<const tvp_bf16*>(in), batch, in_dim,
             reinterpret_cast<const tvp_bf16*>(w), reinterpret_cast<tvp_bf16*>(hidden_states),
             reinterpret_cast<const tvp_bf16*>(gain), reinterpret_cast<tvp_bf16*>(buffers.rms_output),
-            st.norm_counter, stream));
+            st.norm_scratch, stream));
       };
       if (st.native_proj) {
         residual_norm(buffers.attn_output, kHidden, lw.w_o, lw.post_attention_norm);
@@ -462,62 +567,23 @@ std::vector<int> decodeBatchPaged(cublasHandle_t cublas_handle, __nv_bfloat16* h
       tokens.push_back(argmaxLogits(logits + static_cast<size_t>(row) * VOCAB_SIZE));
     raise_device_errors(st);
   } else {
-    // cuBLAS works on the step's stream while this call runs; the caller's
-    // stream (and with it cuBLAS's default workspace) is restored on return.
-    cudaStream_t caller_stream = nullptr;
-    if (cublasGetStream(cublas_handle, &caller_stream) != CUBLAS_STATUS_SUCCESS ||
-        cublasSetStream(cublas_handle, st.stream) != CUBLAS_STATUS_SUCCESS)
-      throw std::runtime_error("cuBLAS stream setup failed");
-    struct RestoreStream {
-      cublasHandle_t handle;
-      cudaStream_t stream;
-      ~RestoreStream() { cublasSetStream(handle, stream); }
-    } restore{cublas_handle, caller_stream};
+    CublasOnStream on_stream(cublas_handle, st.stream);
     PathState::StepGraph& g = st.graphs[batch];
     const std::vector<const void*> key = {
         hidden_states, buffers.rms_output, buffers.q, buffers.k, buffers.v, buffers.attn_output,
         buffers.o_output, buffers.gate, buffers.up, buffers.down, logits, cache.k_blocks,
         cache.v_blocks, reinterpret_cast<const void*>(static_cast<intptr_t>(cache.num_blocks)),
         weights.embedding, weights.final_norm, weights.layers[0].w_q, cublas_handle};
-    if (g.exec && g.key == key) {
-      check_cuda(cudaGraphLaunch(g.exec, st.stream));
-    } else if (g.warm && g.key == key) {
-      // Second step on these buffers: record it once, then replay it.
-      if (cublasSetWorkspace(cublas_handle, st.cublas_workspace, kCublasWorkspace) !=
-          CUBLAS_STATUS_SUCCESS)
-        throw std::runtime_error("cuBLAS workspace setup failed");
-      check_cuda(cudaStreamBeginCapture(st.stream, cudaStreamCaptureModeThreadLocal));
-      cudaGraph_t graph = nullptr;
-      try {
-        enqueue(st.stream);
-      } catch (...) {
-        cudaStreamEndCapture(st.stream, &graph);
-        if (graph) cudaGraphDestroy(graph);
-        throw;
-      }
-      check_cuda(cudaStreamEndCapture(st.stream, &graph));
-      cudaGraphExec_t exec = nullptr;
-      const cudaError_t made = cudaGraphInstantiate(&exec, graph, 0);
-      cudaGraphDestroy(graph);
-      check_cuda(made);
-      if (g.exec) cudaGraphExecDestroy(g.exec);
-      g.exec = exec;
-      check_cuda(cudaGraphLaunch(g.exec, st.stream));
-    } else {
-      // First step on these buffers: eager, which also loads every kernel.
-      if (g.exec) cudaGraphExecDestroy(g.exec);
-      g.exec = nullptr;
-      enqueue(st.stream);
-      g.key = key;
-      g.warm = true;
-    }
-    check_cuda(cudaMemcpyAsync(st.h_out, st.error, (1 + batch) * sizeof(int32_t),
+    run_step_graph(st, g, key, cublas_handle, enqueue);
+    check_cuda(cudaMemcpyAsync(st.h_out, st.error, (kNormScratchAt + 2) * sizeof(int32_t),
                                cudaMemcpyDeviceToHost, st.stream));
     check_cuda(cudaStreamSynchronize(st.stream));
-    if (st.h_out[0]) {
+    if (st.h_out[0] || st.h_out[kNormScratchAt + 1]) {
+      const int32_t bits = st.h_out[0] | st.h_out[kNormScratchAt + 1];
       check_cuda(cudaMemset(st.error, 0, sizeof(int32_t)));
+      check_cuda(cudaMemset(st.error + kNormScratchAt + 1, 0, sizeof(int32_t)));
       throw std::runtime_error("paged-KV kernels reported device error bits " +
-                               std::to_string(st.h_out[0]));
+                               std::to_string(bits));
     }
     tokens.assign(st.h_out + 1, st.h_out + 1 + batch);
   }

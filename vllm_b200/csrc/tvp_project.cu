@@ -61,11 +61,17 @@ struct ProjParams {
   int n[TVP_PROJ_MAX];
   int cta_end[TVP_PROJ_MAX];  // prefix sums of n / 16 (one matrix per CTA)
   int count, rows, k, epilogue;
-  // Residual epilogue followed by the next RMSNorm (norm_out != nullptr): the
-  // last CTA to finish writes norm_out = rmsnorm(out[0]) x norm_gain.
+  // Residual epilogue followed by the next RMSNorm (norm_out != nullptr):
+  // norm_out = rmsnorm(out[0]) x norm_gain.  With norm_spread, every CTA
+  // publishes the sum-of-squares subtree of its rows (norm_part), waits for
+  // all CTAs of the grid at the arrival counter and normalises its own
+  // outputs; otherwise the last CTA to finish normalises all of them.
   const __nv_bfloat16* norm_gain;
   __nv_bfloat16* norm_out;
   int* counter;
+  float* norm_part;   // [8][128]: one subtree sum per (row, CTA)
+  int32_t* norm_err;  // TVP_DEVERR_TIMEOUT when a CTA gave up waiting for the others
+  int norm_spread;
   // kEpiRopeAppend: matrix 0 = q, 1 = k, 2 = v of one token per row; q is
   // stored rotated into out[0], k rotated and v as is into their page slots.
   __nv_bfloat16* k_pool;
@@ -186,6 +192,12 @@ __device__ __forceinline__ uint4 ld_coherent_v4(const void* p) {
   return r;
 }
 
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Epilogue of the Q/K/V projection of one decode token per row, fused with
 // RoPE and the page append (K1's work, tvp_append.cu): thread (r, ln) of the
 // first 128 holds the FP32 sum of MMA row (ln / 4) + 8 (r / 2) for token
@@ -270,7 +282,12 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
   // h 64 + 8 u + g and + 32 (group = 4 h + u), the two halves of one
   // rotate-half pair, so that both halves of every pair meet in this CTA.
   const bool pair_rows = kMats == 1 && p.epilogue == kEpiRopeAppend && mat < 2;
-  const int row0 = pair_rows ? (group >> 2) * kHeadDim + (group & 3) * 8 : group * kProjRows;
+  // With the spread RMSNorm, CTA a takes rows 8 a + g and 1024 + 8 a + g:
+  // the two features of the norm's leaves 8 a .. 8 a + 7.
+  const bool leaf_rows = kMats == 1 && p.norm_out != nullptr && p.norm_spread;
+  const int row0 = pair_rows   ? (group >> 2) * kHeadDim + (group & 3) * 8
+                   : leaf_rows ? group * 8
+                               : group * kProjRows;
   const size_t k0 = (size_t)(row0 + g) * p.k + warp * slice + 8 * q;
   const __nv_bfloat16* wa[kMats];
   wa[0] = w0 + k0;
@@ -282,7 +299,7 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
 #pragma unroll
   for (int m = 0; m < kMats; ++m) c[m][0] = c[m][1] = c[m][2] = c[m][3] = 0.f;
   const int blocks = slice / kProjBlock;
-  const size_t row8 = (size_t)(pair_rows ? kHeadDim / 2 : 8) * p.k;
+  const size_t row8 = (size_t)(pair_rows ? kHeadDim / 2 : leaf_rows ? kHidden / 2 : 8) * p.k;
   // The next launch in the stream may start now; it reads nothing this grid
   // writes before its own wait below.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -341,8 +358,10 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
     rope_append_epilogue(p, s[0], mat, group, r, ln, t);
     return;
   }
+  float h = 0.f;  // the residual epilogue's new hidden value
+  const int row = leaf_rows ? group * 8 + (ln >> 2) + ((r & 2) ? kHidden / 2 : 0)
+                            : group * kProjRows + (ln >> 2) + ((r & 2) ? 8 : 0);
   if (threadIdx.x < 128) {
-    const int row = group * kProjRows + (ln >> 2) + ((r & 2) ? 8 : 0);
     if (t < p.rows) {
       const size_t idx = (size_t)t * n_out + row;
       __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(out);
@@ -354,13 +373,72 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
       } else if (p.epilogue == TVP_PROJ_F32) {
         static_cast<float*>(out)[idx] = s[0];
       } else if (p.epilogue == TVP_PROJ_RESIDUAL) {
-        ob[idx] = ob[idx] + __float2bfloat16_rn(s[0]);  // residualKernel's BF16 add
+        const __nv_bfloat16 hb = ob[idx] + __float2bfloat16_rn(s[0]);  // residualKernel's BF16 add
+        ob[idx] = hb;
+        h = __bfloat162float(hb);
       } else {
         ob[idx] = __float2bfloat16_rn(s[0]);
       }
     }
   }
-  if (kMats == 1 && p.norm_out != nullptr) {
+  if (leaf_rows) {
+    // The reference's sum of squares is a tree over leaves x[i]^2 + x[i +
+    // 1024]^2; this CTA holds both features of leaves 8 a .. 8 a + 7, a whole
+    // subtree.  Its sum per row goes to norm_part; after every CTA's has
+    // arrived, each CTA sums the 128 subtrees by the tree's upper levels
+    // (the same order as the reference, so the same r) and normalises its
+    // own 16 features.  The CTAs of the grid wait for one another: the host
+    // uses this form only when they all fit on the device at once, and the
+    // wait is bounded.
+    __shared__ float hv[4][32];
+    __shared__ float r_rows[kProjMaxTokens];
+    __shared__ int arrived;
+    if (threadIdx.x < 128) hv[r][ln] = h;
+    __syncthreads();
+    if (threadIdx.x < 64) {  // r < 2: leaf ln / 4 of row t
+      float v = norm_leaf(hv[r][ln], hv[r + 2][ln]);
+      float o = __shfl_down_sync(0xffffffffu, v, 4);
+      if (((ln >> 2) & 1) == 0) v = __fadd_rn(v, o);
+      o = __shfl_down_sync(0xffffffffu, v, 8);
+      if (((ln >> 2) & 3) == 0) v = __fadd_rn(v, o);
+      o = __shfl_down_sync(0xffffffffu, v, 16);
+      if ((ln >> 2) == 0) v = __fadd_rn(v, o);
+      if ((ln >> 2) == 0 && t < p.rows) p.norm_part[t * (kHidden / 16) + group] = v;
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      // The counter grows by gridDim.x per launch: this launch is complete
+      // when it reaches the next multiple.
+      unsigned* ctr = reinterpret_cast<unsigned*>(p.counter);
+      const unsigned old = atomicAdd(ctr, 1u);
+      const unsigned target = (old / gridDim.x + 1u) * gridDim.x;
+      bool done = (int)(ld_acquire_u32(ctr) - target) >= 0;
+      const unsigned long long start = global_timer_ns();
+      while (!done) {
+        for (int i = 0; i < 32 && !done; ++i) done = (int)(ld_acquire_u32(ctr) - target) >= 0;
+        if (!done && elapsed_ns(start) > (long long)kWaitLimitNs) break;
+      }
+      if (!done) record_error(p.norm_err, TVP_DEVERR_TIMEOUT);
+      arrived = done;
+    }
+    __syncthreads();
+    if (!arrived) return;
+    if (warp < p.rows) {  // row `warp`: subtrees 4 lane .. 4 lane + 3, then across lanes
+      const float4 v4 = __ldcg(reinterpret_cast<const float4*>(p.norm_part + warp * (kHidden / 16)) + lane);
+      float v = __fadd_rn(__fadd_rn(v4.x, v4.y), __fadd_rn(v4.z, v4.w));
+#pragma unroll
+      for (int off = 1; off < 32; off *= 2) {
+        const float o = __shfl_down_sync(0xffffffffu, v, off);
+        if ((lane & (2 * off - 1)) == 0) v = __fadd_rn(v, o);
+      }
+      if (lane == 0) r_rows[warp] = (float)sqrt((double)v / 2048.0 + 1.0e-5);
+    }
+    __syncthreads();
+    if (threadIdx.x < 128 && t < p.rows)
+      p.norm_out[(size_t)t * kHidden + row] = __float2bfloat16_rn(
+          __fmul_rn(__fdiv_rn(h, r_rows[t]), __bfloat162float(p.norm_gain[row])));
+  } else if (kMats == 1 && p.norm_out != nullptr) {
     // The last CTA to finish normalises the rows: every CTA releases its row
     // stores and counts itself done; the last one acquires them all.
     __shared__ int is_last;
@@ -410,6 +488,29 @@ inline bool overlaps(const void* a, size_t na, const void* b, size_t nb) {
   return x < y + nb && y < x + na;
 }
 
+// Whether every CTA of a `ctas`-CTA residual+RMSNorm launch of width k can be
+// resident at once on the current device (per device, cached), so that they
+// may wait for one another.
+int norm_spread_fits(int k, int ctas, int* fits) {
+  static int cache[64][2] = {};  // 0 unknown, 1 no, 2 yes; [device][16-warp form]
+  const bool wide = k > 4096 && k % 512 == 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return TVP_ERR_RUNTIME;
+  if (dev >= 0 && dev < 64 && cache[dev][wide]) {
+    *fits = cache[dev][wide] == 2;
+    return TVP_OK;
+  }
+  int sms = 0, per_sm = 0;
+  if (tvp_device_sm_count(&sms) != TVP_OK ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+          &per_sm, wide ? decode_projection_kernel<16, 1, 8> : decode_projection_kernel<8, 1, 8>,
+          wide ? 16 * 32 : 8 * 32, 0) != cudaSuccess)
+    return TVP_ERR_RUNTIME;
+  *fits = (long long)sms * per_sm >= ctas;
+  if (dev >= 0 && dev < 64) cache[dev][wide] = *fits ? 2 : 1;
+  return TVP_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -451,16 +552,19 @@ int tvp_decode_projections(const tvp_bf16* x, int rows, int k, int count, const 
 
 int tvp_decode_projection_residual_rmsnorm(const tvp_bf16* x, int rows, int k, const tvp_bf16* w,
                                            tvp_bf16* hidden, const tvp_bf16* norm_gain,
-                                           tvp_bf16* norm_out, int32_t* d_counter,
+                                           tvp_bf16* norm_out, void* d_scratch,
                                            tvp_stream_t stream) {
-  if (!x || !w || !hidden || !norm_gain || !norm_out || !d_counter || rows < 1 ||
+  if (!x || !w || !hidden || !norm_gain || !norm_out || !d_scratch || rows < 1 ||
       rows > kProjMaxTokens || k < 256 || k % 256 != 0 || !aligned16(x) || !aligned16(w) ||
-      !aligned16(hidden) || !aligned16(norm_gain) || !aligned16(norm_out) ||
-      (reinterpret_cast<uintptr_t>(d_counter) & 3u))
+      !aligned16(hidden) || !aligned16(norm_gain) || !aligned16(norm_out) || !aligned16(d_scratch))
     return TVP_ERR_INVALID_ARGUMENT;
   const size_t xb = (size_t)rows * k * 2, hb = (size_t)rows * kHidden * 2;
   if (overlaps(hidden, hb, x, xb) || overlaps(norm_out, hb, x, xb) ||
-      overlaps(norm_out, hb, hidden, hb) || overlaps(norm_out, hb, norm_gain, kHidden * 2))
+      overlaps(norm_out, hb, hidden, hb) || overlaps(norm_out, hb, norm_gain, kHidden * 2) ||
+      overlaps(d_scratch, TVP_NORM_SCRATCH_BYTES, x, xb) ||
+      overlaps(d_scratch, TVP_NORM_SCRATCH_BYTES, hidden, hb) ||
+      overlaps(d_scratch, TVP_NORM_SCRATCH_BYTES, norm_out, hb) ||
+      overlaps(d_scratch, TVP_NORM_SCRATCH_BYTES, norm_gain, kHidden * 2))
     return TVP_ERR_INVALID_ARGUMENT;
   ProjParams p{};
   p.x = reinterpret_cast<const __nv_bfloat16*>(x);
@@ -474,7 +578,15 @@ int tvp_decode_projection_residual_rmsnorm(const tvp_bf16* x, int rows, int k, c
   p.cta_end[0] = kHidden / kProjRows;
   p.norm_gain = reinterpret_cast<const __nv_bfloat16*>(norm_gain);
   p.norm_out = reinterpret_cast<__nv_bfloat16*>(norm_out);
-  p.counter = reinterpret_cast<int*>(d_counter);
+  uint8_t* scratch = static_cast<uint8_t*>(d_scratch);
+  p.counter = reinterpret_cast<int*>(scratch);
+  p.norm_err = reinterpret_cast<int32_t*>(scratch + 4);
+  p.norm_part = reinterpret_cast<float*>(scratch + 256);
+  // The spread form's CTAs wait for one another: only when the device holds
+  // the whole grid at once (148 SMs for 128 CTAs on a B200).
+  int spread = 0;
+  if (norm_spread_fits(k, kHidden / kProjRows, &spread) != TVP_OK) return TVP_ERR_RUNTIME;
+  p.norm_spread = spread;
   return launch_projection(p, kHidden / kProjRows, false, static_cast<cudaStream_t>(stream));
 }
 

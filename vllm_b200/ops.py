@@ -291,12 +291,22 @@ def decode_projections(x, weights, outs=None, epilogue="bf16", stream=None):
     return outs
 
 
-def decode_projection_residual_rmsnorm(x, w, hidden, norm_gain, norm_out, counter, stream=None):
+NORM_SCRATCH_BYTES = 4352  # TVP_NORM_SCRATCH_BYTES
+
+
+def norm_scratch(device):
+    """Device scratch for decode_projection_residual_rmsnorm, zeroed: the
+    launch's arrival counter, its error word and the rows' subtree sums."""
+    return torch.zeros(NORM_SCRATCH_BYTES // 4, dtype=torch.int32, device=device)
+
+
+def decode_projection_residual_rmsnorm(x, w, hidden, norm_gain, norm_out, scratch, stream=None):
     """hidden += bf16(w @ x) (the residual epilogue), then in the same launch
     norm_out = rmsnorm(hidden) * norm_gain with the reference kernel's
     arithmetic.  x: BF16 [rows, k]; w: BF16 [2048, k]; hidden, norm_out: BF16
-    [rows, 2048]; norm_gain: BF16 [2048]; counter: a zeroed int32 tensor of one
-    element, reused by every call (zeroed again by each launch)."""
+    [rows, 2048]; norm_gain: BF16 [2048]; scratch: from norm_scratch(), reused
+    by every call (its element 1 is the error word: TVP_DEVERR_TIMEOUT if the
+    launch's CTAs gave up waiting for one another)."""
     lib = N.load()
     dev = x.device
     _need(x, "x", torch.bfloat16, dev)
@@ -304,13 +314,15 @@ def decode_projection_residual_rmsnorm(x, w, hidden, norm_gain, norm_out, counte
     _need(hidden, "hidden", torch.bfloat16, dev)
     _need(norm_gain, "norm_gain", torch.bfloat16, dev)
     _need(norm_out, "norm_out", torch.bfloat16, dev)
-    _need(counter, "counter", torch.int32, dev)
+    _need(scratch, "scratch", torch.int32, dev)
+    if scratch.numel() * 4 < NORM_SCRATCH_BYTES:
+        raise ValueError(f"scratch must hold {NORM_SCRATCH_BYTES} bytes (norm_scratch())")
     rows, k = x.shape
     if w.shape != (2048, k) or hidden.shape != (rows, 2048) or norm_out.shape != (rows, 2048) \
             or norm_gain.numel() != 2048:
         raise ValueError("shapes: x [rows, k], w [2048, k], hidden/norm_out [rows, 2048], gain [2048]")
     rc = lib.tvp_decode_projection_residual_rmsnorm(_ptr(x), rows, k, _ptr(w), _ptr(hidden),
-                                                    _ptr(norm_gain), _ptr(norm_out), _ptr(counter),
+                                                    _ptr(norm_gain), _ptr(norm_out), _ptr(scratch),
                                                     _stream(stream))
     N.check(rc, "tvp_decode_projection_residual_rmsnorm")
     return hidden, norm_out
