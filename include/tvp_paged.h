@@ -295,6 +295,27 @@ int tvp_decode_qkv_rope_append(const tvp_bf16* x, int rows, int k, const tvp_bf1
                                const int32_t* d_positions, int32_t* d_error, tvp_stream_t stream);
 
 /*
+ * tvp_decode_projection_residual_rmsnorm of the down projection followed by
+ * tvp_decode_qkv_rope_append of the next layer, in one launch: the argument
+ * groups are theirs (x, rows, k, w_down, hidden, norm_gain, norm_out,
+ * d_scratch for the first; w_q, w_k, w_v, q_out, pools, layer, tables,
+ * positions, d_error for the second, whose x is norm_out).  Every output has
+ * the bits of the two launches.  After the grid-wide arrival of the norm
+ * each CTA normalises all rows into shared memory, and its two halves of 8
+ * warps run one Q/K/V item each, with weights loaded before the arrival.  k
+ * a multiple of 512 above 4096 (the down projection's 8192), and a device
+ * that holds all 128 CTAs of 16 warps at once (the spread norm); otherwise
+ * TVP_ERR_UNSUPPORTED, and the caller makes the two launches.
+ */
+int tvp_decode_down_norm_qkv(const tvp_bf16* x, int rows, int k, const tvp_bf16* w_down,
+                             tvp_bf16* hidden, const tvp_bf16* norm_gain, tvp_bf16* norm_out,
+                             void* d_scratch, const tvp_bf16* w_q, const tvp_bf16* w_k,
+                             const tvp_bf16* w_v, tvp_bf16* q_out, tvp_bf16* k_pool,
+                             tvp_bf16* v_pool, int num_pages, int num_layers, int layer,
+                             const int32_t* d_block_tables, int table_stride,
+                             const int32_t* d_positions, int32_t* d_error, tvp_stream_t stream);
+
+/*
  * K2 without any allocation.  This entry point has no counterpart in the
  * reference.  It is for callers that cannot call cudaMalloc: code whose
  * device memory is owned by a host framework's pool, plug-ins running under a

@@ -226,3 +226,25 @@ def test_fused_projection_forms_reject_bad_arguments_on_host(native):
     assert g(*args[:1], 0, *args[2:]) == N.TVP_ERR_INVALID_ARGUMENT     # no rows
     assert g(*args[:13], 0, *args[14:]) == N.TVP_ERR_INVALID_ARGUMENT   # table stride
     assert g(*args[:3], odd, *args[4:]) == N.TVP_ERR_INVALID_ARGUMENT   # weight alignment
+
+
+def test_down_norm_qkv_rejects_bad_arguments_on_host(native):
+    f = native.tvp_decode_down_norm_qkv
+    v = ctypes.c_void_p
+    x, wd, hid, gain, out, scr = v(0x100000), v(0x200000), v(0x300000), v(0x400000), v(0x500000), v(0x600000)
+    wq, wk, wv, q, kp, vp, tab, pos = (v(0x700000), v(0x800000), v(0x900000), v(0xa00000),
+                                       v(0xb00000), v(0xc00000), v(0xd00000), v(0xe00000))
+    ok = [x, 4, 8192, wd, hid, gain, out, scr, wq, wk, wv, q, kp, vp, 8, 16, 0, tab, 64, pos, None, None]
+
+    def call(**kw):
+        args = list(ok)
+        for i, val in kw.items():
+            args[int(i[1:])] = val
+        return f(*args)
+    assert call(a0=None) == N.TVP_ERR_INVALID_ARGUMENT              # no x
+    assert call(a1=9) == N.TVP_ERR_INVALID_ARGUMENT                 # rows 1..8
+    assert call(a7=None) == N.TVP_ERR_INVALID_ARGUMENT              # no scratch
+    assert call(a6=hid) == N.TVP_ERR_INVALID_ARGUMENT               # norm_out on hidden
+    assert call(a11=None) == N.TVP_ERR_INVALID_ARGUMENT             # no q_out
+    assert call(a16=16) == N.TVP_ERR_INVALID_ARGUMENT               # layer out of range
+    assert call(a11=v(0x500000)) == N.TVP_ERR_INVALID_ARGUMENT      # q_out on norm_out

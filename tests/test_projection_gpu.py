@@ -252,6 +252,47 @@ def test_qkv_rope_append_form_equals_projections_then_rope_append(rows):
     assert torch.equal(vp, vp_want)
 
 
+@pytest.mark.parametrize("rows", [1, 4, 8])
+def test_down_norm_qkv_is_the_two_launches_it_replaces(rows):
+    """tvp_decode_down_norm_qkv: the down projection with its residual add and
+    spread RMSNorm, then the next layer's Q/K/V with RoPE and the page append,
+    in one launch: hidden, norm_out, q and every page equal, bit for bit, what
+    decode_projection_residual_rmsnorm then decode_qkv_rope_append produce;
+    twice on one scratch."""
+    g = torch.Generator(device="cuda").manual_seed(300 + rows)
+    x = torch.randn(rows, 8192, generator=g, device="cuda").to(torch.bfloat16)
+    w_down = (torch.randn(2048, 8192, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    _, (wq, wk, wv) = make(rows, 2048, [2048, 512, 512], seed=310 + rows)
+    hidden0 = (torch.randn(rows, 2048, generator=g, device="cuda") * 3).to(torch.bfloat16)
+    gain = (1 + 0.1 * torch.randn(2048, generator=g, device="cuda")).to(torch.bfloat16)
+    kp0, vp0, tables, pos = _pools_and_tables(rows, 17 + rows)
+    layer = 2
+    err = ops.new_error_word("cuda")
+    # the two launches
+    h_want = hidden0.clone()
+    n_want = torch.empty_like(h_want)
+    ops.decode_projection_residual_rmsnorm(x, w_down, h_want, gain, n_want, ops.norm_scratch("cuda"))
+    kp_want, vp_want = kp0.clone(), vp0.clone()
+    q_want = torch.empty(rows, 2048, dtype=torch.bfloat16, device="cuda")
+    ops.decode_qkv_rope_append(n_want, wq, wk, wv, q_want, kp_want, vp_want, layer, tables, pos,
+                               error=err)
+    scratch = ops.norm_scratch("cuda")
+    for _ in range(2):
+        h_got = hidden0.clone()
+        n_got = torch.full_like(h_got, float("nan"))
+        kp, vp = kp0.clone(), vp0.clone()
+        q_got = torch.full_like(q_want, float("nan"))
+        ops.decode_down_norm_qkv(x, w_down, h_got, gain, n_got, scratch, wq, wk, wv, q_got, kp, vp,
+                                 layer, tables, pos, error=err)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0 and int(scratch[1].item()) == 0
+        assert torch.equal(h_got, h_want)
+        assert torch.equal(n_got, n_want)
+        assert torch.equal(q_got, q_want)
+        assert torch.equal(kp, kp_want)
+        assert torch.equal(vp, vp_want)
+
+
 def test_qkv_rope_append_reports_a_bad_page_and_skips_it():
     x, (wq, wk, wv) = make(2, 2048, [2048, 512, 512], seed=140)
     kp, vp, tables, pos = _pools_and_tables(2, 11)

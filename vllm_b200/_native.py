@@ -84,6 +84,10 @@ _SIGNATURES = {
     "tvp_decode_qkv_rope_append": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                            c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                            c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
+    "tvp_decode_down_norm_qkv": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                         c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                         c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "tvp_head_gather_create": (c_int, [c_int, c_int, c_int, c_int, POINTER(c_void_p)]),
     "tvp_head_gather_export": (c_int, [c_void_p, c_void_p]),
     "tvp_head_gather_connect": (c_int, [c_void_p, c_void_p]),

@@ -39,8 +39,10 @@
 //                     append in one launch (tvp_decode_qkv_rope_append); O
 //                     with the residual add and the post-attention RMSNorm
 //                     (tvp_decode_projection_residual_rmsnorm); gate and up
-//                     with silu in their epilogue; down with the residual add
-//                     and the next layer's RMSNorm.  Five launches per layer.
+//                     with silu in their epilogue; down with the residual add,
+//                     the next layer's RMSNorm and that layer's Q, K, V,
+//                     RoPE and page append (tvp_decode_down_norm_qkv).  Four
+//                     launches per layer with the attention.
 //                     The same operands and FP32 accumulation in another
 //                     summation order (the fused residual, silu, RoPE and
 //                     RMSNorm keep the reference's rounding points bit for
@@ -467,13 +469,16 @@ std::vector<int> decodeBatchPaged(cublasHandle_t cublas_handle, __nv_bfloat16* h
     };
     check_tvp(tvp_decode_plan(d_len, batch, kTableStride, kKvHeads, 0, st.workspace,
                               st.workspace_bytes, st.error, stream));
+    bool qkv_done = false;  // native: this layer's Q/K/V ran in the previous layer's down launch
     for (int layer = 0; layer < kLayers; ++layer) {
       const LayerWeights& lw = weights.layers[layer];
-      // native: every RMSNorm but the first runs in the last CTA of the
-      // residual projection before it (tvp_decode_projection_residual_rmsnorm)
+      // native: every RMSNorm but the first runs in the residual projection
+      // before it (tvp_decode_projection_residual_rmsnorm)
       if (!st.native_proj || layer == 0)
         rmsNormKernel<<<batch, 1024, 0, stream>>>(hidden_states, buffers.rms_output, lw.input_norm);
-      if (st.native_proj) {
+      if (st.native_proj && qkv_done) {
+        qkv_done = false;
+      } else if (st.native_proj) {
         // Q, K, V, RoPE and the page append in one launch
         check_tvp(tvp_decode_qkv_rope_append(
             reinterpret_cast<const tvp_bf16*>(buffers.rms_output), batch, kHidden,
@@ -528,6 +533,25 @@ std::vector<int> decodeBatchPaged(cublasHandle_t cublas_handle, __nv_bfloat16* h
         else silu(buffers.gate, buffers.up, batch);
       }
       if (st.native_proj) {  // hidden += down, then the next RMSNorm (the final one last)
+        // with the next layer's Q, K, V, RoPE and page append in the same launch
+        if (layer + 1 < kLayers) {
+          const LayerWeights& nw = weights.layers[layer + 1];
+          const int rc = tvp_decode_down_norm_qkv(
+              reinterpret_cast<const tvp_bf16*>(buffers.gate), batch, 8192,
+              reinterpret_cast<const tvp_bf16*>(lw.w_down), reinterpret_cast<tvp_bf16*>(hidden_states),
+              reinterpret_cast<const tvp_bf16*>(nw.input_norm),
+              reinterpret_cast<tvp_bf16*>(buffers.rms_output), st.norm_scratch,
+              reinterpret_cast<const tvp_bf16*>(nw.w_q), reinterpret_cast<const tvp_bf16*>(nw.w_k),
+              reinterpret_cast<const tvp_bf16*>(nw.w_v), reinterpret_cast<tvp_bf16*>(buffers.q),
+              reinterpret_cast<tvp_bf16*>(cache.k_blocks),
+              reinterpret_cast<tvp_bf16*>(cache.v_blocks), cache.num_blocks, kLayers, layer + 1,
+              d_tables, kTableStride, d_pos, st.error, stream);
+          if (rc != TVP_ERR_UNSUPPORTED) {
+            check_tvp(rc);
+            qkv_done = true;
+            continue;
+          }
+        }
         residual_norm(buffers.gate, 8192, lw.w_down,
                       layer + 1 < kLayers ? weights.layers[layer + 1].input_norm : weights.final_norm);
       } else {

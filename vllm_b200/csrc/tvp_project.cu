@@ -208,13 +208,17 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
 // of page tables[t][pos / 16] of the layer's pools.  Threads with
 // (r & 2) == 0 and ln < 4 hold MMA row 0 for each of the 8 token rows: they
 // report a row's bad position or page once.
+// `tid` is the thread's index in the group of threads that runs the epilogue
+// (a whole CTA, or half of one), `half` that group's exchange buffer and
+// `sync` its barrier.
+template <typename Sync>
 __device__ __forceinline__ void rope_append_epilogue(const ProjParams& p, float sum, int mat,
-                                                     int group, int r, int ln, int t) {
-  __shared__ float half[4][32];
+                                                     int group, int r, int ln, int t, int tid,
+                                                     float (*half)[32], Sync sync) {
   const float own = __bfloat162float(__float2bfloat16_rn(sum));
-  if (threadIdx.x < 128) half[r][ln] = own;
-  __syncthreads();
-  if (threadIdx.x >= 128 || t >= p.rows) return;
+  if (tid < 128) half[r][ln] = own;
+  sync();
+  if (tid >= 128 || t >= p.rows) return;
   const int pos = __ldg(p.pos + t);
   if (pos < 0 || pos / kPage >= p.table_stride) {
     if (mat == 0 && (r & 2) == 0 && (ln >> 2) == 0) record_error(p.err, TVP_DEVERR_BAD_TOKEN);
@@ -355,7 +359,9 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
   }
   const int t = 2 * (ln & 3) + (r & 1);
   if (kMats == 1 && p.epilogue == kEpiRopeAppend) {
-    rope_append_epilogue(p, s[0], mat, group, r, ln, t);
+    __shared__ float rope_half[4][32];
+    rope_append_epilogue(p, s[0], mat, group, r, ln, t, threadIdx.x, rope_half,
+                         [] { __syncthreads(); });
     return;
   }
   float h = 0.f;  // the residual epilogue's new hidden value
@@ -454,6 +460,208 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
   }
 }
 
+// Down projection + residual + spread RMSNorm, then the next layer's Q, K and
+// V projections with RoPE and the page append, in one launch of 128 CTAs x 16
+// warps.  The down part is decode_projection_kernel<16, 1, 8> with the spread
+// norm, instruction for instruction.  Then, instead of ending:
+//  * each CTA's two halves of 8 warps take one Q/K/V item each (items c and
+//    128 + c: all 128 q items, and the 64 k and v items on CTAs 0..63), and
+//    issue that item's weight loads (its whole k-slice, 8 blocks per lane)
+//    right after the down loop, so they fly during the residual epilogue and
+//    the grid-wide arrival;
+//  * after the arrival every CTA has r for every row, and the hidden rows are
+//    final: it normalises all 2048 features of every row into shared memory
+//    (the norm's own arithmetic, so the same bits as norm_out), and writes its
+//    own 16 features to norm_out as the plain form does;
+//  * each half then runs the Q/K/V item exactly as decode_projection_kernel<8,
+//    1, 8> does (same k-slices and order, x read from shared memory), with
+//    the RoPE + page-append epilogue under its own named barrier.
+// So every output has the bits of the two launches it replaces.
+constexpr int kXnRow = kHidden + 32;  // normalised row stride in shared memory (conflict-free reads)
+
+__global__ void __launch_bounds__(512, 1)
+    down_norm_qkv_kernel(const ProjParams pd, const ProjParams pq) {
+  constexpr int kWarps = 16, kUnroll = 8;
+  extern __shared__ __align__(16) __nv_bfloat16 xn[];  // [rows][kXnRow]
+  __shared__ float red[kWarps][4][32];
+  __shared__ float hv[4][32];
+  __shared__ float r_rows[kProjMaxTokens];
+  __shared__ float rope_half[2][4][32];
+  __shared__ int arrived;
+  const int group = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int r = warp & 3, ln = lane;
+  const int t = 2 * (ln & 3) + (r & 1);
+
+  // ---- down: rows 8a + g and 1024 + 8a + g of w_down (the norm's leaves)
+  const int slice = pd.k / kWarps;
+  const size_t k0 = (size_t)(group * 8 + g) * pd.k + warp * slice + 8 * q;
+  const __nv_bfloat16* wa = pd.w[0] + k0;
+  const size_t row8 = (size_t)(kHidden / 2) * pd.k;
+  const bool has_x = g < pd.rows;
+  const __nv_bfloat16* xr = pd.x + (size_t)(has_x ? g : 0) * pd.k + warp * slice + 8 * q;
+  float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
+  const int blocks = slice / kProjBlock;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  for (int b0 = 0; b0 < blocks; b0 += kUnroll) {
+    uint4 va[kUnroll], vb[kUnroll], vx[kUnroll];
+#pragma unroll
+    for (int i = 0; i < kUnroll; ++i) {
+      if (b0 + i < blocks) {
+        const int off = (b0 + i) * kProjBlock;
+        va[i] = ld_stream_v4(wa + off);
+        vb[i] = ld_stream_v4(wa + row8 + off);
+      }
+    }
+    if (b0 == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < kUnroll; ++i)
+      if (b0 + i < blocks)
+        vx[i] = has_x ? ld_coherent_v4(xr + (b0 + i) * kProjBlock) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int i = 0; i < kUnroll; ++i) {
+      if (b0 + i < blocks) {
+        mma_bf16_16816(c0, c1, c2, c3, va[i].x, vb[i].x, va[i].y, vb[i].y, vx[i].x, vx[i].y);
+        mma_bf16_16816(c0, c1, c2, c3, va[i].z, vb[i].z, va[i].w, vb[i].w, vx[i].z, vx[i].w);
+      }
+    }
+  }
+
+  // ---- this half's Q/K/V item: its weights, loaded now
+  const int hh = warp >> 3, hw = warp & 7;
+  const int qitem = blockIdx.x + hh * (int)gridDim.x;
+  const bool has_q = qitem < pq.cta_end[2];
+  int qmat = 0, qgroup = qitem;
+  const __nv_bfloat16* qw = pq.w[0];
+#pragma unroll
+  for (int i = 1; i < 3; ++i)
+    if (qitem >= pq.cta_end[i - 1]) {
+      qw = pq.w[i];
+      qgroup = qitem - pq.cta_end[i - 1];
+      qmat = i;
+    }
+  const bool pair_rows = qmat < 2;
+  const int qrow0 = pair_rows ? (qgroup >> 2) * kHeadDim + (qgroup & 3) * 8 : qgroup * kProjRows;
+  const size_t qrow8 = (size_t)(pair_rows ? kHeadDim / 2 : 8) * pq.k;
+  const int qslice = pq.k / 8;  // 256: 8 blocks of 32
+  const __nv_bfloat16* qwa = qw + (size_t)(qrow0 + g) * pq.k + hw * qslice + 8 * q;
+  uint4 qa[8], qb[8];
+  if (has_q) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      qa[i] = ld_stream_v4(qwa + i * kProjBlock);
+      qb[i] = ld_stream_v4(qwa + qrow8 + i * kProjBlock);
+    }
+  }
+
+  // ---- down epilogue: residual add, leaves, subtree sums, arrival
+  red[warp][0][lane] = c0;
+  red[warp][1][lane] = c1;
+  red[warp][2][lane] = c2;
+  red[warp][3][lane] = c3;
+  __syncthreads();
+  float h = 0.f;
+  const int row = group * 8 + (ln >> 2) + ((r & 2) ? kHidden / 2 : 0);
+  __nv_bfloat16* hidden = static_cast<__nv_bfloat16*>(pd.out[0]);
+  if (threadIdx.x < 128 && t < pd.rows) {
+    float sd = 0.f;
+#pragma unroll
+    for (int wi = 0; wi < kWarps; ++wi) sd += red[wi][r][ln];
+    const size_t idx = (size_t)t * kHidden + row;
+    const __nv_bfloat16 hb = hidden[idx] + __float2bfloat16_rn(sd);  // residualKernel's BF16 add
+    hidden[idx] = hb;
+    h = __bfloat162float(hb);
+  }
+  if (threadIdx.x < 128) hv[r][ln] = h;
+  __syncthreads();
+  if (threadIdx.x < 64) {
+    float v = norm_leaf(hv[r][ln], hv[r + 2][ln]);
+    float o = __shfl_down_sync(0xffffffffu, v, 4);
+    if (((ln >> 2) & 1) == 0) v = __fadd_rn(v, o);
+    o = __shfl_down_sync(0xffffffffu, v, 8);
+    if (((ln >> 2) & 3) == 0) v = __fadd_rn(v, o);
+    o = __shfl_down_sync(0xffffffffu, v, 16);
+    if ((ln >> 2) == 0) v = __fadd_rn(v, o);
+    if ((ln >> 2) == 0 && t < pd.rows) pd.norm_part[t * (kHidden / 16) + group] = v;
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned* ctr = reinterpret_cast<unsigned*>(pd.counter);
+    const unsigned old = atomicAdd(ctr, 1u);
+    const unsigned target = (old / gridDim.x + 1u) * gridDim.x;
+    bool done = (int)(ld_acquire_u32(ctr) - target) >= 0;
+    const unsigned long long start = global_timer_ns();
+    while (!done) {
+      for (int i = 0; i < 32 && !done; ++i) done = (int)(ld_acquire_u32(ctr) - target) >= 0;
+      if (!done && elapsed_ns(start) > (long long)kWaitLimitNs) break;
+    }
+    if (!done) record_error(pd.norm_err, TVP_DEVERR_TIMEOUT);
+    arrived = done;
+  }
+  __syncthreads();
+  if (!arrived) return;
+  if (warp < pd.rows) {
+    const float4 v4 =
+        __ldcg(reinterpret_cast<const float4*>(pd.norm_part + warp * (kHidden / 16)) + lane);
+    float v = __fadd_rn(__fadd_rn(v4.x, v4.y), __fadd_rn(v4.z, v4.w));
+#pragma unroll
+    for (int off = 1; off < 32; off *= 2) {
+      const float o = __shfl_down_sync(0xffffffffu, v, off);
+      if ((lane & (2 * off - 1)) == 0) v = __fadd_rn(v, o);
+    }
+    if (lane == 0) r_rows[warp] = (float)sqrt((double)v / 2048.0 + 1.0e-5);
+  }
+  __syncthreads();
+  if (threadIdx.x < 128 && t < pd.rows)
+    pd.norm_out[(size_t)t * kHidden + row] = __float2bfloat16_rn(
+        __fmul_rn(__fdiv_rn(h, r_rows[t]), __bfloat162float(pd.norm_gain[row])));
+  // every normalised row into shared memory, 8 features per step
+  {
+    const uint4* hvv = reinterpret_cast<const uint4*>(hidden);
+    const uint4* gv = reinterpret_cast<const uint4*>(pd.norm_gain);
+    for (int i = threadIdx.x; i < pd.rows * (kHidden / 8); i += 512) {
+      const int tr = i / (kHidden / 8), f8 = i % (kHidden / 8);
+      const uint4 xw = __ldcg(hvv + i), gw = __ldg(gv + f8);
+      const float rr = r_rows[tr];
+      auto n2 = [rr](uint32_t a, uint32_t b) {
+        return pack_bf16x2(__fmul_rn(__fdiv_rn(bf16lo_to_f32(a), rr), bf16lo_to_f32(b)),
+                           __fmul_rn(__fdiv_rn(bf16hi_to_f32(a), rr), bf16hi_to_f32(b)));
+      };
+      *reinterpret_cast<uint4*>(xn + tr * kXnRow + 8 * f8) =
+          make_uint4(n2(xw.x, gw.x), n2(xw.y, gw.y), n2(xw.z, gw.z), n2(xw.w, gw.w));
+    }
+  }
+  __syncthreads();
+
+  // ---- Q/K/V of this half: decode_projection_kernel<8, 1, 8>'s sums
+  if (!has_q) return;  // a whole half (every thread of it has the same item)
+  float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+  const bool has_xq = g < pq.rows;
+  const __nv_bfloat16* xq = xn + (has_xq ? g : 0) * kXnRow + hw * qslice + 8 * q;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint4 vx = has_xq ? *reinterpret_cast<const uint4*>(xq + i * kProjBlock)
+                            : make_uint4(0, 0, 0, 0);
+    mma_bf16_16816(d0, d1, d2, d3, qa[i].x, qb[i].x, qa[i].y, qb[i].y, vx.x, vx.y);
+    mma_bf16_16816(d0, d1, d2, d3, qa[i].z, qb[i].z, qa[i].w, qb[i].w, vx.z, vx.w);
+  }
+  auto half_sync = [hh] { asm volatile("bar.sync %0, 256;" ::"r"(1 + hh) : "memory"); };
+  red[warp][0][lane] = d0;
+  red[warp][1][lane] = d1;
+  red[warp][2][lane] = d2;
+  red[warp][3][lane] = d3;
+  half_sync();
+  const int tid = threadIdx.x - 256 * hh;
+  float sq = 0.f;
+  if (tid < 128) {
+#pragma unroll
+    for (int wi = 0; wi < 8; ++wi) sq += red[8 * hh + wi][r][ln];
+  }
+  rope_append_epilogue(pq, sq, qmat, qgroup, r, ln, t, tid, rope_half[hh], half_sync);
+}
+
 }  // namespace
 }  // namespace tvp
 
@@ -550,10 +758,9 @@ int tvp_decode_projections(const tvp_bf16* x, int rows, int k, int count, const 
   return launch_projection(p, ctas, swiglu, static_cast<cudaStream_t>(stream));
 }
 
-int tvp_decode_projection_residual_rmsnorm(const tvp_bf16* x, int rows, int k, const tvp_bf16* w,
-                                           tvp_bf16* hidden, const tvp_bf16* norm_gain,
-                                           tvp_bf16* norm_out, void* d_scratch,
-                                           tvp_stream_t stream) {
+static int prep_residual_rmsnorm(const tvp_bf16* x, int rows, int k, const tvp_bf16* w,
+                                 tvp_bf16* hidden, const tvp_bf16* norm_gain, tvp_bf16* norm_out,
+                                 void* d_scratch, ProjParams* out) {
   if (!x || !w || !hidden || !norm_gain || !norm_out || !d_scratch || rows < 1 ||
       rows > kProjMaxTokens || k < 256 || k % 256 != 0 || !aligned16(x) || !aligned16(w) ||
       !aligned16(hidden) || !aligned16(norm_gain) || !aligned16(norm_out) || !aligned16(d_scratch))
@@ -566,7 +773,8 @@ int tvp_decode_projection_residual_rmsnorm(const tvp_bf16* x, int rows, int k, c
       overlaps(d_scratch, TVP_NORM_SCRATCH_BYTES, norm_out, hb) ||
       overlaps(d_scratch, TVP_NORM_SCRATCH_BYTES, norm_gain, kHidden * 2))
     return TVP_ERR_INVALID_ARGUMENT;
-  ProjParams p{};
+  ProjParams& p = *out;
+  p = ProjParams{};
   p.x = reinterpret_cast<const __nv_bfloat16*>(x);
   p.count = 1;
   p.rows = rows;
@@ -582,19 +790,35 @@ int tvp_decode_projection_residual_rmsnorm(const tvp_bf16* x, int rows, int k, c
   p.counter = reinterpret_cast<int*>(scratch);
   p.norm_err = reinterpret_cast<int32_t*>(scratch + 4);
   p.norm_part = reinterpret_cast<float*>(scratch + 256);
-  // The spread form's CTAs wait for one another: only when the device holds
-  // the whole grid at once (148 SMs for 128 CTAs on a B200).
+  return TVP_OK;
+}
+
+// The spread form's CTAs wait for one another: only when the device holds the
+// whole grid at once (148 SMs for 128 CTAs on a B200).  After every argument
+// check, since it asks the device.
+static int choose_norm_form(ProjParams* p) {
   int spread = 0;
-  if (norm_spread_fits(k, kHidden / kProjRows, &spread) != TVP_OK) return TVP_ERR_RUNTIME;
-  p.norm_spread = spread;
+  if (norm_spread_fits(p->k, kHidden / kProjRows, &spread) != TVP_OK) return TVP_ERR_RUNTIME;
+  p->norm_spread = spread;
+  return TVP_OK;
+}
+
+int tvp_decode_projection_residual_rmsnorm(const tvp_bf16* x, int rows, int k, const tvp_bf16* w,
+                                           tvp_bf16* hidden, const tvp_bf16* norm_gain,
+                                           tvp_bf16* norm_out, void* d_scratch,
+                                           tvp_stream_t stream) {
+  ProjParams p;
+  int rc = prep_residual_rmsnorm(x, rows, k, w, hidden, norm_gain, norm_out, d_scratch, &p);
+  if (rc == TVP_OK) rc = choose_norm_form(&p);
+  if (rc != TVP_OK) return rc;
   return launch_projection(p, kHidden / kProjRows, false, static_cast<cudaStream_t>(stream));
 }
 
-int tvp_decode_qkv_rope_append(const tvp_bf16* x, int rows, int k, const tvp_bf16* w_q,
-                               const tvp_bf16* w_k, const tvp_bf16* w_v, tvp_bf16* q_out,
-                               tvp_bf16* k_pool, tvp_bf16* v_pool, int num_pages, int num_layers,
-                               int layer, const int32_t* d_block_tables, int table_stride,
-                               const int32_t* d_positions, int32_t* d_error, tvp_stream_t stream) {
+static int prep_qkv_rope_append(const tvp_bf16* x, int rows, int k, const tvp_bf16* w_q,
+                                const tvp_bf16* w_k, const tvp_bf16* w_v, tvp_bf16* q_out,
+                                tvp_bf16* k_pool, tvp_bf16* v_pool, int num_pages, int num_layers,
+                                int layer, const int32_t* d_block_tables, int table_stride,
+                                const int32_t* d_positions, int32_t* d_error, ProjParams* out) {
   constexpr int kQ = TVP_Q_HEADS * kHeadDim, kKv = kMaxKvHeads * kHeadDim;
   if (!x || !w_q || !w_k || !w_v || !q_out || !k_pool || !v_pool || !d_block_tables ||
       !d_positions || rows < 1 || rows > kProjMaxTokens || k < 256 || k % 256 != 0 ||
@@ -605,7 +829,8 @@ int tvp_decode_qkv_rope_append(const tvp_bf16* x, int rows, int k, const tvp_bf1
     return TVP_ERR_INVALID_ARGUMENT;
   if ((long long)num_layers * num_pages * kPage > 0x7fffffffLL) return TVP_ERR_UNSUPPORTED;
   if (overlaps(q_out, (size_t)rows * kQ * 2, x, (size_t)rows * k * 2)) return TVP_ERR_INVALID_ARGUMENT;
-  ProjParams p{};
+  ProjParams& p = *out;
+  p = ProjParams{};
   p.x = reinterpret_cast<const __nv_bfloat16*>(x);
   p.count = 3;
   p.rows = rows;
@@ -629,7 +854,58 @@ int tvp_decode_qkv_rope_append(const tvp_bf16* x, int rows, int k, const tvp_bf1
   p.tables = d_block_tables;
   p.pos = d_positions;
   p.err = d_error;
+  return TVP_OK;
+}
+
+int tvp_decode_qkv_rope_append(const tvp_bf16* x, int rows, int k, const tvp_bf16* w_q,
+                               const tvp_bf16* w_k, const tvp_bf16* w_v, tvp_bf16* q_out,
+                               tvp_bf16* k_pool, tvp_bf16* v_pool, int num_pages, int num_layers,
+                               int layer, const int32_t* d_block_tables, int table_stride,
+                               const int32_t* d_positions, int32_t* d_error, tvp_stream_t stream) {
+  ProjParams p;
+  const int rc = prep_qkv_rope_append(x, rows, k, w_q, w_k, w_v, q_out, k_pool, v_pool, num_pages,
+                                      num_layers, layer, d_block_tables, table_stride, d_positions,
+                                      d_error, &p);
+  if (rc != TVP_OK) return rc;
   return launch_projection(p, p.cta_end[2], false, static_cast<cudaStream_t>(stream));
 }
+
+int tvp_decode_down_norm_qkv(const tvp_bf16* x, int rows, int k, const tvp_bf16* w_down,
+                             tvp_bf16* hidden, const tvp_bf16* norm_gain, tvp_bf16* norm_out,
+                             void* d_scratch, const tvp_bf16* w_q, const tvp_bf16* w_k,
+                             const tvp_bf16* w_v, tvp_bf16* q_out, tvp_bf16* k_pool,
+                             tvp_bf16* v_pool, int num_pages, int num_layers, int layer,
+                             const int32_t* d_block_tables, int table_stride,
+                             const int32_t* d_positions, int32_t* d_error, tvp_stream_t stream) {
+  ProjParams pd, pq;
+  int rc = prep_residual_rmsnorm(x, rows, k, w_down, hidden, norm_gain, norm_out, d_scratch, &pd);
+  if (rc != TVP_OK) return rc;
+  rc = prep_qkv_rope_append(norm_out, rows, kHidden, w_q, w_k, w_v, q_out, k_pool, v_pool,
+                            num_pages, num_layers, layer, d_block_tables, table_stride,
+                            d_positions, d_error, &pq);
+  if (rc != TVP_OK) return rc;
+  if (overlaps(q_out, (size_t)rows * kHidden * 2, hidden, (size_t)rows * kHidden * 2))
+    return TVP_ERR_INVALID_ARGUMENT;
+  if (k % 512 != 0 || k <= 4096) return TVP_ERR_UNSUPPORTED;
+  rc = choose_norm_form(&pd);
+  if (rc != TVP_OK) return rc;
+  // the fused kernel's fixed shape: 16 warps over k, the spread norm, 128
+  // CTAs whose two halves cover the 192 Q/K/V items
+  if (!pd.norm_spread) return TVP_ERR_UNSUPPORTED;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kHidden / kProjRows);
+  cfg.blockDim = dim3(512);
+  cfg.dynamicSmemBytes = (size_t)rows * kXnRow * sizeof(__nv_bfloat16);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, down_norm_qkv_kernel, pd, pq) == cudaSuccess ? TVP_OK
+                                                                             : TVP_ERR_RUNTIME;
+}
+
+
 
 }  // extern "C"

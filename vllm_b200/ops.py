@@ -355,3 +355,37 @@ def decode_qkv_rope_append(x, w_q, w_k, w_v, q_out, k_pool, v_pool, layer, block
                                         _stream(stream))
     N.check(rc, "tvp_decode_qkv_rope_append")
     return q_out
+
+
+def decode_down_norm_qkv(x, w_down, hidden, norm_gain, norm_out, scratch, w_q, w_k, w_v, q_out,
+                         k_pool, v_pool, layer, block_tables, positions, error=None, stream=None):
+    """decode_projection_residual_rmsnorm(x, w_down, hidden, norm_gain, norm_out,
+    scratch) followed by decode_qkv_rope_append(norm_out, w_q, w_k, w_v, q_out,
+    k_pool, v_pool, layer, block_tables, positions, error), as one launch with
+    the same outputs.  Raises RuntimeError (TVP_ERR_UNSUPPORTED) where the
+    fused form does not apply; the two calls then do the same work."""
+    lib = N.load()
+    num_layers, num_pages, kv_heads = _pool_geometry(k_pool, v_pool)
+    dev = x.device
+    for t, name in ((x, "x"), (w_down, "w_down"), (hidden, "hidden"), (norm_gain, "norm_gain"),
+                    (norm_out, "norm_out"), (w_q, "w_q"), (w_k, "w_k"), (w_v, "w_v"),
+                    (q_out, "q_out")):
+        _need(t, name, torch.bfloat16, dev)
+    _need(scratch, "scratch", torch.int32, dev)
+    _need(block_tables, "block_tables", torch.int32, dev)
+    _need(positions, "positions", torch.int32, dev)
+    if scratch.numel() * 4 < NORM_SCRATCH_BYTES:
+        raise ValueError(f"scratch must hold {NORM_SCRATCH_BYTES} bytes (norm_scratch())")
+    rows, k = x.shape
+    if w_down.shape != (2048, k) or hidden.shape != (rows, 2048) or norm_out.shape != (rows, 2048) \
+            or norm_gain.numel() != 2048 or kv_heads != N.KV_HEADS or w_q.shape != (2048, 2048) \
+            or w_k.shape != (512, 2048) or w_v.shape != (512, 2048) or q_out.shape != (rows, 2048) \
+            or positions.numel() != rows or block_tables.dim() != 2 or block_tables.shape[0] < rows:
+        raise ValueError("shapes: see decode_projection_residual_rmsnorm and decode_qkv_rope_append")
+    rc = lib.tvp_decode_down_norm_qkv(_ptr(x), rows, k, _ptr(w_down), _ptr(hidden), _ptr(norm_gain),
+                                      _ptr(norm_out), _ptr(scratch), _ptr(w_q), _ptr(w_k),
+                                      _ptr(w_v), _ptr(q_out), _ptr(k_pool), _ptr(v_pool), num_pages,
+                                      num_layers, layer, _ptr(block_tables), block_tables.shape[1],
+                                      _ptr(positions), _ptr(error), _stream(stream))
+    N.check(rc, "tvp_decode_down_norm_qkv")
+    return hidden, norm_out, q_out
