@@ -304,6 +304,17 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
   for (int m = 0; m < kMats; ++m) c[m][0] = c[m][1] = c[m][2] = c[m][3] = 0.f;
   const int blocks = slice / kProjBlock;
   const size_t row8 = (size_t)(pair_rows ? kHeadDim / 2 : leaf_rows ? kHidden / 2 : 8) * p.k;
+  // The residual epilogue's operand (thread (r, ln) < 128: token row t of
+  // feature `row`) is the previous grids' output: loaded right after the
+  // wait, so that its latency hides behind the weight stream.
+  const int r = (threadIdx.x >> 5) & 3, ln = threadIdx.x & 31;
+  const int t = 2 * (ln & 3) + (r & 1);
+  const int row = leaf_rows ? group * 8 + (ln >> 2) + ((r & 2) ? kHidden / 2 : 0)
+                            : group * kProjRows + (ln >> 2) + ((r & 2) ? 8 : 0);
+  const bool res_load =
+      kMats == 1 && p.epilogue == TVP_PROJ_RESIDUAL && threadIdx.x < 128 && t < p.rows;
+  __nv_bfloat16* const res_ptr = static_cast<__nv_bfloat16*>(out) + (size_t)t * n_out + row;
+  __nv_bfloat16 res_old = __float2bfloat16_rn(0.f);
   // The next launch in the stream may start now; it reads nothing this grid
   // writes before its own wait below.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -322,7 +333,10 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
     }
     // The input rows may be the previous grid's output: wait for it (a no-op
     // after the first batch, and when this launch was not programmatic).
-    if (b0 == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (b0 == 0) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      if (res_load) res_old = *res_ptr;
+    }
 #pragma unroll
     for (int i = 0; i < kUnroll; ++i)
       if (b0 + i < blocks)
@@ -347,7 +361,6 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
     for (int r = 0; r < 4; ++r) red[m][warp][r][lane] = c[m][r];
   __syncthreads();
   // accumulator r of lane ln: MMA row (ln / 4) + 8 (r / 2), input row 2 (ln % 4) + r % 2
-  const int r = (threadIdx.x >> 5) & 3, ln = threadIdx.x & 31;
   float s[kMats];
 #pragma unroll
   for (int m = 0; m < kMats; ++m) {
@@ -357,7 +370,6 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
       for (int wi = 0; wi < kWarps; ++wi) s[m] += red[m][wi][r][ln];
     }
   }
-  const int t = 2 * (ln & 3) + (r & 1);
   if (kMats == 1 && p.epilogue == kEpiRopeAppend) {
     __shared__ float rope_half[4][32];
     rope_append_epilogue(p, s[0], mat, group, r, ln, t, threadIdx.x, rope_half,
@@ -365,8 +377,6 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
     return;
   }
   float h = 0.f;  // the residual epilogue's new hidden value
-  const int row = leaf_rows ? group * 8 + (ln >> 2) + ((r & 2) ? kHidden / 2 : 0)
-                            : group * kProjRows + (ln >> 2) + ((r & 2) ? 8 : 0);
   if (threadIdx.x < 128) {
     if (t < p.rows) {
       const size_t idx = (size_t)t * n_out + row;
@@ -379,7 +389,7 @@ __global__ void __launch_bounds__(kWarps * 32, 16 / kWarps)
       } else if (p.epilogue == TVP_PROJ_F32) {
         static_cast<float*>(out)[idx] = s[0];
       } else if (p.epilogue == TVP_PROJ_RESIDUAL) {
-        const __nv_bfloat16 hb = ob[idx] + __float2bfloat16_rn(s[0]);  // residualKernel's BF16 add
+        const __nv_bfloat16 hb = res_old + __float2bfloat16_rn(s[0]);  // residualKernel's BF16 add
         ob[idx] = hb;
         h = __bfloat162float(hb);
       } else {
@@ -503,6 +513,11 @@ __global__ void __launch_bounds__(512, 1)
   const __nv_bfloat16* xr = pd.x + (size_t)(has_x ? g : 0) * pd.k + warp * slice + 8 * q;
   float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
   const int blocks = slice / kProjBlock;
+  const int row = group * 8 + (ln >> 2) + ((r & 2) ? kHidden / 2 : 0);
+  __nv_bfloat16* hidden = static_cast<__nv_bfloat16*>(pd.out[0]);
+  const bool res_load = threadIdx.x < 128 && t < pd.rows;
+  __nv_bfloat16* const res_ptr = hidden + (size_t)t * kHidden + row;
+  __nv_bfloat16 res_old = __float2bfloat16_rn(0.f);
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   for (int b0 = 0; b0 < blocks; b0 += kUnroll) {
     uint4 va[kUnroll], vb[kUnroll], vx[kUnroll];
@@ -514,7 +529,10 @@ __global__ void __launch_bounds__(512, 1)
         vb[i] = ld_stream_v4(wa + row8 + off);
       }
     }
-    if (b0 == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (b0 == 0) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      if (res_load) res_old = *res_ptr;
+    }
 #pragma unroll
     for (int i = 0; i < kUnroll; ++i)
       if (b0 + i < blocks)
@@ -562,15 +580,12 @@ __global__ void __launch_bounds__(512, 1)
   red[warp][3][lane] = c3;
   __syncthreads();
   float h = 0.f;
-  const int row = group * 8 + (ln >> 2) + ((r & 2) ? kHidden / 2 : 0);
-  __nv_bfloat16* hidden = static_cast<__nv_bfloat16*>(pd.out[0]);
-  if (threadIdx.x < 128 && t < pd.rows) {
+  if (res_load) {
     float sd = 0.f;
 #pragma unroll
     for (int wi = 0; wi < kWarps; ++wi) sd += red[wi][r][ln];
-    const size_t idx = (size_t)t * kHidden + row;
-    const __nv_bfloat16 hb = hidden[idx] + __float2bfloat16_rn(sd);  // residualKernel's BF16 add
-    hidden[idx] = hb;
+    const __nv_bfloat16 hb = res_old + __float2bfloat16_rn(sd);  // residualKernel's BF16 add
+    *res_ptr = hb;
     h = __bfloat162float(hb);
   }
   if (threadIdx.x < 128) hv[r][ln] = h;
