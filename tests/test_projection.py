@@ -102,3 +102,64 @@ def test_fragment_mapping_covers_every_k_once():
         seen[row, t] = True
         assert abs(acc[ln, r] - expect[row, t]) < 1e-9
     assert seen.all()
+
+
+def _reference_sum_of_squares(x):
+    """rmsNormKernel's sum (src/model/rmsNorm.cu:6-14) in FP32: leaf t < 1024 is
+    x[t]^2 + x[t + 1024]^2, then for i = 1, 2, ..., 512 leaf t += leaf t + i where
+    t % 2i == 0.  x holds BF16 values, so each square is exact in FP32 and the
+    leaf is one rounding (the kernel's FMA form gives the same)."""
+    import numpy as np
+    sq = (x.astype(np.float32) * x.astype(np.float32)).astype(np.float32)
+    leaf = (sq[:1024] + sq[1024:]).astype(np.float32)
+    i = 1
+    while i < 1024:
+        leaf[0::2 * i] = (leaf[0::2 * i] + leaf[i::2 * i]).astype(np.float32)
+        i *= 2
+    return leaf[0]
+
+
+def _spread_sum_of_squares(x):
+    """The spread norm's order: CTA a (of 128) owns features 8a..8a+7 and
+    1024+8a..; it forms leaves 8a..8a+7 and sums them by shuffles of 4, 8 and
+    16 lanes (the tree's levels 1, 2, 4); a warp then sums the 128 subtree
+    values, four per lane as (p0 + p1) + (p2 + p3) (levels 8, 16), then by
+    shuffles down 1, 2, 4, 8, 16 (levels 32 .. 512)."""
+    import numpy as np
+    f = np.float32
+    sq = (x.astype(f) * x.astype(f)).astype(f)
+    parts = []
+    for a in range(128):
+        v = [f(sq[8 * a + j] + sq[1024 + 8 * a + j]) for j in range(8)]
+        for step in (1, 2, 4):                 # lanes j and j + step, j % 2step == 0
+            for j in range(0, 8, 2 * step):
+                v[j] = f(v[j] + v[j + step])
+        parts.append(v[0])
+    lanes = [f(f(parts[4 * l] + parts[4 * l + 1]) + f(parts[4 * l + 2] + parts[4 * l + 3]))
+             for l in range(32)]
+    off = 1
+    while off < 32:
+        for l in range(0, 32, 2 * off):
+            lanes[l] = f(lanes[l] + lanes[l + off])
+        off *= 2
+    return lanes[0]
+
+
+def test_spread_norm_sums_in_the_reference_tree_order():
+    """The subtree decomposition of the spread RMSNorm is the reference's tree,
+    so the FP32 sum is the same bits for any row (checked on rows of every
+    magnitude, including ones where a different order would round differently)."""
+    import numpy as np
+    rng = np.random.default_rng(5)
+    order_matters = 0
+    for scale in (1e-3, 1.0, 3.0, 100.0, 3e4):
+        for _ in range(20):
+            x = (rng.standard_normal(2048) * scale).astype(np.float32)
+            x = (x.view(np.uint32) & 0xFFFF0000).view(np.float32)  # BF16 values
+            ref = np.float32(_reference_sum_of_squares(x))
+            assert np.float32(_spread_sum_of_squares(x)).view(np.uint32) == ref.view(np.uint32)
+            seq = np.float32(0)
+            for v in (x * x).astype(np.float32):
+                seq = np.float32(seq + v)
+            order_matters += int(seq.view(np.uint32) != ref.view(np.uint32))
+    assert order_matters > 50  # a sequential sum would differ on most rows
