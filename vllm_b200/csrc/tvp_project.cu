@@ -39,6 +39,13 @@
 //    bf16(g (1 / (1 + expf(-g))) u) of the BF16-rounded gate and up).  For
 //    SwiGLU one CTA streams the same 16 rows of both matrices, so both sums of
 //    an element meet in its epilogue.
+//  * The RMSNorm after a residual epilogue (O, down) is spread over the grid:
+//    each CTA holds both features of 8 of the reference's sum-of-squares
+//    leaves, publishes that subtree's sum, and after a bounded grid-wide
+//    arrival normalises its own features (the same tree order, so the same
+//    bits).  The down launch can also run the next layer's Q/K/V with RoPE and
+//    the page append (down_norm_qkv_kernel), loading their weights before the
+//    arrival.
 #include <cuda_bf16.h>
 
 #include "tvp_common.cuh"
